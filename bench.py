@@ -1,0 +1,484 @@
+"""Paged-KV decode benchmark (BASELINE metric: paged decode-attention achieved
+TB/s and decode tokens/s at 1/2/4/8 B200).
+
+One step = one decode step of the whole layer stack of the configured
+workload: build the step's slot mapping and page tables on the host (the
+reference's CudaModel::prepare), prepare the attention plan (one H2D copy),
+then per layer append one K/V row per sequence and run paged decode attention.
+
+Default workload: C2 (Qwen3-8B attention shape: hq32/hkv8/d128 bf16, 36
+layers, 64 sequences, contexts U[512,4096], page 16). Under torchrun every
+rank runs its own 64 sequences (weak scaling); NCCL is used only after the
+timed loop to gather per-rank results (no collective on the hot path).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c5]
+  python bench.py --impl reference ...   # the reference's own CPU/ATen path
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "flashengine.cpp_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "paged decode-attn achieved TB/s (% HBM peak); decode tokens/s at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peak_gbs():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="fe_clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.dev)],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                    power.append(float(parts[3]))
+                except ValueError:
+                    continue
+                for name, val in zip(names, parts[5:9]):
+                    if val.lower() == "active":
+                        reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(power) if power else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing (one process per GPU; no collective on the hot path)
+# ---------------------------------------------------------------------------
+
+def dist_setup(n_gpus: int):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def gather_floats(values, world):
+    """All-gather a small float64 vector per rank (after timing only)."""
+    import torch
+
+    t = torch.tensor(values, dtype=torch.float64, device="cuda")
+    if world == 1:
+        return t.unsqueeze(0).cpu().numpy()
+    import torch.distributed as dist
+
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return torch.stack(out).cpu().numpy()
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+
+def make_workload(config, rank, world, total_steps):
+    from fekv import workloads
+
+    if config == "c2":
+        return workloads.c2(seed=1000 + rank, steps=total_steps)
+    if config == "c5":
+        return workloads.c5(rank=rank, world=world, steps=total_steps)
+    raise ValueError(config)
+
+
+class DecodeState:
+    """Device-resident pools and per-layer step inputs for one GPU."""
+
+    def __init__(self, w, physical_layers, seed):
+        import torch
+
+        self.w = w
+        dt = torch.bfloat16 if w.bf16 else torch.float16
+        self.dt = dt
+        g = torch.Generator(device="cuda")
+        g.manual_seed(seed)
+        self.kpools, self.vpools = [], []
+        for _ in range(physical_layers):
+            for lst in (self.kpools, self.vpools):
+                t = torch.empty(w.cache_slots, w.width, dtype=dt, device="cuda")
+                t.normal_(0.0, w.scale, generator=g)
+                lst.append(t)
+        rows = w.batch
+        L = w.layers
+        self.q = torch.randn(L, rows, w.hq, w.dim, generator=g, device="cuda", dtype=dt) * w.scale
+        self.knew = torch.randn(L, rows, w.width, generator=g, device="cuda", dtype=dt) * w.scale
+        self.vnew = torch.randn(L, rows, w.width, generator=g, device="cuda", dtype=dt) * w.scale
+        self.out = torch.empty_like(self.q)
+        self.slots = torch.empty(rows, dtype=torch.int64, device="cuda")
+        self.physical = physical_layers
+
+
+def run_ours(args, rank, world, local):
+    import torch
+
+    import fekv
+
+    fekv.load()
+    peak, peak_kind = measured_peak_gbs()
+    total_steps = args.warmup + args.steps + args.e2e_steps + 1
+    w = make_workload(args.config, rank, world, total_steps)
+    # physical layer pools: all layers when they fit, else pools are reused
+    per_layer = 2 * w.cache_slots * w.width * 2
+    free, _ = torch.cuda.mem_get_info()
+    budget = min(free * 0.85, args.pool_gb * 1e9)
+    physical = int(min(w.layers, max(1, budget // per_layer)))
+    st = DecodeState(w, physical, seed=7 + rank)
+    plan = fekv.AttentionPlan(w.hq, w.hkv, w.dim, w.page, w.batch, w.max_pages(total_steps),
+                              w.bf16, w.num_blocks)
+    stream = torch.cuda.current_stream()
+
+    attn_ev = []
+
+    def step(s, record=False, host_io=None):
+        md = w.metadata(s)
+        if host_io is not None:
+            host_io["h2d"]()
+        plan.prepare(md.qo, md.kv, md.pages, md.last, md.batch, md.rows, False, stream)
+        st.slots.copy_(torch.from_numpy(md.slots).pin_memory(), non_blocking=True)
+        for layer in range(w.layers):
+            p = layer % st.physical
+            fekv.store(st.knew[layer], st.vnew[layer], st.kpools[p], st.vpools[p], st.slots,
+                       md.rows, w.width, w.bf16, stream, w.cache_slots)
+            if record:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            plan.attention(st.q[layer], st.kpools[p], st.vpools[p], st.out[layer], True, stream)
+            if record:
+                e1.record(stream)
+                attn_ev.append((e0, e1))
+        if host_io is not None:
+            host_io["d2h"]()
+        return md
+
+    # warm-up
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    barrier(world)
+
+    # timed region (device-resident inputs)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    kv_bytes = 0
+    keys = 0
+    t0.record(stream)
+    for i in range(args.steps):
+        md = step(args.warmup + i, record=True)
+        lengths = md.lengths(w.page)
+        keys += int(lengths.sum())
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    attn_ms = [a.elapsed_time(b) for a, b in attn_ev]
+    barrier(world)
+
+    # algorithmic bytes of one decode-attention launch (averaged over steps)
+    per_launch_bytes = (keys / args.steps) * 2 * w.width * 2 + 2 * w.batch * w.hq * w.dim * 2
+    attn_avg_ms = float(np.mean(attn_ms))
+    achieved_gbs = per_launch_bytes / (attn_avg_ms * 1e-3) / 1e9
+
+    # end-to-end through the C ABI with host buffers: per step, H2D of every
+    # layer's q/k/v from pinned memory and D2H of every layer's output.
+    hq_pin = torch.empty(st.q.shape, dtype=st.dt, pin_memory=True)
+    hk_pin = torch.empty(st.knew.shape, dtype=st.dt, pin_memory=True)
+    hv_pin = torch.empty(st.vnew.shape, dtype=st.dt, pin_memory=True)
+    ho_pin = torch.empty(st.out.shape, dtype=st.dt, pin_memory=True)
+    hq_pin.copy_(st.q)
+    hk_pin.copy_(st.knew)
+    hv_pin.copy_(st.vnew)
+    io = {
+        "h2d": lambda: (st.q.copy_(hq_pin, non_blocking=True),
+                        st.knew.copy_(hk_pin, non_blocking=True),
+                        st.vnew.copy_(hv_pin, non_blocking=True)),
+        "d2h": lambda: ho_pin.copy_(st.out, non_blocking=True),
+    }
+    h2d_bytes = (hq_pin.numel() + hk_pin.numel() + hv_pin.numel()) * 2
+    d2h_bytes = ho_pin.numel() * 2
+    barrier(world)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    base = args.warmup + args.steps
+    e0.record(stream)
+    for i in range(args.e2e_steps):
+        step(base + i, host_io=io)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+
+    stats = gather_floats([ms, e2e_ms, attn_avg_ms, achieved_gbs, keys], world)
+    plan.close()
+    if rank != 0:
+        return None
+    ms_max = float(stats[:, 0].max())
+    e2e_max = float(stats[:, 1].max())
+    tokens = w.batch * args.steps * world
+    value = tokens / (ms_max * 1e-3)
+    e2e_value = w.batch * args.e2e_steps * world / (e2e_max * 1e-3)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_max / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16" if w.bf16 else "f16",
+        "data": "synthetic (seeded N(0,1) x scale K/V/q; random non-contiguous pages)",
+        "config": {
+            "workload": f"{w.name}: hq{w.hq}/hkv{w.hkv}/d{w.dim} page{w.page}, {w.layers} layers, "
+                        f"{w.batch} seqs/GPU, 1 appended token + decode attention per layer-step",
+            "seqs_per_gpu": w.batch, "layers": w.layers, "physical_layer_pools": physical,
+            "mean_context": float(np.mean(w.cached)),
+            "kv_bytes_per_step": float(per_launch_bytes * w.layers),
+            "l2": "inputs larger than L2 (each layer's KV pages exceed 126 MB)",
+            "parallelism": f"sequence-sharded x{world}, no hot-path collective",
+        },
+        "decode_attn_tbs": round(float(stats[:, 3].sum()) / 1e3, 4),
+        "decode_attn_frac_of_peak": round(float(stats[:, 3].mean()) / peak, 4),
+        "roofline": {
+            "bound": "hbm",
+            "achieved": round(float(stats[0, 3]), 1),
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": round(float(stats[0, 3]) / peak, 4),
+            "peak_kind": peak_kind,
+            "kernel": "paged_attn_kernel (decode)",
+            "algorithmic_bytes_per_launch": float(per_launch_bytes),
+            "avg_launch_ms": round(float(stats[0, 2]), 5),
+            "traffic": None,
+        },
+        "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": int(d2h_bytes),
+                "steps": args.e2e_steps},
+        "gpu_launches": 2 * w.layers * args.steps,
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(w, args)
+    return line
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own ATen path (oracle/_ref), all host threads
+# ---------------------------------------------------------------------------
+
+def _ref_layer_step(ref, w, md, pools, inputs):
+    kp, vp = pools
+    q, kn, vn = inputs
+    ref.store(kn, vn, kp, vp, md.slots)
+    ref.prepare(md.qo, md.kv, md.pages, md.last)
+    return ref.attention(q, kp, vp, True)
+
+
+def cpu_reference_setup(w, steps):
+    import oracle
+    from fekv import workloads
+
+    threads = os.cpu_count() or 1
+    oracle.ref_set_threads(threads)
+    rng = np.random.default_rng(5)
+    kp = workloads.random_bits(rng, (w.cache_slots, w.width), w.bf16, w.scale)
+    vp = workloads.random_bits(rng, (w.cache_slots, w.width), w.bf16, w.scale)
+    q = workloads.random_bits(rng, (w.batch, w.hq, w.dim), w.bf16, w.scale)
+    kn = workloads.random_bits(rng, (w.batch, w.width), w.bf16, w.scale)
+    vn = workloads.random_bits(rng, (w.batch, w.width), w.bf16, w.scale)
+    ref = oracle.RefAten(w.hq, w.hkv, w.dim, w.page, w.batch, w.max_pages(steps), w.bf16,
+                         w.num_blocks)
+    return ref, (kp, vp), (q, kn, vn), oracle.ref_get_threads()
+
+
+def cpu_baseline(w, args):
+    """One layer-step of the workload (store + prepare_plan + attention for
+    every sequence) through the reference library, repeated for ~10 s."""
+    import oracle
+
+    if not oracle.ref_available():
+        return {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference",
+                "sample": "oracle/_ref not built"}
+    ref, pools, inputs, threads = cpu_reference_setup(w, 4)
+    md = w.metadata(0)
+    _ref_layer_step(ref, w, md, pools, inputs)  # warm
+    times = []
+    t_end = time.time() + args.cpu_seconds
+    while time.time() < t_end or len(times) < 3:
+        t = time.perf_counter()
+        _ref_layer_step(ref, w, md, pools, inputs)
+        times.append(time.perf_counter() - t)
+    ref.close()
+    layer_s = statistics.median(times)
+    return {"value": round(w.batch / (layer_s * w.layers), 3), "unit": "tokens/s",
+            "cores": threads, "kind": "reference",
+            "sample": f"{len(times)} layer-steps of {w.name} ({w.batch} seqs: store + prepare_plan "
+                      f"+ attention), median {layer_s*1e3:.1f} ms/layer, scaled to {w.layers} layers",
+            "cpu_model": _cpu_model()}
+
+
+def _cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return None
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU/ATen implementation of the path
+    (FlashEngine.cpp src/portable_gpu_ops.cpp compiled for the CPU), all host
+    threads. Each step = one layer-step of the workload; rank 0 only."""
+    if rank != 0:
+        return None
+    import oracle
+
+    w = make_workload(args.config, 0, 1, 4)
+    if not oracle.ref_available():
+        return {"impl": "reference", "unavailable": "oracle/_ref/libfe_ref_aten.so not built"}
+    ref, pools, inputs, threads = cpu_reference_setup(w, 4)
+    md = w.metadata(0)
+    for _ in range(args.warmup):
+        _ref_layer_step(ref, w, md, pools, inputs)
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        _ref_layer_step(ref, w, md, pools, inputs)
+    el = time.perf_counter() - t
+    ref.close()
+    layer_s = el / args.steps
+    value = w.batch / (layer_s * w.layers)
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(layer_s * 1e3 * w.layers, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if w.bf16 else "f16",
+        "data": "synthetic", "config": {"workload": f"{w.name} (one layer-step per step, scaled "
+                                                    f"to {w.layers} layers)",
+                                        "seqs": w.batch, "layers": w.layers},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads,
+                         "kind": "reference",
+                         "sample": f"{args.steps} layer-steps of {w.name}, all sequences"},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=["c2", "c5"], default="c2")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--pool-gb", type=float, default=150.0)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+    else:
+        rank, world, local = dist_setup(args.gpus)
+        line = run_ours(args, rank, world, local)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

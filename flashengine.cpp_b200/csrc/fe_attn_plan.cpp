@@ -1,0 +1,295 @@
+// Host work planner for the paged-attention kernel (see fe_attn_plan.h).
+#include "fe_attn_plan.h"
+
+#include <algorithm>
+#include <cstring>
+#include <functional>
+#include <queue>
+#include <utility>
+
+#include "fe_kv.h"
+
+namespace fe {
+namespace {
+
+struct Unit {
+  int seq, kvh, key_mode, rb0, nrb, tiles, rows;
+};
+
+inline int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
+
+inline size_t align16(size_t n) { return (n + 15) & ~size_t(15); }
+
+struct View {
+  std::vector<int32_t> cta_off;
+  std::vector<WorkItem> items;
+  std::vector<SplitGroup> groups;
+  int grid = 0, chunk = 0, decode_items = 0, prefill_items = 0, split_units = 0;
+  int64_t partial_floats = 0;
+};
+
+// Split every unit's key range into balanced chunks and assign the items to
+// CTAs, longest first onto the least-loaded CTA.
+int build_view(const PlanConfig& cfg, const std::vector<Unit>& units, bool fixed_grid, View& v,
+               std::string& err) {
+  int64_t total_tiles = 0;
+  for (const auto& u : units) total_tiles += u.tiles;
+  const int grid_cap = std::max(1, cfg.grid_cap);
+  int chunk = std::max<int>(16, ceil_div(total_tiles, int64_t(grid_cap) * 4));
+  for (int attempt = 0; attempt < 32; ++attempt) {
+    v.items.clear();
+    v.groups.clear();
+    v.decode_items = v.prefill_items = v.split_units = 0;
+    v.partial_floats = 0;
+    bool over = false;
+    for (const auto& u : units) {
+      const int nsplit = std::max(1, ceil_div(u.tiles, chunk));
+      const int base = u.tiles / nsplit, extra = u.tiles % nsplit;
+      int group = -1, part0 = -1;
+      const int rec = partial_rec_floats(u.rows);
+      if (nsplit > 1) {
+        group = static_cast<int>(v.groups.size());
+        part0 = static_cast<int>(v.partial_floats);
+        v.groups.push_back(SplitGroup{nsplit, part0, rec, u.rows});
+        v.partial_floats += int64_t(rec) * nsplit;
+        ++v.split_units;
+      }
+      int kt = 0;
+      for (int s = 0; s < nsplit; ++s) {
+        const int n = base + (s < extra ? 1 : 0);
+        WorkItem it;
+        it.seq = u.seq;
+        it.kvh = static_cast<int16_t>(u.kvh);
+        it.key_mode = static_cast<int16_t>(u.key_mode);
+        it.rb0 = u.rb0;
+        it.nrb = u.nrb;
+        it.kt0 = kt;
+        it.kt1 = kt + n;
+        it.part = nsplit > 1 ? part0 + s * rec : -1;
+        it.group = group;
+        kt += n;
+        v.items.push_back(it);
+        (u.key_mode ? v.decode_items : v.prefill_items)++;
+      }
+    }
+    if (static_cast<int>(v.items.size()) > cfg.max_items || v.partial_floats > cfg.partial_capacity ||
+        static_cast<int>(v.groups.size()) > cfg.max_groups ||
+        v.partial_floats > int64_t(INT32_MAX)) {
+      over = true;
+    }
+    if (!over) break;
+    if (attempt == 31) {
+      err = "attention work exceeds the plan's item / split-workspace capacity";
+      return FE_ERR_CAPACITY;
+    }
+    chunk *= 2;
+  }
+  v.chunk = chunk;
+
+  const int n = static_cast<int>(v.items.size());
+  v.grid = n == 0 ? 0 : (fixed_grid ? grid_cap : std::min(grid_cap, n));
+  // Cost model: key tiles times row blocks computed, plus a fixed per-item
+  // overhead (Q load, epilogue) worth a few tiles.
+  std::vector<std::pair<int64_t, int>> order(n);
+  for (int i = 0; i < n; ++i) {
+    const auto& it = v.items[i];
+    const int64_t tiles = it.kt1 - it.kt0;
+    const int64_t cost = (it.key_mode ? tiles : tiles * it.nrb) + 4;
+    order[i] = {cost, i};
+  }
+  std::stable_sort(order.begin(), order.end(),
+                   [](const auto& a, const auto& b) { return a.first > b.first; });
+  std::vector<std::vector<int>> per_cta(std::max(1, v.grid));
+  using Load = std::pair<int64_t, int>;
+  std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+  for (int c = 0; c < v.grid; ++c) heap.push({0, c});
+  for (const auto& [cost, idx] : order) {
+    auto [load, c] = heap.top();
+    heap.pop();
+    per_cta[c].push_back(idx);
+    heap.push({load + cost, c});
+  }
+  std::vector<WorkItem> sorted;
+  sorted.reserve(n);
+  v.cta_off.assign(v.grid + 1, 0);
+  for (int c = 0; c < v.grid; ++c) {
+    v.cta_off[c] = static_cast<int32_t>(sorted.size());
+    for (int idx : per_cta[c]) sorted.push_back(v.items[idx]);
+  }
+  v.cta_off[v.grid] = static_cast<int32_t>(sorted.size());
+  v.items.swap(sorted);
+  return FE_OK;
+}
+
+}  // namespace
+
+int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, const int32_t* pages,
+               const int32_t* last, int batch, int rows, bool fixed_grid, PlanResult& out,
+               std::string& err) {
+  out = PlanResult{};
+  if (batch < 0 || rows < 0) {
+    err = "batch and rows must be non-negative";
+    return FE_ERR_INVALID_ARGUMENT;
+  }
+  if (batch > 0 && (!qo || !kv || !last)) {
+    err = "qo, kv and last must be non-null";
+    return FE_ERR_INVALID_ARGUMENT;
+  }
+  // Capacity check of the reference's CUDA plan (src/flashinfer_attention.cu:30).
+  if (batch > cfg.max_batch || (batch > 0 && int64_t(kv[batch]) > int64_t(cfg.max_batch) * cfg.max_pages)) {
+    err = "attention metadata exceeds plan capacity";
+    return FE_ERR_CAPACITY;
+  }
+  if (batch > 0 && (qo[0] != 0 || kv[0] != 0)) {
+    err = "qo[0] and kv[0] must be 0";
+    return FE_ERR_INVALID_ARGUMENT;
+  }
+  if ((batch == 0 && rows != 0) || (batch > 0 && qo[batch] != rows)) {
+    err = "qo[batch] must equal rows";
+    return FE_ERR_INVALID_ARGUMENT;
+  }
+  const int G = cfg.hq / cfg.hkv;
+  const int total_pages = batch > 0 ? kv[batch] : 0;
+  if (total_pages > 0 && !pages) {
+    err = "pages must be non-null";
+    return FE_ERR_INVALID_ARGUMENT;
+  }
+  std::vector<SeqInfo> seqs(batch);
+  std::vector<Unit> key_units, row_units_causal, row_units_full;
+  int64_t kv_tokens = 0;
+  for (int b = 0; b < batch; ++b) {
+    const int q0 = qo[b], q1 = qo[b + 1];
+    const int p0 = kv[b], p1 = kv[b + 1];
+    if (q1 < q0 || p1 <= p0) {
+      err = "qo must be non-decreasing and every sequence must own at least one page (b=" +
+            std::to_string(b) + ")";
+      return FE_ERR_INVALID_ARGUMENT;
+    }
+    if (last[b] < 1 || last[b] > cfg.page) {
+      err = "last[b] must be in [1, page] (b=" + std::to_string(b) + ")";
+      return FE_ERR_INVALID_ARGUMENT;
+    }
+    if (p1 - p0 > cfg.max_pages) {
+      err = "sequence uses more pages than max_pages (b=" + std::to_string(b) + ")";
+      return FE_ERR_CAPACITY;
+    }
+    const int64_t length = int64_t(p1 - p0 - 1) * cfg.page + last[b];
+    const int qrows = q1 - q0;
+    // Context check of the reference ATen path (src/portable_gpu_ops.cpp:30).
+    if (length < qrows) {
+      err = "sequence has fewer keys than query rows (b=" + std::to_string(b) + ")";
+      return FE_ERR_CONTEXT;
+    }
+    for (int i = p0; i < p1; ++i)
+      if (pages[i] < 0 || pages[i] > cfg.num_blocks) {
+        err = "page id out of range [0, num_blocks] at pages[" + std::to_string(i) + "]";
+        return FE_ERR_INVALID_ARGUMENT;
+      }
+    seqs[b] = SeqInfo{q0, qrows, static_cast<int32_t>(length), p0};
+    kv_tokens += length;
+    if (qrows == 0) continue;
+    const int P = qrows * G;
+    const int RB = ceil_div(P, kRowBlock);
+    const int tiles_full = ceil_div(length, kTileTokens);
+    if (RB == 1) {
+      for (int h = 0; h < cfg.hkv; ++h) key_units.push_back(Unit{b, h, 1, 0, 1, tiles_full, P});
+    } else {
+      for (int rb0 = 0; rb0 < RB; rb0 += kConsumerWarps) {
+        const int nrb = std::min(kConsumerWarps, RB - rb0);
+        const int last_row = std::min(P, (rb0 + nrb) * kRowBlock) - 1;
+        const int rows_valid = last_row + 1 - rb0 * kRowBlock;
+        const int64_t i_max = last_row / G;
+        const int64_t limit = length - qrows + i_max + 1;  // bottom-right causal
+        const int tiles_causal = ceil_div(limit, kTileTokens);
+        for (int h = 0; h < cfg.hkv; ++h) {
+          row_units_full.push_back(Unit{b, h, 0, rb0, nrb, tiles_full, rows_valid});
+          row_units_causal.push_back(Unit{b, h, 0, rb0, nrb, tiles_causal, rows_valid});
+        }
+      }
+    }
+  }
+
+  // View 0: non-causal, view 1: causal. Identical when no row-mode work.
+  View views[2];
+  const bool same = row_units_full.empty();
+  for (int c = 0; c < (same ? 1 : 2); ++c) {
+    std::vector<Unit> units = key_units;
+    const auto& ru = c == 0 ? row_units_full : row_units_causal;
+    units.insert(units.end(), ru.begin(), ru.end());
+    int rc = build_view(cfg, units, fixed_grid, views[c], err);
+    if (rc != FE_OK) return rc;
+  }
+
+  // Pack: header | per view: cta_off, items, groups | seqs | pages.
+  size_t off = align16(sizeof(MetaHeader));
+  size_t cta_off_off[2], items_off[2], groups_off[2];
+  for (int c = 0; c < 2; ++c) {
+    const View& v = views[same ? 0 : c];
+    if (same && c == 1) {
+      cta_off_off[1] = cta_off_off[0];
+      items_off[1] = items_off[0];
+      groups_off[1] = groups_off[0];
+      continue;
+    }
+    cta_off_off[c] = off;
+    off = align16(off + sizeof(int32_t) * v.cta_off.size());
+    items_off[c] = off;
+    off = align16(off + sizeof(WorkItem) * v.items.size());
+    groups_off[c] = off;
+    off = align16(off + sizeof(SplitGroup) * v.groups.size());
+  }
+  const size_t seqs_off = off;
+  off = align16(off + sizeof(SeqInfo) * seqs.size());
+  const size_t pages_off = off;
+  off = align16(off + sizeof(int32_t) * total_pages);
+  if (off > size_t(INT32_MAX)) {
+    err = "metadata too large";
+    return FE_ERR_CAPACITY;
+  }
+  out.meta.assign(off, 0);
+  uint8_t* m = out.meta.data();
+  for (int c = 0; c < 2; ++c) {
+    const View& v = views[same ? 0 : c];
+    if (same && c == 1) break;
+    if (!v.cta_off.empty())
+      std::memcpy(m + cta_off_off[c], v.cta_off.data(), sizeof(int32_t) * v.cta_off.size());
+    if (!v.items.empty())
+      std::memcpy(m + items_off[c], v.items.data(), sizeof(WorkItem) * v.items.size());
+    if (!v.groups.empty())
+      std::memcpy(m + groups_off[c], v.groups.data(), sizeof(SplitGroup) * v.groups.size());
+  }
+  if (!seqs.empty()) std::memcpy(m + seqs_off, seqs.data(), sizeof(SeqInfo) * seqs.size());
+  if (total_pages) std::memcpy(m + pages_off, pages, sizeof(int32_t) * total_pages);
+
+  MetaHeader h{};
+  for (int c = 0; c < 2; ++c) {
+    const View& v = views[same ? 0 : c];
+    h.n_items[c] = static_cast<int32_t>(v.items.size());
+    h.n_groups[c] = static_cast<int32_t>(v.groups.size());
+    h.grid[c] = v.grid;
+    h.cta_off_off[c] = static_cast<int32_t>(cta_off_off[c]);
+    h.items_off[c] = static_cast<int32_t>(items_off[c]);
+    h.groups_off[c] = static_cast<int32_t>(groups_off[c]);
+  }
+  h.batch = batch;
+  h.rows = rows;
+  h.seqs_off = static_cast<int32_t>(seqs_off);
+  h.pages_off = static_cast<int32_t>(pages_off);
+  h.total_bytes = static_cast<int32_t>(off);
+  h.chunk_tiles = views[0].chunk;
+  std::memcpy(m, &h, sizeof(h));
+
+  const View& vc = views[same ? 0 : 1];
+  out.n_items = static_cast<int>(vc.items.size());
+  out.n_groups = std::max(views[0].groups.size(), same ? 0 : views[1].groups.size());
+  out.decode_items = vc.decode_items;
+  out.prefill_items = vc.prefill_items;
+  out.split_units = vc.split_units;
+  out.chunk_tiles = vc.chunk;
+  out.grid = std::max(views[0].grid, same ? 0 : views[1].grid);
+  out.kv_tokens = kv_tokens;
+  out.partial_floats = std::max(views[0].partial_floats, same ? 0 : views[1].partial_floats);
+  return FE_OK;
+}
+
+}  // namespace fe

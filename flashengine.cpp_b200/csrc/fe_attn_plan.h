@@ -1,0 +1,93 @@
+// Host-side work planner for the paged-attention kernel, and the device
+// metadata layout it produces. Pure C++ (no CUDA calls), so the planner runs
+// and is tested without a GPU.
+//
+// Replaces the role of FlashInfer's PrefillPlan in the reference
+// (src/flashinfer_attention.cu:29-34), with two differences: work over long
+// contexts is split across CTAs (split-K; the reference disables split-KV,
+// :31) and the per-CTA work lists are balanced on the host (longest item
+// first onto the least-loaded CTA), so the kernel needs no atomics to fetch
+// work and a captured CUDA graph stays valid for any later layout.
+#pragma once
+
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+namespace fe {
+
+constexpr int kHeadDim = 128;
+constexpr int kTileTokens = 16;   // key tokens per tile (one TMA box per K/V half)
+constexpr int kRowBlock = 16;     // packed query rows per mma row block
+constexpr int kConsumerWarps = 4; // row blocks per row-mode item / key-tile lanes in key mode
+
+struct SeqInfo {  // 16 bytes
+  int32_t q_row0;    // first query row (qo[b])
+  int32_t qrows;     // query rows
+  int32_t length;    // keys
+  int32_t page_off;  // kv[b]: first entry of this sequence in pages[]
+};
+
+// One CTA-sized unit of work: packed query rows [rb0*16, (rb0+nrb)*16) of
+// sequence `seq` against KV head `kvh`, keys in tiles [kt0, kt1).
+//   key_mode = 1: a single row block; the consumer warps split the key tiles
+//                 (decode and short verify) and their results are merged in
+//                 shared memory.
+//   key_mode = 0: up to four row blocks, one per consumer warp, each over all
+//                 key tiles of the item (prefill / long verify).
+// A packed row p is query row p / G of the sequence, query head kvh*G + p % G.
+struct WorkItem {  // 32 bytes
+  int32_t seq;
+  int16_t kvh;
+  int16_t key_mode;
+  int32_t rb0;
+  int32_t nrb;
+  int32_t kt0, kt1;
+  int32_t part;   // float offset of this item's partial record, -1 if unsplit
+  int32_t group;  // split group id, -1 if unsplit
+};
+
+struct SplitGroup {  // 16 bytes
+  int32_t nsplit;
+  int32_t part0;       // float offset of split 0's record; split s at part0 + s*rec_floats
+  int32_t rec_floats;  // rows*130 rounded up to a multiple of 4
+  int32_t rows;        // valid packed rows in each record
+};
+
+// Byte offsets are from the start of the metadata buffer. Index [c] of the
+// per-view arrays selects the work list: 0 = non-causal, 1 = causal (the two
+// differ only when a sequence has row-mode work, whose key range depends on
+// the mask).
+struct MetaHeader {  // 128 bytes
+  int32_t n_items[2], n_groups[2], grid[2], cta_off_off[2], items_off[2], groups_off[2];
+  int32_t batch, rows, seqs_off, pages_off, total_bytes, chunk_tiles;
+  int32_t pad[14];
+};
+static_assert(sizeof(MetaHeader) == 128, "MetaHeader layout");
+
+struct PlanConfig {
+  int hq, hkv, dim, page, max_batch, max_pages, num_blocks;
+  int grid_cap;               // persistent CTAs available (SMs x CTAs per SM)
+  int max_items;              // work-item capacity
+  int64_t partial_capacity;   // floats in the split-K workspace
+  int max_groups;             // split-counter capacity
+};
+
+struct PlanResult {
+  std::vector<uint8_t> meta;  // packed device metadata (header first)
+  int n_items = 0, n_groups = 0, decode_items = 0, prefill_items = 0, split_units = 0;
+  int chunk_tiles = 0, grid = 0;
+  int64_t kv_tokens = 0, partial_floats = 0;
+};
+
+// Validates the step metadata (same checks as the reference plus range
+// checks on page ids) and builds the work list. Returns an fe_status; on
+// failure `err` holds the reason.
+int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, const int32_t* pages,
+               const int32_t* last, int batch, int rows, bool fixed_grid, PlanResult& out,
+               std::string& err);
+
+inline int partial_rec_floats(int rows) { return ((rows * (kHeadDim + 2)) + 3) & ~3; }
+
+}  // namespace fe

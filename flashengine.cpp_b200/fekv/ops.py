@@ -1,0 +1,263 @@
+"""Python mirror of the reference's ``fe::cuda`` KV/attention operator
+interface (Cambridgebit/FlashEngine.cpp include/fe/native_cuda.hpp:6-14), over
+the fe_kv C ABI. Device buffers are torch CUDA tensors (PyTorch is only the
+allocator and stream provider here); per-step plan metadata are host arrays.
+
+Names, argument meaning and error behaviour follow the reference:
+``create_plan``/``AttentionPlan``, ``prepare_plan``, ``attention``, ``store``;
+a failing call raises (the reference throws std::runtime_error).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from ._lib import FE_DTYPE_BF16, FE_DTYPE_F16, FeError, check
+
+_P = ctypes.c_void_p
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    return _P(t.data_ptr())
+
+
+def _stream(stream):
+    if stream is None:
+        torch = _torch()
+        return _P(torch.cuda.current_stream().cuda_stream)
+    if hasattr(stream, "cuda_stream"):
+        return _P(stream.cuda_stream)
+    return _P(int(stream))
+
+
+def dtype_code(t) -> int:
+    torch = _torch()
+    if t.dtype == torch.bfloat16:
+        return FE_DTYPE_BF16
+    if t.dtype == torch.float16:
+        return FE_DTYPE_F16
+    raise TypeError(f"unsupported dtype {t.dtype}; expected float16 or bfloat16")
+
+
+def _host_i32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+
+
+# ---------------------------------------------------------------------------
+# fe::cuda::store  (include/fe/native_cuda.hpp:14)
+# ---------------------------------------------------------------------------
+
+def store(k, v, kc, vc, slots, rows=None, width=None, bf16=None, stream=None, cache_slots=None):
+    """Scatter rows of k/v into the pools through `slots` (int64, device).
+    Rows with a negative slot are skipped, as in the reference CUDA kernel."""
+    lib = _lib.load()
+    rows = int(slots.shape[0]) if rows is None else int(rows)
+    width = int(k.numel() // max(rows, 1)) if width is None else int(width)
+    dtype = dtype_code(kc) if bf16 is None else (FE_DTYPE_BF16 if bf16 else FE_DTYPE_F16)
+    cache_slots = int(kc.numel() // width) if cache_slots is None else int(cache_slots)
+    check(lib.fe_kv_append(_ptr(k), _ptr(v), _ptr(kc), _ptr(vc), _ptr(slots), rows, width, dtype,
+                           cache_slots, _stream(stream)), "store")
+
+
+# ---------------------------------------------------------------------------
+# block copy / copy-on-write and page clearing (no reference counterpart)
+# ---------------------------------------------------------------------------
+
+def copy_blocks(k_pools, v_pools, src, dst, ntok, page, width, num_pages_total, dtype=None,
+                stream=None):
+    """Copy token rows [0, ntok[c]) of page src[c] onto page dst[c] in every
+    layer's K and V pool. src/dst/ntok: int32 device tensors."""
+    lib = _lib.load()
+    n = len(k_pools)
+    if n != len(v_pools):
+        raise ValueError("k_pools and v_pools differ in length")
+    kp = (_P * max(n, 1))(*[t.data_ptr() for t in k_pools])
+    vp = (_P * max(n, 1))(*[t.data_ptr() for t in v_pools])
+    dtype = dtype_code(k_pools[0]) if dtype is None else int(dtype)
+    check(lib.fe_kv_copy_blocks(kp, vp, n, _ptr(src), _ptr(dst), _ptr(ntok), int(src.shape[0]),
+                                int(page), int(width), int(num_pages_total), dtype,
+                                _stream(stream)), "copy_blocks")
+
+
+def clear_pages(pools, pages, page, width, num_pages_total, dtype=None, stream=None):
+    """Zero whole pages (int32 device tensor `pages`) of every pool."""
+    lib = _lib.load()
+    n = len(pools)
+    arr = (_P * max(n, 1))(*[t.data_ptr() for t in pools])
+    dtype = dtype_code(pools[0]) if dtype is None else int(dtype)
+    check(lib.fe_kv_clear_pages(arr, n, _ptr(pages), int(pages.shape[0]), int(page), int(width),
+                                int(num_pages_total), dtype, _stream(stream)), "clear_pages")
+
+
+def gather(pool, out, kv, pages, last, row_offset, batch, max_len, page, width, dtype=None,
+           stream=None):
+    """Dense copy of whole sequences' KV rows (device int32 metadata)."""
+    lib = _lib.load()
+    dtype = dtype_code(pool) if dtype is None else int(dtype)
+    check(lib.fe_kv_gather(_ptr(pool), _ptr(out), _ptr(kv), _ptr(pages), _ptr(last),
+                           _ptr(row_offset), int(batch), int(max_len), int(page), int(width), dtype,
+                           _stream(stream)), "gather")
+
+
+def device_errors(stream=None) -> int:
+    """Read and clear the device-side error bits (FE_DEVERR_*)."""
+    lib = _lib.load()
+    bits = ctypes.c_uint32(0)
+    check(lib.fe_device_errors(_stream(stream), ctypes.byref(bits)), "device_errors")
+    return int(bits.value)
+
+
+# ---------------------------------------------------------------------------
+# fe::cuda::create_plan / destroy_plan / prepare_plan / attention
+# (include/fe/native_cuda.hpp:7-10)
+# ---------------------------------------------------------------------------
+
+class AttentionPlan:
+    """Owns an fe_attn_plan. `prepare` takes host metadata (as
+    fe::cuda::prepare_plan); `attention` takes device tensors."""
+
+    def __init__(self, hq, hkv, dim, page, max_batch, max_pages, bf16, blocks):
+        self.lib = _lib.load()
+        h = _P()
+        dtype = FE_DTYPE_BF16 if bf16 else FE_DTYPE_F16
+        check(self.lib.fe_attn_plan_create(int(hq), int(hkv), int(dim), int(page), int(max_batch),
+                                           int(max_pages), dtype, int(blocks), ctypes.byref(h)),
+              "create_plan")
+        self.handle = h
+        self.hq, self.hkv, self.dim, self.page = hq, hkv, dim, page
+        self.bf16, self.blocks = bool(bf16), blocks
+
+    def prepare(self, qo, kv, pages, last, batch=None, rows=None, graph=False, stream=None):
+        qo, kv, pages, last = _host_i32(qo), _host_i32(kv), _host_i32(pages), _host_i32(last)
+        batch = kv.shape[0] - 1 if batch is None else int(batch)
+        rows = int(qo[batch]) if rows is None else int(rows)
+        check(self.lib.fe_attn_plan_prepare(self.handle, qo.ctypes.data_as(_P),
+                                            kv.ctypes.data_as(_P), pages.ctypes.data_as(_P),
+                                            last.ctypes.data_as(_P), batch, rows, int(bool(graph)),
+                                            _stream(stream)), "prepare_plan")
+
+    def attention(self, q, k, v, out, causal=True, stream=None):
+        check(self.lib.fe_attn_run(self.handle, _ptr(q), _ptr(k), _ptr(v), _ptr(out),
+                                   int(bool(causal)), _stream(stream)), "attention")
+
+    def info(self) -> dict:
+        inf = _lib.PlanInfo()
+        check(self.lib.fe_attn_plan_get_info(self.handle, ctypes.byref(inf)), "plan_info")
+        return {name: getattr(inf, name) for name, _ in _lib.PlanInfo._fields_}
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.fe_attn_plan_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def create_plan(hq, hkv, dim, page, max_batch, max_pages, bf16, blocks) -> AttentionPlan:
+    return AttentionPlan(hq, hkv, dim, page, max_batch, max_pages, bf16, blocks)
+
+
+def destroy_plan(plan: AttentionPlan):
+    plan.close()
+
+
+def prepare_plan(plan: AttentionPlan, qo, kv, pages, last, batch, rows, graph=False, stream=None):
+    plan.prepare(qo, kv, pages, last, batch, rows, graph, stream)
+
+
+def attention(plan: AttentionPlan, q, k, v, output, causal=True, stream=None):
+    plan.attention(q, k, v, output, causal, stream)
+
+
+# ---------------------------------------------------------------------------
+# host-only planner (test hook): inspect the work list without a GPU
+# ---------------------------------------------------------------------------
+
+ITEM_DTYPE = np.dtype([("seq", "<i4"), ("kvh", "<i2"), ("key_mode", "<i2"), ("rb0", "<i4"),
+                       ("nrb", "<i4"), ("kt0", "<i4"), ("kt1", "<i4"), ("part", "<i4"),
+                       ("group", "<i4")])
+GROUP_DTYPE = np.dtype([("nsplit", "<i4"), ("part0", "<i4"), ("rec_floats", "<i4"),
+                        ("rows", "<i4")])
+SEQ_DTYPE = np.dtype([("q_row0", "<i4"), ("qrows", "<i4"), ("length", "<i4"),
+                      ("page_off", "<i4")])
+
+
+class HostPlan:
+    """fe_attn_plan_create_host: validates metadata and builds the work list
+    on the host for `grid_cap` CTAs, without touching a GPU."""
+
+    def __init__(self, hq, hkv, dim, page, max_batch, max_pages, bf16, blocks, grid_cap=296):
+        self.lib = _lib.load()
+        h = _P()
+        dtype = FE_DTYPE_BF16 if bf16 else FE_DTYPE_F16
+        check(self.lib.fe_attn_plan_create_host(int(hq), int(hkv), int(dim), int(page),
+                                                int(max_batch), int(max_pages), dtype, int(blocks),
+                                                int(grid_cap), ctypes.byref(h)), "create_host")
+        self.handle = h
+        self.G = hq // hkv
+
+    def prepare(self, qo, kv, pages, last, batch=None, rows=None, graph=False):
+        qo, kv, pages, last = _host_i32(qo), _host_i32(kv), _host_i32(pages), _host_i32(last)
+        batch = kv.shape[0] - 1 if batch is None else int(batch)
+        rows = int(qo[batch]) if rows is None else int(rows)
+        check(self.lib.fe_attn_plan_prepare(self.handle, qo.ctypes.data_as(_P),
+                                            kv.ctypes.data_as(_P), pages.ctypes.data_as(_P),
+                                            last.ctypes.data_as(_P), batch, int(rows),
+                                            int(bool(graph)), None), "prepare_plan")
+        return self.meta()
+
+    def meta(self) -> dict:
+        n = ctypes.c_int64(0)
+        check(self.lib.fe_attn_plan_debug_meta(self.handle, None, 0, ctypes.byref(n)), "meta")
+        buf = np.zeros(n.value, dtype=np.uint8)
+        check(self.lib.fe_attn_plan_debug_meta(self.handle, buf.ctypes.data_as(_P), n.value,
+                                               ctypes.byref(n)), "meta")
+        h = buf[:128].view(np.int32)
+        out = {"batch": int(h[12]), "rows": int(h[13]), "chunk_tiles": int(h[17]), "views": []}
+        seqs_off, pages_off = int(h[14]), int(h[15])
+        batch = out["batch"]
+        out["seqs"] = buf[seqs_off:seqs_off + SEQ_DTYPE.itemsize * batch].view(SEQ_DTYPE)
+        for c in range(2):
+            n_items, n_groups, grid = int(h[0 + c]), int(h[2 + c]), int(h[4 + c])
+            co, io, go = int(h[6 + c]), int(h[8 + c]), int(h[10 + c])
+            view = {
+                "grid": grid,
+                "cta_off": buf[co:co + 4 * (grid + 1)].view(np.int32) if grid else np.zeros(1, np.int32),
+                "items": buf[io:io + ITEM_DTYPE.itemsize * n_items].view(ITEM_DTYPE),
+                "groups": buf[go:go + GROUP_DTYPE.itemsize * n_groups].view(GROUP_DTYPE),
+            }
+            out["views"].append(view)
+        total_pages = int(pages_off)
+        out["pages_off"] = total_pages
+        out["buf"] = buf
+        return out
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.fe_attn_plan_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+__all__ = ["store", "copy_blocks", "clear_pages", "gather", "device_errors", "AttentionPlan",
+           "create_plan", "destroy_plan", "prepare_plan", "attention", "HostPlan", "FeError",
+           "dtype_code", "ITEM_DTYPE", "GROUP_DTYPE", "SEQ_DTYPE"]

@@ -1,0 +1,179 @@
+/*
+ * fe_kv.h — C ABI of the B200 (sm_100a) paged-KV hot path for FlashEngine.cpp.
+ *
+ * Drop-in for the KV and attention operators behind the reference's CUDA
+ * DeviceModel (Cambridgebit/FlashEngine.cpp include/fe/native_cuda.hpp:6-14):
+ * K/V append through the slot mapping, paged GQA attention (decode, chunked
+ * prefill, speculative verify) over per-sequence block tables, plus a
+ * block-copy / copy-on-write operator the reference does not have.
+ *
+ * Conventions
+ *  - Every entry point returns an fe_status; 0 (FE_OK) is success. No C++
+ *    exception crosses this boundary. fe_last_error() returns a detail string
+ *    for the calling thread's most recent failure.
+ *  - `stream` is a cudaStream_t passed as void* (0 = legacy default stream),
+ *    the same convention as the reference's `void* stream`.
+ *  - Element data are fp16 or bf16 (`dtype`: FE_DTYPE_F16 / FE_DTYPE_BF16).
+ *    `bf16` in the shim (fe_native_cuda.hpp) maps to FE_DTYPE_BF16.
+ *  - KV pools are laid out as in the reference (src/cuda_model.cpp:60):
+ *    [num_blocks + 1, page, hkv, dim], i.e. a flat [cache_slots, hkv*dim]
+ *    with cache_slots = (num_blocks + 1) * page. The last page
+ *    (index num_blocks) is the graph-padding page and is never handed to a
+ *    request.
+ *  - Device pointers unless stated "host".
+ */
+#ifndef FE_KV_H_
+#define FE_KV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FE_KV_ABI_VERSION 1
+
+typedef enum fe_status {
+  FE_OK = 0,
+  FE_ERR_INVALID_ARGUMENT = 1, /* bad shape, null pointer, unsupported combination */
+  FE_ERR_CAPACITY = 2,         /* batch/pages/work beyond the plan's fixed capacity */
+  FE_ERR_CONTEXT = 3,          /* a sequence's length < its query rows, or > max context */
+  FE_ERR_CUDA = 4,             /* a CUDA runtime call failed (detail in fe_last_error) */
+  FE_ERR_UNSUPPORTED = 5,      /* head_dim / page size / group size not compiled */
+  FE_ERR_DEVICE = 6,           /* a kernel recorded an error (e.g. out-of-range slot) */
+  FE_ERR_NO_DEVICE = 7         /* no usable sm_100 device */
+} fe_status;
+
+typedef enum fe_dtype { FE_DTYPE_F16 = 0, FE_DTYPE_BF16 = 1 } fe_dtype;
+
+/* Bits reported by fe_device_errors(). */
+#define FE_DEVERR_SLOT_RANGE 0x1u  /* append: slot >= cache_slots (row skipped) */
+#define FE_DEVERR_PAGE_RANGE 0x2u  /* copy/clear: page index out of range (copy skipped) */
+#define FE_DEVERR_NTOK_RANGE 0x4u  /* copy: ntok outside [0, page] (copy skipped) */
+#define FE_DEVERR_TIMEOUT 0x8u     /* attention: a pipeline wait exceeded its bound */
+
+const char* fe_status_string(int status);
+const char* fe_last_error(void);
+int fe_abi_version(void);
+
+/* Read and clear the device-side error bits of the current device (see
+ * FE_DEVERR_*). Synchronises `stream`. */
+int fe_device_errors(void* stream, uint32_t* bits_out);
+
+/* ------------------------------------------------------------------------
+ * K/V append. Replaces fe::cuda::store (include/fe/native_cuda.hpp:14;
+ * src/cuda_kernels.cu:24 store_kernel and :34 its launcher).
+ *   k, v:        [rows, width] new post-RoPE keys / values (width = hkv*dim)
+ *   k_pool/v_pool: [cache_slots, width]
+ *   slots:       int64 [rows] (device); slot < 0 rows are skipped (graph
+ *                padding, as the reference CUDA kernel does); a slot
+ *                >= cache_slots is skipped and raises FE_DEVERR_SLOT_RANGE.
+ * Bit-exact copy. width must be a multiple of 8 elements (16 bytes).
+ * ------------------------------------------------------------------------ */
+int fe_kv_append(const void* k, const void* v, void* k_pool, void* v_pool, const int64_t* slots,
+                 int rows, int width, int dtype, int cache_slots, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Block copy / copy-on-write. No reference counterpart: the reference
+ * shares only whole published pages and never copies one
+ * (src/scheduler.cpp:6-29). For each copy c and each layer l, token rows
+ * [0, ntok[c]) of page src[c] are copied onto page dst[c] in both
+ * k_pools[l] and v_pools[l] (ntok = page copies a whole block; a smaller
+ * ntok is the copy-on-write of a shared partial tail block).
+ *   k_pools, v_pools: HOST arrays of num_layers device pool pointers
+ *                     (num_layers <= FE_MAX_LAYERS)
+ *   src, dst, ntok:   int32 [num_copies] (device)
+ * Source and destination pages of one call must not overlap.
+ * ------------------------------------------------------------------------ */
+#define FE_MAX_LAYERS 128
+int fe_kv_copy_blocks(void* const* k_pools, void* const* v_pools, int num_layers,
+                      const int32_t* src, const int32_t* dst, const int32_t* ntok, int num_copies,
+                      int page, int width, int num_pages_total, int dtype, void* stream);
+
+/* Zero-fill whole pages (e.g. the graph-padding page num_blocks, which the
+ * reference gets from at::zeros at start-up, src/cuda_model.cpp:60).
+ *   pools: HOST array of num_pools device pool pointers
+ *   pages: int32 [num_pages] (device) */
+int fe_kv_clear_pages(void* const* pools, int num_pools, const int32_t* pages, int num_pages,
+                      int page, int width, int num_pages_total, int dtype, void* stream);
+
+/* Gather the KV of whole sequences into a dense buffer: the index_select
+ * of the reference ATen path (src/portable_gpu_ops.cpp:40) without its
+ * padding to max_context. Token t of sequence b is read from slot
+ * pages[kv[b] + t/page]*page + t%page, and written to row
+ * kv_row_offset[b] + t of `out` ([sum of lengths, width]).
+ *   kv, pages, last, kv_row_offset: int32 (device), as in prepare. */
+int fe_kv_gather(const void* pool, void* out, const int32_t* kv, const int32_t* pages,
+                 const int32_t* last, const int32_t* row_offset, int batch, int max_len, int page,
+                 int width, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Paged attention plan. Replaces fe::cuda::create_plan / destroy_plan /
+ * prepare_plan (include/fe/native_cuda.hpp:7-9; src/flashinfer_attention.cu:22-34).
+ * ------------------------------------------------------------------------ */
+typedef struct fe_attn_plan fe_attn_plan;
+
+/* head_dim must be 128 (as src/flashinfer_attention.cu:23 requires); page a
+ * multiple of 16; hq a multiple of hkv with hq/hkv <= 16.
+ * max_pages = per-sequence page capacity (the reference passes
+ * ceil(max_model_len/page)+1, src/cuda_model.cpp:118). Allocates the plan's
+ * fixed device workspaces on the current device. */
+int fe_attn_plan_create(int hq, int hkv, int dim, int page, int max_batch, int max_pages,
+                        int dtype, int num_blocks, fe_attn_plan** plan_out);
+int fe_attn_plan_destroy(fe_attn_plan* plan);
+
+/* Per-step metadata, HOST pointers (as fe::cuda::prepare_plan):
+ *   qo[batch+1]   query-row prefix sums (rows per sequence: 1 = decode,
+ *                 k+1 = verify, chunk = prefill)
+ *   kv[batch+1]   page-count prefix sums into `pages`
+ *   pages[kv[batch]] physical page ids, each in [0, num_blocks]
+ *   last[batch]   tokens in each sequence's last page, 1..page
+ * length_b = (kv[b+1]-kv[b]-1)*page + last[b] keys; query row r of
+ * sequence b is its (r - qo[b])-th of qrows_b = qo[b+1]-qo[b] rows.
+ * Builds the work list on the host and uploads it with one async copy on
+ * `stream` into fixed device buffers, so a CUDA graph that captured
+ * fe_attn_run replays correctly after any later prepare (graph != 0 only
+ * asserts that the row count is unchanged). */
+int fe_attn_plan_prepare(fe_attn_plan* plan, const int32_t* qo, const int32_t* kv,
+                         const int32_t* pages, const int32_t* last, int batch, int rows, int graph,
+                         void* stream);
+
+/* Paged GQA attention. Replaces fe::cuda::attention
+ * (include/fe/native_cuda.hpp:10; src/flashinfer_attention.cu:35-44).
+ *   q, out: [rows, hq, 128]; k_pool, v_pool: [cache_slots, hkv, 128]
+ *   causal != 0: row i of a sequence with qrows rows sees keys
+ *                t <= length - qrows + i (bottom-right aligned);
+ *   causal == 0: every row sees t < length (DFlash draft / block verify).
+ * Scale 1/sqrt(128); fp32 accumulation; output rounded to nearest even. */
+int fe_attn_run(fe_attn_plan* plan, const void* q, const void* k_pool, const void* v_pool,
+                void* out, int causal, void* stream);
+
+/* Introspection of the last prepare (host-side numbers, no sync). */
+typedef struct fe_attn_plan_info {
+  int batch, rows;
+  int decode_items, prefill_items; /* work items queued for the two kernels */
+  int split_sequences;             /* (sequence, kv head) pairs split over > 1 item */
+  int chunk_tiles;                 /* key tiles (16 tokens) per decode item */
+  int grid_ctas;                   /* persistent CTAs launched by fe_attn_run */
+  int64_t kv_tokens;               /* sum of sequence lengths */
+} fe_attn_plan_info;
+int fe_attn_plan_get_info(const fe_attn_plan* plan, fe_attn_plan_info* info);
+
+/* ------------------------------------------------------------------------
+ * Test hooks (no reference counterpart): exercise the host planner without
+ * a GPU.
+ * ------------------------------------------------------------------------ */
+/* A plan with no device state; fe_attn_plan_prepare() then only validates
+ * and builds the work list, for `grid_cap` persistent CTAs. */
+int fe_attn_plan_create_host(int hq, int hkv, int dim, int page, int max_batch, int max_pages,
+                             int dtype, int num_blocks, int grid_cap, fe_attn_plan** plan_out);
+/* Copy the packed work-list metadata of the last prepare into `dst` (at most
+ * `cap` bytes); *bytes receives its full size. Layout: fe_attn_plan.h. */
+int fe_attn_plan_debug_meta(const fe_attn_plan* plan, void* dst, int64_t cap, int64_t* bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FE_KV_H_ */

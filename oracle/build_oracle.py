@@ -1,0 +1,84 @@
+"""Build recipe for the CPU checkers (test infrastructure only).
+
+* ``oracle/libfe_oracle.so``  — the plain-C restatement, ``oracle/fe_oracle.c``.
+* ``oracle/_ref/libfe_ref_aten.so`` — the reference's own ATen path
+  (FlashEngine.cpp ``src/portable_gpu_ops.cpp``), compiled unmodified from the
+  reference source tree through ``oracle/ref_aten_wrap.cpp`` and linked against
+  the CPU LibTorch that ships with the PyTorch wheel. Built only where the
+  reference tree exists (it is not present on the GPU box, which uses the
+  prebuilt file that travels with the repository snapshot).
+
+Run directly: ``python oracle/build_oracle.py [--reference-root DIR]``.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+DEFAULT_REFERENCE_ROOT = os.environ.get("FE_REFERENCE_ROOT", "/root/reference")
+
+C_ORACLE_SRC = os.path.join(HERE, "fe_oracle.c")
+C_ORACLE_LIB = os.path.join(HERE, "libfe_oracle.so")
+REF_WRAP_SRC = os.path.join(HERE, "ref_aten_wrap.cpp")
+REF_DIR = os.path.join(HERE, "_ref")
+REF_LIB = os.path.join(REF_DIR, "libfe_ref_aten.so")
+
+
+def _stale(target: str, *sources: str) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(s) > t for s in sources if os.path.exists(s))
+
+
+def build_c_oracle(force: bool = False) -> str:
+    if force or _stale(C_ORACLE_LIB, C_ORACLE_SRC):
+        cmd = ["gcc", "-O2", "-std=c11", "-fPIC", "-shared", "-Wall", "-Wextra",
+               C_ORACLE_SRC, "-o", C_ORACLE_LIB, "-lm"]
+        subprocess.run(cmd, check=True)
+    return C_ORACLE_LIB
+
+
+def reference_source(reference_root: str = DEFAULT_REFERENCE_ROOT) -> str:
+    return os.path.join(reference_root, "src", "portable_gpu_ops.cpp")
+
+
+def build_reference(reference_root: str = DEFAULT_REFERENCE_ROOT, force: bool = False) -> str | None:
+    """Compile the reference ATen path for the CPU. Returns the library path,
+    or None when the reference tree is absent (e.g. on the GPU box)."""
+    src = reference_source(reference_root)
+    if not os.path.exists(src):
+        return REF_LIB if os.path.exists(REF_LIB) else None
+    if not (force or _stale(REF_LIB, REF_WRAP_SRC, src)):
+        return REF_LIB
+    import torch  # only for its include and library paths
+
+    troot = os.path.dirname(torch.__file__)
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    os.makedirs(REF_DIR, exist_ok=True)
+    cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           "-I", os.path.join(reference_root, "include"),
+           "-I", os.path.join(troot, "include"),
+           "-I", os.path.join(troot, "include", "torch", "csrc", "api", "include"),
+           REF_WRAP_SRC, "-o", REF_LIB,
+           "-L", os.path.join(troot, "lib"), "-ltorch_cpu", "-lc10",
+           f"-Wl,-rpath,{os.path.join(troot, 'lib')}"]
+    subprocess.run(cmd, check=True)
+    return REF_LIB
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference-root", default=DEFAULT_REFERENCE_ROOT)
+    ap.add_argument("--force", action="store_true")
+    a = ap.parse_args(argv)
+    print(build_c_oracle(a.force))
+    print(build_reference(a.reference_root, a.force))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

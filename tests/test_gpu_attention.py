@@ -1,0 +1,223 @@
+"""Paged attention on the GPU through the C ABI against the reference's own
+outputs (golden fixtures from src/portable_gpu_ops.cpp), the CPU oracle, and
+— at full config sizes the CPU cannot finish quickly — an fp32 torch
+restatement of the same ATen algorithm. Tolerance: fe_testutil.ATOL (2e-3)
+widened by one output ulp (see fe_testutil)."""
+import numpy as np
+import pytest
+
+import cases
+import oracle
+from fe_testutil import (compare_attention, to_device, to_host_bits,
+                         torch_reference_attention)
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def fk():
+    import torch
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    import fekv
+    fekv.load()
+    return fekv
+
+
+def _i64(a):
+    import torch
+    return torch.from_numpy(np.asarray(a, np.int64)).cuda()
+
+
+def run_case(fk, case, inp, md, causal=None, graph=False):
+    import torch
+    causal = case.causal if causal is None else causal
+    kc, vc = to_device(inp["kpool"], case.bf16), to_device(inp["vpool"], case.bf16)
+    fk.store(to_device(inp["knew"], case.bf16), to_device(inp["vnew"], case.bf16), kc, vc,
+             _i64(md.slots), md.rows, case.width, case.bf16, None, case.cache_slots)
+    plan = fk.AttentionPlan(case.hq, case.hkv, case.dim, case.page, md.batch, case.max_pages(),
+                            case.bf16, case.num_blocks)
+    plan.prepare(md.qo, md.kv, md.pages, md.last, md.batch, md.rows, graph)
+    q = to_device(inp["q"], case.bf16)
+    out = torch.full_like(q, float("nan"))
+    plan.attention(q, kc, vc, out, causal)
+    torch.cuda.synchronize()
+    assert fk.device_errors() == 0
+    info = plan.info()
+    plan.close()
+    return to_host_bits(out).reshape(inp["q"].shape), info
+
+
+@pytest.mark.parametrize("name", [c.name for c in cases.all_cases()])
+def test_attention_matches_reference_fixture(fk, name):
+    case = cases.case_by_name(name)
+    fx = dict(np.load(cases.fixture_path(name)))
+    inp = case.inputs()
+    md = case.metadata()
+    out, info = run_case(fk, case, inp, md)
+    real = np.arange(md.rows) < int(md.qo[len(case.block_tables)])  # graph-padding rows excluded
+    # CPU oracle (float64) for the unrounded comparison
+    ko, vo = inp["kpool"].copy(), inp["vpool"].copy()
+    oracle.append(inp["knew"], inp["vnew"], ko, vo, md.slots, case.cache_slots)
+    _, ref32 = oracle.attention(inp["q"], ko, vo, md.qo, md.kv, md.pages, md.last, case.hq,
+                                case.hkv, case.dim, case.page, case.causal, case.dtype_code)
+    res = compare_attention(out, fx["ref_out"], case.bf16, rows=real, ref_f32=ref32)
+    assert res["excess"] <= 0, (res, info)
+    assert res["excess_vs_f32"] <= 0, (res, info)
+    assert np.isfinite(oracle.to_float(out[real], case.dtype_code)).all()
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_attention_both_masks_vs_oracle(fk, causal):
+    """The same metadata run with either mask (the plan serves both)."""
+    case = cases.case_by_name("prefill_causal_bf16")
+    inp = case.inputs()
+    md = case.metadata()
+    out, _ = run_case(fk, case, inp, md, causal=causal)
+    ko, vo = inp["kpool"].copy(), inp["vpool"].copy()
+    oracle.append(inp["knew"], inp["vnew"], ko, vo, md.slots, case.cache_slots)
+    want, want32 = oracle.attention(inp["q"], ko, vo, md.qo, md.kv, md.pages, md.last, case.hq,
+                                    case.hkv, case.dim, case.page, causal, case.dtype_code)
+    res = compare_attention(out, want, case.bf16, ref_f32=want32)
+    assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, res
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_attention_random_shapes_vs_oracle(fk, seed):
+    rng = np.random.default_rng(1000 + seed)
+    hkv = int(rng.choice([1, 2, 4, 8]))
+    G = int(rng.choice([1, 2, 4, 8, 16]))
+    batch = int(rng.integers(1, 7))
+    cached = rng.integers(0, 1200, size=batch)
+    rows = np.where(rng.random(batch) < 0.5, 1, rng.integers(1, 40, size=batch))
+    bf16, causal = bool(seed % 2), bool(seed % 3 != 0)
+    case = cases._case("rand", hkv * G, hkv, cached, rows, bf16, causal, 2000 + seed,
+                       page=int(rng.choice([16, 32, 64])))
+    inp = case.inputs()
+    md = case.metadata()
+    out, info = run_case(fk, case, inp, md)
+    ko, vo = inp["kpool"].copy(), inp["vpool"].copy()
+    oracle.append(inp["knew"], inp["vnew"], ko, vo, md.slots, case.cache_slots)
+    want, want32 = oracle.attention(inp["q"], ko, vo, md.qo, md.kv, md.pages, md.last, case.hq,
+                                    case.hkv, case.dim, case.page, causal, case.dtype_code)
+    res = compare_attention(out, want, bf16, ref_f32=want32)
+    assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, (res, info)
+
+
+def _full_size(fk, w, layer_seed=0):
+    """One layer of a BASELINE config at full size, against the fp32 torch
+    restatement of the ATen algorithm."""
+    import torch
+    md = w.metadata()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(layer_seed)
+    dt = torch.bfloat16 if w.bf16 else torch.float16
+    kc = (torch.randn(w.cache_slots, w.width, generator=g, device="cuda") * w.scale).to(dt)
+    vc = (torch.randn(w.cache_slots, w.width, generator=g, device="cuda") * w.scale).to(dt)
+    q = (torch.randn(md.rows, w.hq, w.dim, generator=g, device="cuda") * w.scale).to(dt)
+    knew = (torch.randn(md.rows, w.width, generator=g, device="cuda") * w.scale).to(dt)
+    vnew = (torch.randn(md.rows, w.width, generator=g, device="cuda") * w.scale).to(dt)
+    if w.cow is not None:
+        src, dst, ntok = (torch.from_numpy(np.asarray(a, np.int32)).cuda() for a in w.cow)
+        fk.copy_blocks([kc], [vc], src, dst, ntok, w.page, w.width, w.num_blocks + 1)
+    fk.store(knew, vnew, kc, vc, _i64(md.slots), md.rows, w.width, w.bf16, None, w.cache_slots)
+    plan = fk.AttentionPlan(w.hq, w.hkv, w.dim, w.page, md.batch, w.max_pages(), w.bf16,
+                            w.num_blocks)
+    plan.prepare(md.qo, md.kv, md.pages, md.last)
+    out = torch.empty_like(q)
+    plan.attention(q, kc, vc, out, w.causal)
+    ref = torch_reference_attention(q, kc, vc, md.qo, md.kv, md.pages, md.last, w.hq, w.hkv,
+                                    w.page, w.causal)
+    torch.cuda.synchronize()
+    assert fk.device_errors() == 0
+    ref16 = ref.to(dt)
+    res = compare_attention(to_host_bits(out), to_host_bits(ref16), w.bf16,
+                            ref_f32=ref.cpu().numpy())
+    info = plan.info()
+    plan.close()
+    return res, info
+
+
+def test_c2_layer_full_size(fk):
+    import fekv.workloads as wl
+    res, info = _full_size(fk, wl.c2(seed=0))
+    assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, (res, info)
+    assert res["n_over_2e-3"] == 0, res  # |o| is small at this scale: the flat bar holds
+
+
+def test_c3_layer_full_size(fk):
+    import fekv.workloads as wl
+    res, info = _full_size(fk, wl.c3(seed=0))
+    assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, (res, info)
+
+
+def test_c4_layer_full_size(fk):
+    import fekv.workloads as wl
+    res, info = _full_size(fk, wl.c4(seed=0))
+    assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, (res, info)
+
+
+def test_graph_replay_follows_new_metadata(fk):
+    """Capture append + attention in a CUDA graph once, then re-prepare with
+    different metadata (lengths, splits) and replay: the output tracks the new
+    step, as the reference's graph path requires (src/cuda_model.cpp:150-157)."""
+    import torch
+    import fekv.workloads as wl
+    w = wl.decode_workload("g", 16, 4, [100, 900, 2500, 40], True, 7, steps=8)
+    dt = torch.bfloat16
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    kc = torch.randn(w.cache_slots, w.width, generator=g, device="cuda").to(dt)
+    vc = torch.randn(w.cache_slots, w.width, generator=g, device="cuda").to(dt)
+    plan = fk.AttentionPlan(w.hq, w.hkv, w.dim, w.page, w.batch, w.max_pages(8), True,
+                            w.num_blocks)
+    rows = w.batch
+    q = torch.randn(rows, w.hq, w.dim, generator=g, device="cuda").to(dt)
+    knew = torch.randn(rows, w.width, generator=g, device="cuda").to(dt)
+    vnew = torch.randn(rows, w.width, generator=g, device="cuda").to(dt)
+    slots = torch.zeros(rows, dtype=torch.int64, device="cuda")
+    out = torch.empty_like(q)
+    md0 = w.metadata(0)
+    slots.copy_(_i64(md0.slots))
+    plan.prepare(md0.qo, md0.kv, md0.pages, md0.last, graph=True)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fk.store(knew, vnew, kc, vc, slots, rows, w.width, True, s, w.cache_slots)
+        plan.attention(q, kc, vc, out, True, s)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        st = torch.cuda.current_stream()
+        fk.store(knew, vnew, kc, vc, slots, rows, w.width, True, st, w.cache_slots)
+        plan.attention(q, kc, vc, out, True, st)
+    for step in range(1, 6):
+        md = w.metadata(step)
+        slots.copy_(_i64(md.slots))
+        q.copy_(torch.randn(rows, w.hq, w.dim, generator=g, device="cuda").to(dt))
+        plan.prepare(md.qo, md.kv, md.pages, md.last, graph=True)
+        graph.replay()
+        ref = torch_reference_attention(q, kc, vc, md.qo, md.kv, md.pages, md.last, w.hq, w.hkv,
+                                        w.page, True)
+        torch.cuda.synchronize()
+        res = compare_attention(to_host_bits(out), to_host_bits(ref.to(dt)), True,
+                                ref_f32=ref.cpu().numpy())
+        assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, (step, res)
+    del graph
+    plan.close()
+    assert fk.device_errors() == 0
+
+
+def test_plan_validation_errors(fk):
+    plan = fk.AttentionPlan(8, 2, 128, 16, 2, 4, True, 10)
+    with pytest.raises(fk.FeError) as e:
+        plan.prepare([0, 5], [0, 1], [0], [3])          # 3 keys < 5 query rows
+    assert e.value.status == fk._lib.FE_ERR_CONTEXT
+    with pytest.raises(fk.FeError) as e:
+        plan.prepare([0, 1, 2, 3], [0, 1, 2, 3], [0, 1, 2], [1, 1, 1])  # batch 3 > 2
+    assert e.value.status == fk._lib.FE_ERR_CAPACITY
+    with pytest.raises(fk.FeError) as e:
+        plan.prepare([0, 1], [0, 1], [11], [1])         # page id > num_blocks
+    assert e.value.status == fk._lib.FE_ERR_INVALID_ARGUMENT
+    with pytest.raises(fk.FeError):
+        fk.AttentionPlan(8, 2, 64, 16, 2, 4, True, 10)  # head_dim 64 not compiled
+    plan.close()
