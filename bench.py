@@ -194,6 +194,8 @@ def run_ours(args, rank, world, local):
     peak, peak_kind = measured_peak_gbs()
     total_steps = args.warmup + args.steps + args.e2e_steps + 1
     w = make_workload(args.config, rank, world, total_steps)
+    if args.layers:
+        w.layers = args.layers
     # physical layer pools: all layers when they fit, else pools are reused
     per_layer = 2 * w.cache_slots * w.width * 2
     free, _ = torch.cuda.mem_get_info()
@@ -461,6 +463,8 @@ def main(argv=None):
     ap.add_argument("--pool-gb", type=float, default=150.0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the layer count (profiling a small case only)")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -35,63 +35,215 @@
 #include <new>
 #include <string>
 
-#include "fe_attn_plan.h"
-#include "fe_common.cuh"
+#include "fe_attn_common.cuh"
 
 namespace fe {
+
+int decode_launch(int dtype, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                  bool per_head_tma, const void* args, int grid, cudaStream_t stream);
+
 namespace {
 
 constexpr int kStages = 8;
-constexpr int kHalfBytes = kTileTokens * 128;  // 16 rows x 128 B (64 dims)
-constexpr int kStageBytes = 4 * kHalfBytes;    // K lo, K hi, V lo, V hi
+constexpr int kStageBytes = 4 * kHalfBytes;  // K lo, K hi, V lo, V hi of one head
 constexpr int kThreadsAttn = (kConsumerWarps + 1) * 32;
-constexpr int kCombStride = kHeadDim + 4;  // O[128], m, l, pad
 constexpr int kCombBytes = kConsumerWarps * kRowBlock * kCombStride * 4;
 constexpr int kBarBytes = 2 * kStages * 8 + 16;
 constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCombBytes + kBarBytes;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-template <typename T>
-struct AttnArgs {
-  const uint8_t* meta;
-  const T* q;
-  T* out;
-  float* partials;
-  int32_t* counters;
-  unsigned int* err;
-  int hq, G, page, view;
-  float scale_log2;
+struct ConsumerCtx {
+  uint8_t* stages;
+  uint64_t* full;
+  uint64_t* empty;
+  volatile int* flags;
+  float* comb;
+  int w, lane;
+  bool causal;
 };
 
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
+// Wait for a tile's full barrier; false once the CTA has given up.
+__device__ __forceinline__ bool acquire_tile(const ConsumerCtx& cx, uint32_t gg, bool& aborted) {
+  if (aborted) return false;
+  const int s = gg % kStages;
+  if (cx.flags[0] || !wait_bounded(&cx.full[s], (gg / kStages) & 1u, cx.flags)) aborted = true;
+  return !aborted;
 }
 
-// Bounded mbarrier wait. Returns false when the phase did not complete
-// within kWaitLimitNs, or when another warp of the CTA already gave up
-// (abort flag), so that every warp of the CTA winds down together.
-__device__ __noinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (;;) {
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (global_ns() - t0 > kWaitLimitNs) {
-      *abort_flag = 1;
-      return false;
+// Row mode: warp w owns packed-row block rb0 + w (if any) and walks every key
+// tile of the item. S = Q K^T with the rows on the mma M side. Each active
+// warp releases a stage with one arrival; warp 0 also arrives for the
+// warps that have no block, so every stage still completes with four.
+template <typename T>
+__device__ __forceinline__ void row_item(const AttnArgs<T>& a, const WorkItem& wi,
+                                         const SeqInfo& si, const ConsumerCtx& cx, uint32_t& g,
+                                         bool& aborted) {
+  const int lane = cx.lane, w = cx.w;
+  const int ntiles = wi.kt1 - wi.kt0;
+  if (w >= wi.nrb) {
+    g += ntiles;
+    return;
+  }
+  const int r_lo = lane >> 2, cq = lane & 3, mi = lane >> 3, li = lane & 7;
+  const int G = a.G;
+  const int P = si.qrows * G;
+  const int my_rb = wi.rb0 + w;
+  const int p_lo = my_rb * kRowBlock + r_lo, p_hi = p_lo + 8;
+  const uint32_t arrivals = w == 0 ? 1u + kConsumerWarps - wi.nrb : 1u;
+
+  uint32_t qa[8][4];
+  {
+    const T* q_lo = nullptr;
+    const T* q_hi = nullptr;
+    if (p_lo < P)
+      q_lo = a.q + (static_cast<int64_t>(si.q_row0 + p_lo / G) * a.hq + wi.kvh * G + p_lo % G) *
+                       kHeadDim;
+    if (p_hi < P)
+      q_hi = a.q + (static_cast<int64_t>(si.q_row0 + p_hi / G) * a.hq + wi.kvh * G + p_hi % G) *
+                       kHeadDim;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int col = kk * 16 + 2 * cq;
+      qa[kk][0] = q_lo ? ldg32(q_lo + col) : 0u;
+      qa[kk][1] = q_hi ? ldg32(q_hi + col) : 0u;
+      qa[kk][2] = q_lo ? ldg32(q_lo + col + 8) : 0u;
+      qa[kk][3] = q_hi ? ldg32(q_hi + col + 8) : 0u;
     }
   }
-}
+  const int lim_lo = (cx.causal && p_lo < P) ? si.length - si.qrows + p_lo / G + 1 : si.length;
+  const int lim_hi = (cx.causal && p_hi < P) ? si.length - si.qrows + p_hi / G + 1 : si.length;
+  const int lim_min = min(lim_lo, lim_hi);
 
-template <typename T>
-__device__ __forceinline__ void store4(T* dst, float a, float b, float c, float d) {
-  uint2 v;
-  v.x = pack2<T>(a, b);
-  v.y = pack2<T>(c, d);
-  *reinterpret_cast<uint2*>(dst) = v;
+  float m_r[2] = {-INFINITY, -INFINITY};
+  float l_r[2] = {0.f, 0.f};
+  float o[16][4];
+#pragma unroll
+  for (int dn = 0; dn < 16; ++dn) o[dn][0] = o[dn][1] = o[dn][2] = o[dn][3] = 0.f;
+
+  for (int jt = 0; jt < ntiles; ++jt) {
+    const uint32_t gg = g + jt;
+    if (!acquire_tile(cx, gg, aborted)) break;
+    const int s = gg % kStages;
+    const uint32_t kb0 = smem_u32(cx.stages + s * kStageBytes);
+    const uint32_t kb1 = kb0 + kHalfBytes, vb0 = kb0 + 2 * kHalfBytes, vb1 = kb0 + 3 * kHalfBytes;
+    const int tbase = (wi.kt0 + jt) * kTileTokens;
+
+    // ---- S = Q K^T (16 packed rows x 16 tokens)
+    float sc[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int sp = 0; sp < 2; ++sp) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int tok = nt * 8 + li;
+          const int c = sp * 4 + mi;
+          const uint32_t addr = (h ? kb1 : kb0) + tok * 128 + ((c ^ li) << 4);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(addr, b0, b1, b2, b3);
+          const int kk = h * 4 + sp * 2;
+          mma_16816<T>(sc[nt], qa[kk], b0, b1);
+          mma_16816<T>(sc[nt], qa[kk + 1], b2, b3);
+        }
+      }
+    }
+    if (tbase + kTileTokens > lim_min) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int t = tbase + nt * 8 + 2 * cq + e;
+          if (t >= lim_lo) sc[nt][e] = -INFINITY;
+          if (t >= lim_hi) sc[nt][2 + e] = -INFINITY;
+        }
+    }
+    float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+    float mx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m_r[0], mx0 * a.scale_log2);
+    const float mn1 = fmaxf(m_r[1], mx1 * a.scale_log2);
+    const float base0 = mn0 == -INFINITY ? 0.f : mn0;
+    const float base1 = mn1 == -INFINITY ? 0.f : mn1;
+    const float al0 = fast_exp2(m_r[0] - base0), al1 = fast_exp2(m_r[1] - base1);
+    m_r[0] = mn0;
+    m_r[1] = mn1;
+    float p[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      p[nt][0] = fast_exp2(fmaf(sc[nt][0], a.scale_log2, -base0));
+      p[nt][1] = fast_exp2(fmaf(sc[nt][1], a.scale_log2, -base0));
+      p[nt][2] = fast_exp2(fmaf(sc[nt][2], a.scale_log2, -base1));
+      p[nt][3] = fast_exp2(fmaf(sc[nt][3], a.scale_log2, -base1));
+    }
+    l_r[0] = l_r[0] * al0 + (p[0][0] + p[0][1]) + (p[1][0] + p[1][1]);
+    l_r[1] = l_r[1] * al1 + (p[0][2] + p[0][3]) + (p[1][2] + p[1][3]);
+#pragma unroll
+    for (int dn = 0; dn < 16; ++dn) {
+      o[dn][0] *= al0;
+      o[dn][1] *= al0;
+      o[dn][2] *= al1;
+      o[dn][3] *= al1;
+    }
+    uint32_t phi[4], plo[4];
+    {
+      const float pv[4][2] = {{p[0][0], p[0][1]}, {p[0][2], p[0][3]},
+                              {p[1][0], p[1][1]}, {p[1][2], p[1][3]}};
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        phi[r] = pack2<T>(pv[r][0], pv[r][1]);
+        const float2 f = unpack2<T>(phi[r]);
+        plo[r] = pack2<T>(pv[r][0] - f.x, pv[r][1] - f.y);
+      }
+    }
+    uint32_t vm0 = 0xffffffffu, vm1 = 0xffffffffu;
+    if (tbase + kTileTokens > si.length) {
+      const int ta = tbase + 2 * cq;
+      vm0 = (ta < si.length ? 0x0000ffffu : 0u) | (ta + 1 < si.length ? 0xffff0000u : 0u);
+      vm1 = (ta + 8 < si.length ? 0x0000ffffu : 0u) | (ta + 9 < si.length ? 0xffff0000u : 0u);
+    }
+#pragma unroll
+    for (int qd = 0; qd < 8; ++qd) {
+      const int tok = (mi & 1) * 8 + li;
+      const int c = 2 * qd + (mi >> 1);
+      const uint32_t addr = ((c >> 3) ? vb1 : vb0) + tok * 128 + (((c & 7) ^ li) << 4);
+      uint32_t r0, r1, r2, r3;
+      ldmatrix_x4_trans(addr, r0, r1, r2, r3);
+      r0 &= vm0;
+      r1 &= vm1;
+      r2 &= vm0;
+      r3 &= vm1;
+      mma_16816<T>(o[2 * qd], phi, r0, r1);
+      mma_16816<T>(o[2 * qd], plo, r0, r1);
+      mma_16816<T>(o[2 * qd + 1], phi, r2, r3);
+      mma_16816<T>(o[2 * qd + 1], plo, r2, r3);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cnt(&cx.empty[s], arrivals);
+  }
+  g += ntiles;
+
+  l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 1);
+  l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 2);
+  l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 1);
+  l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 2);
+  float* cw = cx.comb + w * kRowBlock * kCombStride;
+#pragma unroll
+  for (int dn = 0; dn < 16; ++dn) {
+    *reinterpret_cast<float2*>(cw + r_lo * kCombStride + dn * 8 + 2 * cq) =
+        make_float2(o[dn][0], o[dn][1]);
+    *reinterpret_cast<float2*>(cw + (r_lo + 8) * kCombStride + dn * 8 + 2 * cq) =
+        make_float2(o[dn][2], o[dn][3]);
+  }
+  if (cq == 0) {
+    cw[r_lo * kCombStride + kHeadDim] = m_r[0];
+    cw[r_lo * kCombStride + kHeadDim + 1] = l_r[0];
+    cw[(r_lo + 8) * kCombStride + kHeadDim] = m_r[1];
+    cw[(r_lo + 8) * kCombStride + kHeadDim + 1] = l_r[1];
+  }
 }
 
 template <typename T>
@@ -193,227 +345,24 @@ __global__ void __launch_bounds__(kThreadsAttn, 2)
 
   // -------------------------------------------------------------- consumers
   const int tid = threadIdx.x;  // 0..127
-  const int w = warp;
-  const int r_lo = lane >> 2, cq = lane & 3;
   const int G = a.G;
-  const bool causal = view == 1;
+  ConsumerCtx cx{stages, full, empty, flags, comb, warp, lane, view == 1};
   uint32_t g = 0;
   bool aborted = false;
 
   for (int it = it0; it < it1; ++it) {
     const WorkItem wi = items[it];
     const SeqInfo si = seqs[wi.seq];
-    const bool key_mode = wi.key_mode != 0;
-    const int my_rb = key_mode ? wi.rb0 : wi.rb0 + w;
-    const bool has_rows = key_mode || (w < wi.nrb);
     const int P = si.qrows * G;
-    const int p_lo = my_rb * kRowBlock + r_lo, p_hi = p_lo + 8;
-
-    // Query fragments (A operand, row-major 16 x 16 per k-step).
-    uint32_t qa[8][4];
-    {
-      const T* q_lo = nullptr;
-      const T* q_hi = nullptr;
-      if (has_rows && p_lo < P)
-        q_lo = a.q + (static_cast<int64_t>(si.q_row0 + p_lo / G) * a.hq + wi.kvh * G + p_lo % G) *
-                         kHeadDim;
-      if (has_rows && p_hi < P)
-        q_hi = a.q + (static_cast<int64_t>(si.q_row0 + p_hi / G) * a.hq + wi.kvh * G + p_hi % G) *
-                         kHeadDim;
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const int col = kk * 16 + 2 * cq;
-        qa[kk][0] = q_lo ? __ldg(reinterpret_cast<const uint32_t*>(q_lo + col)) : 0u;
-        qa[kk][1] = q_hi ? __ldg(reinterpret_cast<const uint32_t*>(q_hi + col)) : 0u;
-        qa[kk][2] = q_lo ? __ldg(reinterpret_cast<const uint32_t*>(q_lo + col + 8)) : 0u;
-        qa[kk][3] = q_hi ? __ldg(reinterpret_cast<const uint32_t*>(q_hi + col + 8)) : 0u;
-      }
-    }
-    const int lim_lo = (causal && p_lo < P) ? si.length - si.qrows + p_lo / G + 1 : si.length;
-    const int lim_hi = (causal && p_hi < P) ? si.length - si.qrows + p_hi / G + 1 : si.length;
-    const int lim_min = min(lim_lo, lim_hi);
-
-    float m_r[2] = {-INFINITY, -INFINITY};
-    float l_r[2] = {0.f, 0.f};
-    float o[16][4];
-#pragma unroll
-    for (int dn = 0; dn < 16; ++dn) o[dn][0] = o[dn][1] = o[dn][2] = o[dn][3] = 0.f;
-
-    const int ntiles = wi.kt1 - wi.kt0;
-    for (int jt = 0; jt < ntiles; ++jt) {
-      const int s = g % kStages;
-      const uint32_t ph = (g / kStages) & 1u;
-      // After an abort the warp keeps walking the same tiles without waiting
-      // or computing, so all consumer warps still meet at the same named
-      // barriers below.
-      if (!aborted && (flags[0] || !wait_bounded(&full[s], ph, flags))) aborted = true;
-      const bool mine = !aborted && has_rows && (!key_mode || (jt & (kConsumerWarps - 1)) == w);
-      if (mine) {
-        const uint32_t kb0 = smem_u32(stages + s * kStageBytes);
-        const uint32_t kb1 = kb0 + kHalfBytes, vb0 = kb0 + 2 * kHalfBytes,
-                       vb1 = kb0 + 3 * kHalfBytes;
-        const int tbase = (wi.kt0 + jt) * kTileTokens;
-        const int mi = lane >> 3, li = lane & 7;
-
-        // ---- S = Q K^T (16 packed rows x 16 tokens)
-        float sc[2][4];
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-#pragma unroll
-          for (int sp = 0; sp < 2; ++sp) {
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-              const int tok = nt * 8 + li;
-              const int c = sp * 4 + mi;
-              const uint32_t addr = (h ? kb1 : kb0) + tok * 128 + ((c ^ li) << 4);
-              uint32_t b0, b1, b2, b3;
-              ldmatrix_x4(addr, b0, b1, b2, b3);
-              const int kk = h * 4 + sp * 2;
-              mma_16816<T>(sc[nt], qa[kk], b0, b1);
-              mma_16816<T>(sc[nt], qa[kk + 1], b2, b3);
-            }
-          }
-        }
-        // ---- mask (causal limit per row; tokens past the sequence end)
-        if (tbase + kTileTokens > lim_min) {
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int t = tbase + nt * 8 + 2 * cq + e;
-              if (t >= lim_lo) sc[nt][e] = -INFINITY;
-              if (t >= lim_hi) sc[nt][2 + e] = -INFINITY;
-            }
-        }
-        // ---- online softmax (base 2, scores scaled by log2(e)/sqrt(d))
-        float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
-        float mx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-        const float mn0 = fmaxf(m_r[0], mx0 * a.scale_log2);
-        const float mn1 = fmaxf(m_r[1], mx1 * a.scale_log2);
-        const float base0 = mn0 == -INFINITY ? 0.f : mn0;
-        const float base1 = mn1 == -INFINITY ? 0.f : mn1;
-        const float al0 = fast_exp2(m_r[0] - base0), al1 = fast_exp2(m_r[1] - base1);
-        m_r[0] = mn0;
-        m_r[1] = mn1;
-        float p[2][4];
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          p[nt][0] = fast_exp2(fmaf(sc[nt][0], a.scale_log2, -base0));
-          p[nt][1] = fast_exp2(fmaf(sc[nt][1], a.scale_log2, -base0));
-          p[nt][2] = fast_exp2(fmaf(sc[nt][2], a.scale_log2, -base1));
-          p[nt][3] = fast_exp2(fmaf(sc[nt][3], a.scale_log2, -base1));
-        }
-        l_r[0] = l_r[0] * al0 + (p[0][0] + p[0][1]) + (p[1][0] + p[1][1]);
-        l_r[1] = l_r[1] * al1 + (p[0][2] + p[0][3]) + (p[1][2] + p[1][3]);
-#pragma unroll
-        for (int dn = 0; dn < 16; ++dn) {
-          o[dn][0] *= al0;
-          o[dn][1] *= al0;
-          o[dn][2] *= al1;
-          o[dn][3] *= al1;
-        }
-        // ---- P as A fragments: high 16-bit part and the rounding residual
-        uint32_t phi[4], plo[4];
-        {
-          const float pv[4][2] = {{p[0][0], p[0][1]}, {p[0][2], p[0][3]},
-                                  {p[1][0], p[1][1]}, {p[1][2], p[1][3]}};
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            phi[r] = pack2<T>(pv[r][0], pv[r][1]);
-            const float2 f = unpack2<T>(phi[r]);
-            plo[r] = pack2<T>(pv[r][0] - f.x, pv[r][1] - f.y);
-          }
-        }
-        // ---- V fragment masks for tokens past the sequence end (the pool
-        // may hold anything there; zeroing keeps 0 * garbage out of O).
-        uint32_t vm0 = 0xffffffffu, vm1 = 0xffffffffu;
-        if (tbase + kTileTokens > si.length) {
-          const int ta = tbase + 2 * cq;
-          vm0 = (ta < si.length ? 0x0000ffffu : 0u) | (ta + 1 < si.length ? 0xffff0000u : 0u);
-          vm1 = (ta + 8 < si.length ? 0x0000ffffu : 0u) | (ta + 9 < si.length ? 0xffff0000u : 0u);
-        }
-        // ---- O += P V
-#pragma unroll
-        for (int qd = 0; qd < 8; ++qd) {
-          const int tok = (mi & 1) * 8 + li;
-          const int c = 2 * qd + (mi >> 1);
-          const uint32_t addr = ((c >> 3) ? vb1 : vb0) + tok * 128 + (((c & 7) ^ li) << 4);
-          uint32_t r0, r1, r2, r3;
-          ldmatrix_x4_trans(addr, r0, r1, r2, r3);
-          r0 &= vm0;
-          r1 &= vm1;
-          r2 &= vm0;
-          r3 &= vm1;
-          mma_16816<T>(o[2 * qd], phi, r0, r1);
-          mma_16816<T>(o[2 * qd], plo, r0, r1);
-          mma_16816<T>(o[2 * qd + 1], phi, r2, r3);
-          mma_16816<T>(o[2 * qd + 1], plo, r2, r3);
-        }
-      }
-      __syncwarp();
-      if (lane == 0 && !aborted) mbar_arrive(&empty[s]);
-      ++g;
-    }
-
-    // ---------------------------------------------------------- epilogue
-    l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 1);
-    l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 2);
-    l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 1);
-    l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 2);
-    if (has_rows) {
-      float* cw = comb + w * kRowBlock * kCombStride;
-#pragma unroll
-      for (int dn = 0; dn < 16; ++dn) {
-        *reinterpret_cast<float2*>(cw + r_lo * kCombStride + dn * 8 + 2 * cq) =
-            make_float2(o[dn][0], o[dn][1]);
-        *reinterpret_cast<float2*>(cw + (r_lo + 8) * kCombStride + dn * 8 + 2 * cq) =
-            make_float2(o[dn][2], o[dn][3]);
-      }
-      if (cq == 0) {
-        cw[r_lo * kCombStride + kHeadDim] = m_r[0];
-        cw[r_lo * kCombStride + kHeadDim + 1] = l_r[0];
-        cw[(r_lo + 8) * kCombStride + kHeadDim] = m_r[1];
-        cw[(r_lo + 8) * kCombStride + kHeadDim + 1] = l_r[1];
-      }
-    }
+    row_item<T>(a, wi, si, cx, g, aborted);
     named_barrier_sync(1, kConsumerWarps * 32);
 
-    const int nrows = min(key_mode ? kRowBlock : wi.nrb * kRowBlock, P - wi.rb0 * kRowBlock);
+    const int nrows = min(wi.nrb * kRowBlock, P - wi.rb0 * kRowBlock);
     const int d4 = (tid & 31) * 4;
     for (int r = tid >> 5; r < nrows; r += kConsumerWarps) {
-      float M, L;
-      float4 acc;
-      if (key_mode) {
-        M = -INFINITY;
-#pragma unroll
-        for (int ww = 0; ww < kConsumerWarps; ++ww)
-          M = fmaxf(M, comb[(ww * kRowBlock + r) * kCombStride + kHeadDim]);
-        const float base = M == -INFINITY ? 0.f : M;
-        L = 0.f;
-        acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int ww = 0; ww < kConsumerWarps; ++ww) {
-          const float* row = comb + (ww * kRowBlock + r) * kCombStride;
-          const float sc = fast_exp2(row[kHeadDim] - base);
-          L = fmaf(row[kHeadDim + 1], sc, L);
-          const float4 x = *reinterpret_cast<const float4*>(row + d4);
-          acc.x = fmaf(x.x, sc, acc.x);
-          acc.y = fmaf(x.y, sc, acc.y);
-          acc.z = fmaf(x.z, sc, acc.z);
-          acc.w = fmaf(x.w, sc, acc.w);
-        }
-      } else {
-        const float* row = comb + r * kCombStride;  // warp r/16, row r%16: contiguous
-        M = row[kHeadDim];
-        L = row[kHeadDim + 1];
-        acc = *reinterpret_cast<const float4*>(row + d4);
-      }
+      const float* row = comb + r * kCombStride;  // warp r/16, row r%16: contiguous
+      const float M = row[kHeadDim], L = row[kHeadDim + 1];
+      const float4 acc = *reinterpret_cast<const float4*>(row + d4);
       const int pr = wi.rb0 * kRowBlock + r;
       if (wi.group < 0) {
         const float inv = 1.f / L;
@@ -442,32 +391,11 @@ __global__ void __launch_bounds__(kThreadsAttn, 2)
       if (flags[1]) {
         __threadfence();
         const SplitGroup gi = groups[wi.group];
-        for (int r = tid >> 5; r < gi.rows; r += kConsumerWarps) {
-          float M = -INFINITY;
-          for (int sidx = 0; sidx < gi.nsplit; ++sidx) {
-            const float* rec = a.partials + gi.part0 + sidx * gi.rec_floats;
-            M = fmaxf(M, __ldcg(rec + gi.rows * kHeadDim + r));
-          }
-          const float base = M == -INFINITY ? 0.f : M;
-          float L = 0.f;
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int sidx = 0; sidx < gi.nsplit; ++sidx) {
-            const float* rec = a.partials + gi.part0 + sidx * gi.rec_floats;
-            const float sc = fast_exp2(__ldcg(rec + gi.rows * kHeadDim + r) - base);
-            L = fmaf(__ldcg(rec + gi.rows * (kHeadDim + 1) + r), sc, L);
-            const float4 x = __ldcg(reinterpret_cast<const float4*>(rec + r * kHeadDim + d4));
-            acc.x = fmaf(x.x, sc, acc.x);
-            acc.y = fmaf(x.y, sc, acc.y);
-            acc.z = fmaf(x.z, sc, acc.z);
-            acc.w = fmaf(x.w, sc, acc.w);
-          }
-          const float inv = 1.f / L;
+        merge_partials<T>(a.partials, gi, tid, kConsumerWarps * 32, [&](int r) {
           const int pr = wi.rb0 * kRowBlock + r;
-          T* dst = a.out +
-                   (static_cast<int64_t>(si.q_row0 + pr / G) * a.hq + wi.kvh * G + pr % G) *
-                       kHeadDim + d4;
-          store4<T>(dst, acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-        }
+          return a.out +
+                 (static_cast<int64_t>(si.q_row0 + pr / G) * a.hq + wi.kvh * G + pr % G) * kHeadDim;
+        });
         if (tid == 0) a.counters[wi.group] = 0;
       }
     }
@@ -499,14 +427,10 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// Pool viewed as [cache_slots][hkv*2][64] (64-element half rows of 128 B);
-// box = 16 slots x 1 half-row x 64 elements, 128-byte swizzle.
-int encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int hkv, int64_t cache_slots) {
+int encode_3d(CUtensorMap* map, const void* pool, int dtype, const cuuint64_t dims[3],
+              const cuuint64_t strides[2], const cuuint32_t box[3]) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return fail(FE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
-  cuuint64_t dims[3] = {64, cuuint64_t(hkv) * 2, cuuint64_t(cache_slots)};
-  cuuint64_t strides[2] = {128, cuuint64_t(hkv) * 256};
-  cuuint32_t box[3] = {64, 1, kTileTokens};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map,
                   dtype == FE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -517,6 +441,27 @@ int encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int hkv, int6
   if (r != CUDA_SUCCESS)
     return fail(FE_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(r));
   return FE_OK;
+}
+
+// Row kernel: pool viewed as [cache_slots][hkv*2][64] (64-element head-half
+// rows of 128 B); box = 16 slots x 1 head-half x 64 elements.
+int encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int hkv, int64_t cache_slots) {
+  const cuuint64_t dims[3] = {64, cuuint64_t(hkv) * 2, cuuint64_t(cache_slots)};
+  const cuuint64_t strides[2] = {128, cuuint64_t(hkv) * 256};
+  const cuuint32_t box[3] = {64, 1, kTileTokens};
+  return encode_3d(map, pool, dtype, dims, strides, box);
+}
+
+// Decode kernel: the same memory walked slots-first, [hkv*2][cache_slots][64];
+// box = 2H head-halves x 16 slots x 64 elements, so one TMA copies a 16-token
+// tile of H heads (a contiguous 16 x H x 256 B block of the page) and lays it
+// out head-half by head-half, 16 swizzled rows each.
+int encode_decode_map(CUtensorMap* map, const void* pool, int dtype, int hkv, int heads,
+                      int64_t cache_slots) {
+  const cuuint64_t dims[3] = {64, cuuint64_t(cache_slots), cuuint64_t(hkv) * 2};
+  const cuuint64_t strides[2] = {cuuint64_t(hkv) * 256, 128};
+  const cuuint32_t box[3] = {64, kTileTokens, cuuint32_t(2 * heads)};
+  return encode_3d(map, pool, dtype, dims, strides, box);
 }
 
 template <typename T>
@@ -564,19 +509,20 @@ struct fe_attn_plan {
   bool graph_shape_set = false;
   int graph_batch = 0, graph_rows = 0;
   PlanResult last;
-  int grid_view[2] = {0, 0};
-  // cached tensor maps
-  CUtensorMap kmap, vmap;
+  int grid_view[3] = {0, 0, 0};
+  // cached tensor maps (row kernel, decode kernel)
+  CUtensorMap kmap, vmap, kmap_dec, vmap_dec;
   const void* kmap_ptr = nullptr;
   const void* vmap_ptr = nullptr;
+  bool per_head_tma = false;  // decode falls back to per-head-half boxes
 };
 
 namespace {
 
 size_t meta_capacity(const PlanConfig& c) {
-  size_t per_view = sizeof(int32_t) * (c.grid_cap + 1) + sizeof(WorkItem) * c.max_items +
-                    sizeof(SplitGroup) * c.max_groups + 64;
-  return sizeof(MetaHeader) + 2 * per_view + sizeof(SeqInfo) * c.max_batch +
+  size_t per_view = sizeof(int32_t) * (std::max(c.grid_cap, c.dec_grid_cap) + 1) +
+                    sizeof(WorkItem) * c.max_items + sizeof(SplitGroup) * c.max_groups + 64;
+  return sizeof(MetaHeader) + 3 * per_view + sizeof(SeqInfo) * c.max_batch +
          sizeof(int32_t) * size_t(c.max_batch) * c.max_pages + 256;
 }
 
@@ -601,8 +547,14 @@ int check_shape(int hq, int hkv, int dim, int page, int max_batch, int max_pages
   return FE_OK;
 }
 
+int gcd8(int hkv) {
+  int h = 8;
+  while (hkv % h) h >>= 1;
+  return h;
+}
+
 PlanConfig make_config(int hq, int hkv, int dim, int page, int max_batch, int max_pages,
-                       int num_blocks, int grid_cap) {
+                       int num_blocks, int grid_cap, int dec_grid_cap) {
   PlanConfig c{};
   c.hq = hq;
   c.hkv = hkv;
@@ -612,6 +564,8 @@ PlanConfig make_config(int hq, int hkv, int dim, int page, int max_batch, int ma
   c.max_pages = max_pages;
   c.num_blocks = num_blocks;
   c.grid_cap = grid_cap;
+  c.dec_grid_cap = dec_grid_cap;
+  c.dec_heads = gcd8(hkv);
   int64_t items = int64_t(max_batch) * hkv * 64;
   if (items < 8192) items = 8192;
   if (items > (1 << 20)) items = 1 << 20;
@@ -658,7 +612,7 @@ int fe_attn_plan_create(int hq, int hkv, int dim, int page, int max_batch, int m
   if (rc != FE_OK) return rc;
   auto* p = new (std::nothrow) fe_attn_plan();
   if (!p) return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_plan_create: out of host memory");
-  p->cfg = make_config(hq, hkv, dim, page, max_batch, max_pages, num_blocks, sms * per_sm);
+  p->cfg = make_config(hq, hkv, dim, page, max_batch, max_pages, num_blocks, sms * per_sm, sms);
   p->dtype = dtype;
   p->device = dev;
   p->meta_cap = meta_capacity(p->cfg);
@@ -691,7 +645,8 @@ int fe_attn_plan_create_host(int hq, int hkv, int dim, int page, int max_batch, 
   if (grid_cap <= 0) return fail(FE_ERR_INVALID_ARGUMENT, "grid_cap must be positive");
   auto* p = new (std::nothrow) fe_attn_plan();
   if (!p) return fail(FE_ERR_INVALID_ARGUMENT, "out of host memory");
-  p->cfg = make_config(hq, hkv, dim, page, max_batch, max_pages, num_blocks, grid_cap);
+  p->cfg = make_config(hq, hkv, dim, page, max_batch, max_pages, num_blocks, grid_cap,
+                       std::max(1, grid_cap / 2));
   p->dtype = dtype;
   p->host_only = true;
   p->meta_cap = meta_capacity(p->cfg);
@@ -729,10 +684,7 @@ int fe_attn_plan_prepare(fe_attn_plan* p, const int32_t* qo, const int32_t* kv,
     if (res.n_groups > 0)
       FE_CUDA_TRY(cudaMemsetAsync(p->d_counters, 0, sizeof(int32_t) * res.n_groups, s));
   }
-  MetaHeader h;
-  std::memcpy(&h, res.meta.data(), sizeof(h));
-  p->grid_view[0] = h.grid[0];
-  p->grid_view[1] = h.grid[1];
+  for (int c = 0; c < 3; ++c) p->grid_view[c] = res.grid[c];
   p->last = std::move(res);
   p->prepared = true;
   p->fixed_grid = graph != 0;
@@ -750,36 +702,58 @@ int fe_attn_run(fe_attn_plan* p, const void* q, const void* k_pool, const void* 
   if (p->host_only) return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_run: host-only plan");
   if (!p->prepared) return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_run: plan not prepared");
   const int view = causal ? 1 : 0;
-  const int grid = p->fixed_grid ? p->cfg.grid_cap : p->grid_view[view];
-  if (grid == 0) return FE_OK;
+  // A plan prepared for graph capture launches both kernels at full width
+  // every time (CTAs without work exit at once), so the captured launches
+  // stay valid for any later metadata.
+  const int grid_rows = p->fixed_grid ? p->cfg.grid_cap : p->grid_view[view];
+  const int grid_dec = p->fixed_grid ? p->cfg.dec_grid_cap : p->grid_view[2];
+  if (grid_rows == 0 && grid_dec == 0) return FE_OK;
   if (!q || !k_pool || !v_pool || !out)
     return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_run: null pointer");
   if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out))
     return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_run: buffers must be 16-byte aligned");
   const int64_t cache_slots = int64_t(p->cfg.num_blocks + 1) * p->cfg.page;
+  const int H = p->cfg.dec_heads;
   if (k_pool != p->kmap_ptr) {
     int rc = encode_pool_map(&p->kmap, k_pool, p->dtype, p->cfg.hkv, cache_slots);
     if (rc != FE_OK) return rc;
+    if (encode_decode_map(&p->kmap_dec, k_pool, p->dtype, p->cfg.hkv, H, cache_slots) != FE_OK)
+      p->per_head_tma = true;
     p->kmap_ptr = k_pool;
   }
   if (v_pool != p->vmap_ptr) {
     int rc = encode_pool_map(&p->vmap, v_pool, p->dtype, p->cfg.hkv, cache_slots);
     if (rc != FE_OK) return rc;
+    if (encode_decode_map(&p->vmap_dec, v_pool, p->dtype, p->cfg.hkv, H, cache_slots) != FE_OK)
+      p->per_head_tma = true;
     p->vmap_ptr = v_pool;
   }
   const float scale_log2 = 1.4426950408889634f / sqrtf(float(p->cfg.dim));
   auto s = static_cast<cudaStream_t>(stream);
+  const int G = p->cfg.hq / p->cfg.hkv;
+  const CUtensorMap& kd = p->per_head_tma ? p->kmap : p->kmap_dec;
+  const CUtensorMap& vd = p->per_head_tma ? p->vmap : p->vmap_dec;
   if (p->dtype == FE_DTYPE_BF16) {
     AttnArgs<__nv_bfloat16> a{p->d_meta, static_cast<const __nv_bfloat16*>(q),
                               static_cast<__nv_bfloat16*>(out), p->d_partials, p->d_counters,
-                              device_error_word(), p->cfg.hq, p->cfg.hq / p->cfg.hkv, p->cfg.page, view, scale_log2};
-    paged_attn_kernel<__nv_bfloat16><<<grid, kThreadsAttn, kSmemBytes, s>>>(p->kmap, p->vmap, a);
+                              device_error_word(), p->cfg.hq, G, p->cfg.page, view, scale_log2};
+    if (grid_dec > 0) {
+      int rc = decode_launch(p->dtype, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
+      if (rc != FE_OK) return rc;
+    }
+    if (grid_rows > 0)
+      paged_attn_kernel<__nv_bfloat16><<<grid_rows, kThreadsAttn, kSmemBytes, s>>>(p->kmap,
+                                                                                  p->vmap, a);
   } else {
     AttnArgs<__half> a{p->d_meta, static_cast<const __half*>(q), static_cast<__half*>(out),
-                       p->d_partials, p->d_counters, device_error_word(), p->cfg.hq,
-                       p->cfg.hq / p->cfg.hkv,
+                       p->d_partials, p->d_counters, device_error_word(), p->cfg.hq, G,
                        p->cfg.page, view, scale_log2};
-    paged_attn_kernel<__half><<<grid, kThreadsAttn, kSmemBytes, s>>>(p->kmap, p->vmap, a);
+    if (grid_dec > 0) {
+      int rc = decode_launch(p->dtype, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
+      if (rc != FE_OK) return rc;
+    }
+    if (grid_rows > 0)
+      paged_attn_kernel<__half><<<grid_rows, kThreadsAttn, kSmemBytes, s>>>(p->kmap, p->vmap, a);
   }
   FE_CUDA_TRY(cudaGetLastError());
   return FE_OK;
@@ -797,7 +771,8 @@ int fe_attn_plan_get_info(const fe_attn_plan* p, fe_attn_plan_info* info) {
   info->prefill_items = p->last.prefill_items;
   info->split_sequences = p->last.split_units;
   info->chunk_tiles = p->last.chunk_tiles;
-  info->grid_ctas = p->fixed_grid ? p->cfg.grid_cap : p->last.grid;
+  info->grid_ctas = p->fixed_grid ? p->cfg.grid_cap + p->cfg.dec_grid_cap
+                                  : p->last.grid[1] + p->last.grid[2];
   info->kv_tokens = p->last.kv_tokens;
   return FE_OK;
 }

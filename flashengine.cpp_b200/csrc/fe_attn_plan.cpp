@@ -30,12 +30,12 @@ struct View {
 
 // Split every unit's key range into balanced chunks and assign the items to
 // CTAs, longest first onto the least-loaded CTA.
-int build_view(const PlanConfig& cfg, const std::vector<Unit>& units, bool fixed_grid, View& v,
-               std::string& err) {
+int build_view(const PlanConfig& cfg, const std::vector<Unit>& units, int grid_cap_in,
+               int items_per_cta, int min_chunk, bool fixed_grid, View& v, std::string& err) {
   int64_t total_tiles = 0;
   for (const auto& u : units) total_tiles += u.tiles;
-  const int grid_cap = std::max(1, cfg.grid_cap);
-  int chunk = std::max<int>(16, ceil_div(total_tiles, int64_t(grid_cap) * 4));
+  const int grid_cap = std::max(1, grid_cap_in);
+  int chunk = std::max<int>(min_chunk, ceil_div(total_tiles, int64_t(grid_cap) * items_per_cta));
   for (int attempt = 0; attempt < 32; ++attempt) {
     v.items.clear();
     v.groups.clear();
@@ -121,6 +121,102 @@ int build_view(const PlanConfig& cfg, const std::vector<Unit>& units, bool fixed
   return FE_OK;
 }
 
+// Decode lists are bandwidth-bound and their cost is proportional to key
+// tiles, so they are balanced exactly: the units' tile ranges are laid end to
+// end and cut into `grid` equal contiguous pieces, one per CTA. A unit cut
+// into several pieces becomes a split unit (merged by the last piece to
+// finish). Every CTA streams the same number of tiles, to within one.
+int build_cut_view(const PlanConfig& cfg, const std::vector<Unit>& units, int grid_cap_in,
+                   int min_tiles_per_cta, bool fixed_grid, View& v, std::string& err) {
+  v = View{};
+  int64_t total = 0;
+  for (const auto& u : units) total += u.tiles;
+  if (total == 0) {
+    v.grid = 0;
+    return FE_OK;
+  }
+  const int grid_cap = std::max(1, grid_cap_in);
+  int n = static_cast<int>(std::min<int64_t>(grid_cap, std::max<int64_t>(1, total / min_tiles_per_cta)));
+  const int64_t per = (total + n - 1) / n;
+  n = static_cast<int>((total + per - 1) / per);
+  // pass 1: pieces per unit
+  std::vector<int> pieces(units.size(), 0);
+  {
+    int64_t room = per;
+    for (size_t i = 0; i < units.size(); ++i) {
+      int64_t left = units[i].tiles;
+      while (left > 0) {
+        const int64_t take = std::min(left, room);
+        ++pieces[i];
+        left -= take;
+        room -= take;
+        if (room == 0) room = per;
+      }
+    }
+  }
+  // pass 2: emit items CTA by CTA
+  std::vector<int> group_of(units.size(), -1), part0_of(units.size(), -1), next_split(units.size(), 0);
+  for (size_t i = 0; i < units.size(); ++i) {
+    if (pieces[i] > 1) {
+      const int rec = partial_rec_floats(units[i].rows);
+      group_of[i] = static_cast<int>(v.groups.size());
+      part0_of[i] = static_cast<int>(v.partial_floats);
+      v.groups.push_back(SplitGroup{pieces[i], part0_of[i], rec, units[i].rows});
+      v.partial_floats += int64_t(rec) * pieces[i];
+      ++v.split_units;
+    }
+  }
+  v.cta_off.clear();
+  int64_t room = per;
+  int cta = 0;
+  v.cta_off.push_back(0);
+  for (size_t i = 0; i < units.size(); ++i) {
+    const Unit& u = units[i];
+    int kt = 0;
+    while (kt < u.tiles) {
+      const int take = static_cast<int>(std::min<int64_t>(u.tiles - kt, room));
+      WorkItem it;
+      it.seq = u.seq;
+      it.kvh = static_cast<int16_t>(u.kvh);
+      it.key_mode = static_cast<int16_t>(u.key_mode);
+      it.rb0 = u.rb0;
+      it.nrb = u.nrb;
+      it.kt0 = kt;
+      it.kt1 = kt + take;
+      const int s = next_split[i]++;
+      it.group = group_of[i];
+      it.part = group_of[i] >= 0 ? part0_of[i] + s * partial_rec_floats(u.rows) : -1;
+      v.items.push_back(it);
+      (u.key_mode ? v.decode_items : v.prefill_items)++;
+      kt += take;
+      room -= take;
+      if (room == 0) {
+        room = per;
+        ++cta;
+        v.cta_off.push_back(static_cast<int32_t>(v.items.size()));
+      }
+    }
+  }
+  if (static_cast<int>(v.cta_off.size()) == cta + 1 && v.cta_off.back() != static_cast<int32_t>(v.items.size())) {
+    ++cta;
+    v.cta_off.push_back(static_cast<int32_t>(v.items.size()));
+  }
+  v.grid = static_cast<int>(v.cta_off.size()) - 1;
+  v.chunk = static_cast<int>(per);
+  if (static_cast<int>(v.items.size()) > cfg.max_items || v.partial_floats > cfg.partial_capacity ||
+      static_cast<int>(v.groups.size()) > cfg.max_groups) {
+    err = "decode work exceeds the plan's item / split-workspace capacity";
+    return FE_ERR_CAPACITY;
+  }
+  if (fixed_grid && v.grid < grid_cap) {
+    // graph mode launches grid_cap CTAs; the extra ones get empty lists
+    while (static_cast<int>(v.cta_off.size()) < grid_cap + 1)
+      v.cta_off.push_back(static_cast<int32_t>(v.items.size()));
+    v.grid = grid_cap;
+  }
+  return FE_OK;
+}
+
 }  // namespace
 
 int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, const int32_t* pages,
@@ -192,7 +288,9 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
     const int RB = ceil_div(P, kRowBlock);
     const int tiles_full = ceil_div(length, kTileTokens);
     if (RB == 1) {
-      for (int h = 0; h < cfg.hkv; ++h) key_units.push_back(Unit{b, h, 1, 0, 1, tiles_full, P});
+      const int H = cfg.dec_heads;
+      for (int h = 0; h < cfg.hkv; h += H)
+        key_units.push_back(Unit{b, h, 1, 0, 1, tiles_full, H * P});
     } else {
       for (int rb0 = 0; rb0 < RB; rb0 += kConsumerWarps) {
         const int nrb = std::min(kConsumerWarps, RB - rb0);
@@ -209,28 +307,45 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
     }
   }
 
-  // View 0: non-causal, view 1: causal. Identical when no row-mode work.
-  View views[2];
-  const bool same = row_units_full.empty();
-  for (int c = 0; c < (same ? 1 : 2); ++c) {
-    std::vector<Unit> units = key_units;
-    const auto& ru = c == 0 ? row_units_full : row_units_causal;
-    units.insert(units.end(), ru.begin(), ru.end());
-    int rc = build_view(cfg, units, fixed_grid, views[c], err);
-    if (rc != FE_OK) return rc;
+  // List 0: row work, non-causal; 1: row work, causal (identical key ranges
+  // when there is no row work); 2: decode work.
+  View views[3];
+  int rc = build_view(cfg, row_units_full, cfg.grid_cap, 4, 16, fixed_grid, views[0], err);
+  if (rc != FE_OK) return rc;
+  rc = build_view(cfg, row_units_causal, cfg.grid_cap, 4, 16, fixed_grid, views[1], err);
+  if (rc != FE_OK) return rc;
+  rc = build_cut_view(cfg, key_units, cfg.dec_grid_cap, 8, fixed_grid, views[2], err);
+  if (rc != FE_OK) return rc;
+  // Both kernels of one run share the split workspace and counters: offset
+  // the decode list's records and groups past the larger row list's.
+  const int64_t row_floats = std::max(views[0].partial_floats, views[1].partial_floats);
+  const int row_groups = static_cast<int>(std::max(views[0].groups.size(), views[1].groups.size()));
+  for (auto& it : views[2].items) {
+    if (it.group >= 0) {
+      it.group += row_groups;
+      it.part += static_cast<int32_t>(row_floats);
+    }
+  }
+  {
+    std::vector<SplitGroup> shifted(row_groups);
+    for (auto gi : views[2].groups) {
+      gi.part0 += static_cast<int32_t>(row_floats);
+      shifted.push_back(gi);
+    }
+    views[2].groups.swap(shifted);
+  }
+  if (row_floats + views[2].partial_floats > cfg.partial_capacity ||
+      row_floats + views[2].partial_floats > int64_t(INT32_MAX) ||
+      static_cast<int>(views[2].groups.size()) > cfg.max_groups) {
+    err = "attention work exceeds the plan's split-workspace capacity";
+    return FE_ERR_CAPACITY;
   }
 
-  // Pack: header | per view: cta_off, items, groups | seqs | pages.
+  // Pack: header | per list: cta_off, items, groups | seqs | pages.
   size_t off = align16(sizeof(MetaHeader));
-  size_t cta_off_off[2], items_off[2], groups_off[2];
-  for (int c = 0; c < 2; ++c) {
-    const View& v = views[same ? 0 : c];
-    if (same && c == 1) {
-      cta_off_off[1] = cta_off_off[0];
-      items_off[1] = items_off[0];
-      groups_off[1] = groups_off[0];
-      continue;
-    }
+  size_t cta_off_off[3], items_off[3], groups_off[3];
+  for (int c = 0; c < 3; ++c) {
+    const View& v = views[c];
     cta_off_off[c] = off;
     off = align16(off + sizeof(int32_t) * v.cta_off.size());
     items_off[c] = off;
@@ -248,9 +363,8 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
   }
   out.meta.assign(off, 0);
   uint8_t* m = out.meta.data();
-  for (int c = 0; c < 2; ++c) {
-    const View& v = views[same ? 0 : c];
-    if (same && c == 1) break;
+  for (int c = 0; c < 3; ++c) {
+    const View& v = views[c];
     if (!v.cta_off.empty())
       std::memcpy(m + cta_off_off[c], v.cta_off.data(), sizeof(int32_t) * v.cta_off.size());
     if (!v.items.empty())
@@ -262,8 +376,8 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
   if (total_pages) std::memcpy(m + pages_off, pages, sizeof(int32_t) * total_pages);
 
   MetaHeader h{};
-  for (int c = 0; c < 2; ++c) {
-    const View& v = views[same ? 0 : c];
+  for (int c = 0; c < 3; ++c) {
+    const View& v = views[c];
     h.n_items[c] = static_cast<int32_t>(v.items.size());
     h.n_groups[c] = static_cast<int32_t>(v.groups.size());
     h.grid[c] = v.grid;
@@ -276,19 +390,19 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
   h.seqs_off = static_cast<int32_t>(seqs_off);
   h.pages_off = static_cast<int32_t>(pages_off);
   h.total_bytes = static_cast<int32_t>(off);
-  h.chunk_tiles = views[0].chunk;
+  h.chunk_tiles = views[2].items.empty() ? views[1].chunk : views[2].chunk;
+  h.dec_heads = cfg.dec_heads;
   std::memcpy(m, &h, sizeof(h));
 
-  const View& vc = views[same ? 0 : 1];
-  out.n_items = static_cast<int>(vc.items.size());
-  out.n_groups = std::max(views[0].groups.size(), same ? 0 : views[1].groups.size());
-  out.decode_items = vc.decode_items;
-  out.prefill_items = vc.prefill_items;
-  out.split_units = vc.split_units;
-  out.chunk_tiles = vc.chunk;
-  out.grid = std::max(views[0].grid, same ? 0 : views[1].grid);
+  out.n_items = static_cast<int>(views[1].items.size() + views[2].items.size());
+  out.n_groups = static_cast<int>(views[2].groups.size());
+  out.decode_items = static_cast<int>(views[2].items.size());
+  out.prefill_items = static_cast<int>(views[1].items.size());
+  out.split_units = views[1].split_units + views[2].split_units;
+  out.chunk_tiles = h.chunk_tiles;
+  for (int c = 0; c < 3; ++c) out.grid[c] = views[c].grid;
   out.kv_tokens = kv_tokens;
-  out.partial_floats = std::max(views[0].partial_floats, same ? 0 : views[1].partial_floats);
+  out.partial_floats = row_floats + views[2].partial_floats;
   return FE_OK;
 }
 

@@ -56,19 +56,22 @@ struct SplitGroup {  // 16 bytes
 };
 
 // Byte offsets are from the start of the metadata buffer. Index [c] of the
-// per-view arrays selects the work list: 0 = non-causal, 1 = causal (the two
-// differ only when a sequence has row-mode work, whose key range depends on
-// the mask).
+// per-list arrays selects a work list: 0 = row-mode work for the non-causal
+// mask, 1 = row-mode work for the causal mask (the key range of a row block
+// depends on the mask), 2 = decode work (key mode, mask-independent ranges;
+// served by the decode kernel with H heads per item).
 struct MetaHeader {  // 128 bytes
-  int32_t n_items[2], n_groups[2], grid[2], cta_off_off[2], items_off[2], groups_off[2];
-  int32_t batch, rows, seqs_off, pages_off, total_bytes, chunk_tiles;
-  int32_t pad[14];
+  int32_t n_items[3], n_groups[3], grid[3], cta_off_off[3], items_off[3], groups_off[3];
+  int32_t batch, rows, seqs_off, pages_off, total_bytes, chunk_tiles, dec_heads;
+  int32_t pad[7];
 };
 static_assert(sizeof(MetaHeader) == 128, "MetaHeader layout");
 
 struct PlanConfig {
   int hq, hkv, dim, page, max_batch, max_pages, num_blocks;
-  int grid_cap;               // persistent CTAs available (SMs x CTAs per SM)
+  int grid_cap;               // persistent CTAs of the row kernel (SMs x CTAs per SM)
+  int dec_grid_cap;           // persistent CTAs of the decode kernel (one per SM)
+  int dec_heads;              // KV heads per decode item: gcd(hkv, 8)
   int max_items;              // work-item capacity
   int64_t partial_capacity;   // floats in the split-K workspace
   int max_groups;             // split-counter capacity
@@ -77,7 +80,8 @@ struct PlanConfig {
 struct PlanResult {
   std::vector<uint8_t> meta;  // packed device metadata (header first)
   int n_items = 0, n_groups = 0, decode_items = 0, prefill_items = 0, split_units = 0;
-  int chunk_tiles = 0, grid = 0;
+  int chunk_tiles = 0;
+  int grid[3] = {0, 0, 0};    // CTAs per work list (0 = nothing to launch)
   int64_t kv_tokens = 0, partial_floats = 0;
 };
 

@@ -69,20 +69,29 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Arrive `count` times at once (one thread standing in for several).
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                "r"(bytes)
                : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+// One poll of a phase; the hardware may suspend the thread for up to
+// `suspend_ns` while the phase is incomplete instead of returning at once.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity,
+                                              uint32_t suspend_ns = 1000000u) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
       : "memory");
   return ok != 0;
 }
@@ -165,6 +174,13 @@ __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t v) {
 template <>
 __device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
   return __half22float2(*reinterpret_cast<__half2*>(&v));
+}
+
+// Transpose an 8x8 matrix of 16-bit elements held in mma fragment layout.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
 }
 
 // 2^x via the hardware approximation instruction (PTX ex2.approx).

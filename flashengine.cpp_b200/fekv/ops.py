@@ -227,22 +227,25 @@ class HostPlan:
         check(self.lib.fe_attn_plan_debug_meta(self.handle, buf.ctypes.data_as(_P), n.value,
                                                ctypes.byref(n)), "meta")
         h = buf[:128].view(np.int32)
-        out = {"batch": int(h[12]), "rows": int(h[13]), "chunk_tiles": int(h[17]), "views": []}
-        seqs_off, pages_off = int(h[14]), int(h[15])
+        out = {"batch": int(h[18]), "rows": int(h[19]), "chunk_tiles": int(h[23]),
+               "dec_heads": int(h[24]), "views": []}
+        seqs_off, pages_off = int(h[20]), int(h[21])
         batch = out["batch"]
         out["seqs"] = buf[seqs_off:seqs_off + SEQ_DTYPE.itemsize * batch].view(SEQ_DTYPE)
-        for c in range(2):
-            n_items, n_groups, grid = int(h[0 + c]), int(h[2 + c]), int(h[4 + c])
-            co, io, go = int(h[6 + c]), int(h[8 + c]), int(h[10 + c])
+        # lists: 0 = row work (non-causal), 1 = row work (causal), 2 = decode work
+        for c in range(3):
+            n_items, n_groups, grid = int(h[0 + c]), int(h[3 + c]), int(h[6 + c])
+            co, io, go = int(h[9 + c]), int(h[12 + c]), int(h[15 + c])
             view = {
                 "grid": grid,
-                "cta_off": buf[co:co + 4 * (grid + 1)].view(np.int32) if grid else np.zeros(1, np.int32),
+                "cta_off": (buf[co:co + 4 * (grid + 1)].view(np.int32) if grid
+                            else np.zeros(1, np.int32)),
                 "items": buf[io:io + ITEM_DTYPE.itemsize * n_items].view(ITEM_DTYPE),
                 "groups": buf[go:go + GROUP_DTYPE.itemsize * n_groups].view(GROUP_DTYPE),
             }
             out["views"].append(view)
-        total_pages = int(pages_off)
-        out["pages_off"] = total_pages
+        total = int(h[22])
+        out["pages"] = buf[pages_off:total].view(np.int32)
         out["buf"] = buf
         return out
 

@@ -1,0 +1,153 @@
+"""Host work planner (fe_attn_plan.cpp) without a GPU: every (sequence, KV
+head, packed query row, key tile) the attention needs is covered exactly
+once by the work lists, split units are consistent, CTAs are balanced, and
+bad metadata is rejected with the reference's error classes."""
+import numpy as np
+import pytest
+
+import cases
+import fekv
+from fekv import HostPlan, workloads
+from fekv import _lib
+
+
+def _plan(w_or_case, grid_cap=296, graph=False):
+    md = w_or_case.metadata()
+    hp = HostPlan(w_or_case.hq, w_or_case.hkv, 128, w_or_case.page, md.batch,
+                  int((md.kv[1:] - md.kv[:-1]).max()) + 1, w_or_case.bf16, w_or_case.num_blocks,
+                  grid_cap=grid_cap)
+    return md, hp.prepare(md.qo, md.kv, md.pages, md.last, graph=graph), hp
+
+
+def _coverage(md, meta, hq, hkv, page, causal):
+    """Count how many times each (seq, kv head, packed row, tile) is visited."""
+    G = hq // hkv
+    H = meta["dec_heads"]
+    lengths = md.lengths(page)
+    qrows = md.qo[1:] - md.qo[:-1]
+    seen = {}
+    lists = [meta["views"][1 if causal else 0], meta["views"][2]]
+    for li, v in enumerate(lists):
+        for it in v["items"]:
+            b = int(it["seq"])
+            heads = range(int(it["kvh"]), int(it["kvh"]) + (H if li == 1 else 1))
+            P = int(qrows[b]) * G
+            rows = range(int(it["rb0"]) * 16, min(P, (int(it["rb0"]) + int(it["nrb"])) * 16))
+            for h in heads:
+                for p in rows:
+                    for t in range(int(it["kt0"]), int(it["kt1"])):
+                        key = (b, h, p, t)
+                        seen[key] = seen.get(key, 0) + 1
+    # every needed tile exactly once
+    for b in range(md.batch):
+        P = int(qrows[b]) * G
+        for h in range(hkv):
+            for p in range(P):
+                i = p // G
+                limit = int(lengths[b]) - int(qrows[b]) + i + 1 if causal else int(lengths[b])
+                need = -(-limit // 16)
+                for t in range(need):
+                    assert seen.pop((b, h, p, t), 0) == 1, (b, h, p, t)
+    # anything left over must lie beyond the causal limit of its row (row
+    # blocks share a key range) -- never beyond the sequence itself
+    for (b, h, p, t), n in seen.items():
+        assert n == 1
+        assert t * 16 < lengths[b], (b, h, p, t)
+
+
+@pytest.mark.parametrize("name", [c.name for c in cases.all_cases()])
+@pytest.mark.parametrize("causal", [True, False])
+def test_work_lists_cover_each_tile_once(name, causal):
+    case = cases.case_by_name(name)
+    md, meta, _ = _plan(case, grid_cap=8)
+    _coverage(md, meta, case.hq, case.hkv, case.page, causal)
+
+
+@pytest.mark.parametrize("maker", [workloads.c1, workloads.c2, workloads.c3, workloads.c4])
+def test_configs_plan_and_balance(maker):
+    w = maker()
+    md, meta, _ = _plan(w)
+    dec = meta["views"][2]
+    if len(dec["items"]):
+        co = dec["cta_off"]
+        loads = [int((dec["items"][co[g]:co[g + 1]]["kt1"] - dec["items"][co[g]:co[g + 1]]["kt0"]).sum())
+                 for g in range(dec["grid"])]
+        # exact cut: all CTAs but the last stream the same number of tiles
+        assert max(loads[:-1]) - min(loads[:-1]) <= 0 if len(loads) > 1 else True
+        assert dec["grid"] <= 148
+    for v in meta["views"]:
+        for it in v["items"]:
+            assert it["kt1"] > it["kt0"]
+
+
+def test_split_groups_are_consistent():
+    w = workloads.c5(steps=1)
+    md, meta, _ = _plan(w)
+    for v in meta["views"]:
+        groups = v["groups"]
+        by_group = {}
+        for it in v["items"]:
+            if it["group"] >= 0:
+                by_group.setdefault(int(it["group"]), []).append(it)
+            else:
+                assert it["part"] == -1
+        for gid, its in by_group.items():
+            gi = groups[gid]
+            assert gi["nsplit"] == len(its)
+            parts = sorted(int(i["part"]) for i in its)
+            assert parts == [int(gi["part0"]) + s * int(gi["rec_floats"]) for s in range(len(its))]
+            ranges = sorted((int(i["kt0"]), int(i["kt1"])) for i in its)
+            for (a0, a1), (b0, b1) in zip(ranges, ranges[1:]):
+                assert a1 == b0
+    # partial records of different groups never overlap
+    recs = []
+    for v in meta["views"]:
+        for gi in v["groups"]:
+            if gi["nsplit"]:
+                recs.append((int(gi["part0"]), int(gi["part0"]) + int(gi["nsplit"]) * int(gi["rec_floats"])))
+    recs = sorted(set(recs))
+    for (a0, a1), (b0, b1) in zip(recs, recs[1:]):
+        assert a1 <= b0
+
+
+def test_graph_mode_uses_full_grid():
+    w = workloads.c2()
+    _, meta, _ = _plan(w, graph=True)
+    assert meta["views"][2]["grid"] == 148
+
+
+def _err(fn):
+    with pytest.raises(fekv.FeError) as e:
+        fn()
+    return e.value.status
+
+
+def test_validation_matches_reference_error_classes():
+    hp = HostPlan(8, 2, 128, 16, 2, 4, True, 10, grid_cap=8)
+    # src/portable_gpu_ops.cpp:30 -- fewer keys than query rows
+    assert _err(lambda: hp.prepare([0, 5], [0, 1], [0], [3])) == _lib.FE_ERR_CONTEXT
+    # src/flashinfer_attention.cu:30 -- batch beyond the plan
+    assert _err(lambda: hp.prepare([0, 1, 2, 3], [0, 1, 2, 3], [0, 1, 2], [1, 1, 1])) == \
+        _lib.FE_ERR_CAPACITY
+    # page id out of [0, num_blocks]
+    assert _err(lambda: hp.prepare([0, 1], [0, 1], [11], [1])) == _lib.FE_ERR_INVALID_ARGUMENT
+    assert _err(lambda: hp.prepare([0, 1], [0, 1], [-1], [1])) == _lib.FE_ERR_INVALID_ARGUMENT
+    # last outside [1, page]
+    assert _err(lambda: hp.prepare([0, 1], [0, 1], [0], [17])) == _lib.FE_ERR_INVALID_ARGUMENT
+    assert _err(lambda: hp.prepare([0, 1], [0, 1], [0], [0])) == _lib.FE_ERR_INVALID_ARGUMENT
+    # more pages than max_pages
+    assert _err(lambda: hp.prepare([0, 1], [0, 5], [0, 1, 2, 3, 4], [1])) == _lib.FE_ERR_CAPACITY
+    # qo[batch] must equal rows
+    assert _err(lambda: hp.prepare([0, 1], [0, 1], [0], [1], rows=2)) == _lib.FE_ERR_INVALID_ARGUMENT
+    # the dummy page (num_blocks) is a valid page id (graph padding)
+    hp.prepare([0, 1], [0, 1], [10], [1])
+    # empty batch is a no-op
+    meta = hp.prepare([0], [0], [], [])
+    assert all(len(v["items"]) == 0 for v in meta["views"])
+
+
+def test_zero_row_sequences_are_skipped():
+    hp = HostPlan(8, 2, 128, 16, 3, 4, True, 10, grid_cap=8)
+    meta = hp.prepare([0, 0, 1, 1], [0, 1, 2, 3], [0, 1, 2], [5, 5, 5])
+    seqs = [int(it["seq"]) for v in meta["views"] for it in v["items"]]
+    assert set(seqs) == {1}
