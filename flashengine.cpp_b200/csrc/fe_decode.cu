@@ -368,3 +368,340 @@ int decode_launch(int dtype, int heads, const CUtensorMap& kmap, const CUtensorM
 }
 
 }  // namespace fe
+
+// ===========================================================================
+// Allocation-free decode entry point (fe_paged_decode_noalloc, fe_kv.h).
+//
+// For callers that cannot allocate device memory on their path: code running
+// under CUDA stream capture, hosts that hand all of HBM to their own pool
+// allocator (as a KV-cache engine sized by a memory-utilisation fraction
+// does), or latency-critical loops where cudaMalloc may block. The plan-based
+// entry points allocate their work lists and split-K workspace in
+// fe_attn_plan_create; this one needs neither: its work split is computed on
+// the device from the caller's metadata, and its split-K scratch is the
+// file-scope array below.
+//
+// The array is fixed at kNoAllocScratchBytes (16 MiB of fp32 split records +
+// 64 KiB of split counters) and exists on every GPU that loads this library
+// until the process exits. Every call shares it and it keeps the last call's
+// contents: the counters are cleared by each call (cudaMemsetAsync, no
+// allocation) and every record is written before it is read, so sequential
+// calls are safe, but calls that overlap on the GPU (other streams, other
+// host threads) race on it.
+// ===========================================================================
+namespace fe {
+namespace {
+
+constexpr size_t kNoAllocPartialBytes = size_t(16) << 20;
+constexpr int kNoAllocCounters = 16384;
+constexpr size_t kNoAllocScratchBytes =
+    kNoAllocPartialBytes + sizeof(int32_t) * size_t(kNoAllocCounters);
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+template <typename T, int H>
+__global__ void __launch_bounds__(kDecThreads, 1)
+    paged_decode_noalloc_kernel(const __grid_constant__ CUtensorMap kmap,
+                                const __grid_constant__ CUtensorMap vmap, const AttnArgs<T> a0,
+                                const int32_t* __restrict__ kv, const int32_t* __restrict__ pages,
+                                const int32_t* __restrict__ last, int groups_per_seq, int nsplit,
+                                int max_pages, int num_blocks, int rec_floats, int per_head_tma) {
+  using C = DecCfg<H>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ SplitGroup sg;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  float* comb = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* empty = full + C::kStages;
+  volatile int* flags = reinterpret_cast<volatile int*>(empty + C::kStages);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z, grp = blockIdx.y, s = blockIdx.x;
+  const int p0 = __ldg(kv + b), p1 = __ldg(kv + b + 1), ln = __ldg(last + b);
+  if (p1 <= p0 || p1 - p0 > max_pages || ln < 1 || ln > a0.page) {
+    if (threadIdx.x == 0 && s == 0 && grp == 0) raise_device_error(a0.err, FE_DEVERR_PAGE_RANGE);
+    return;
+  }
+  const int length = (p1 - p0 - 1) * a0.page + ln;
+  const int tiles = (length + kTileTokens - 1) / kTileTokens;
+  const int unit = b * groups_per_seq + grp;
+  WorkItem wi;
+  wi.seq = b;
+  wi.kvh = static_cast<int16_t>(grp * H);
+  wi.key_mode = 1;
+  wi.rb0 = 0;
+  wi.nrb = 1;
+  wi.kt0 = static_cast<int>(int64_t(tiles) * s / nsplit);
+  wi.kt1 = static_cast<int>(int64_t(tiles) * (s + 1) / nsplit);
+  wi.part = nsplit > 1 ? (unit * nsplit + s) * rec_floats : -1;
+  wi.group = nsplit > 1 ? 0 : -1;  // counters below are offset to this unit
+  SeqInfo si;
+  si.q_row0 = b;
+  si.qrows = 1;
+  si.length = length;
+  si.page_off = p0;
+  AttnArgs<T> a = a0;
+  a.counters = a0.counters + unit;
+
+  if (threadIdx.x == 0) {
+    sg.nsplit = nsplit;
+    sg.part0 = unit * nsplit * rec_floats;
+    sg.rec_floats = rec_floats;
+    sg.rows = H * a0.G;
+    for (int st = 0; st < C::kStages; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], kDecWarps);
+    }
+    flags[0] = 0;
+    flags[1] = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kDecWarps) {
+    if (lane == 0) {
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+    }
+    uint32_t g = 0;
+    bool ok = true;
+    const int hh0 = wi.kvh * 2;
+    for (int j0 = wi.kt0; j0 < wi.kt1 && ok; j0 += 32) {
+      const int n = min(32, wi.kt1 - j0);
+      int slot0 = 0;
+      if (lane < n) {
+        const int t0 = (j0 + lane) * kTileTokens;
+        int pid = __ldg(pages + p0 + t0 / a.page);
+        if (pid < 0 || pid > num_blocks) {
+          raise_device_error(a.err, FE_DEVERR_PAGE_RANGE);
+          pid = num_blocks;  // read the padding page instead
+        }
+        slot0 = pid * a.page + (t0 % a.page);
+      }
+      for (int jj = 0; jj < n; ++jj) {
+        const int s0 = __shfl_sync(0xffffffffu, slot0, jj);
+        const int st = g % C::kStages;
+        const uint32_t ph = (g / C::kStages) & 1u;
+        int good = 1;
+        if (lane == 0) {
+          if (flags[0] || !wait_bounded(&empty[st], ph ^ 1u, flags)) {
+            good = 0;
+          } else {
+            mbar_arrive_expect_tx(&full[st], C::kStageBytes);
+            uint8_t* dst = stages + st * C::kStageBytes;
+            if (!per_head_tma) {
+              tma_load_3d(dst, &kmap, &full[st], 0, s0, hh0);
+              tma_load_3d(dst + C::kKBytes, &vmap, &full[st], 0, s0, hh0);
+            } else {
+              for (int x = 0; x < 2 * H; ++x) {
+                tma_load_3d(dst + x * kHalfBytes, &kmap, &full[st], 0, hh0 + x, s0);
+                tma_load_3d(dst + C::kKBytes + x * kHalfBytes, &vmap, &full[st], 0, hh0 + x, s0);
+              }
+            }
+          }
+        }
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) {
+          ok = false;
+          break;
+        }
+        ++g;
+      }
+    }
+    if (!ok && lane == 0) {
+      raise_device_error(a.err, FE_DEVERR_TIMEOUT);
+      flags[0] = 1;
+      const uint32_t pending = g < C::kStages ? g : C::kStages;
+      for (uint32_t k = 1; k <= pending; ++k) {
+        const uint32_t gg = g - k;
+        volatile int never = 0;
+        (void)wait_bounded(&full[gg % C::kStages], (gg / C::kStages) & 1u, &never);
+      }
+    }
+    return;
+  }
+
+  uint32_t g = 0;
+  bool aborted = false;
+  if (a.G <= 8)
+    decode_item<T, H, 1>(a, wi, si, &sg, stages, full, empty, flags, comb, warp, lane, g, aborted);
+  else
+    decode_item<T, H, 2>(a, wi, si, &sg, stages, full, empty, flags, comb, warp, lane, g, aborted);
+  if (aborted && lane == 0) raise_device_error(a.err, FE_DEVERR_TIMEOUT);
+}
+
+using NoAllocEncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                     const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                     const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                     CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// Per-device set-up of the allocation-free path: the device address of the
+// scratch array (the host-side symbol is only a stand-in) and the kernels'
+// shared-memory attribute. Done by the first call on each device.
+struct NoAllocDevice {
+  unsigned char* scratch = nullptr;
+  bool attr_set[2][4] = {};
+  int sms = 0;
+};
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc_dev[64];
+
+template <typename T, int H>
+int noalloc_launch(NoAllocDevice& d, int ti, const CUtensorMap& km, const CUtensorMap& vm,
+                   const AttnArgs<T>& a, const int32_t* kv, const int32_t* pages,
+                   const int32_t* last, int batch, int groups, int nsplit, int max_pages,
+                   int num_blocks, int rec, bool per_head, cudaStream_t stream) {
+  using C = DecCfg<H>;
+  const int hi = H == 8 ? 3 : H == 4 ? 2 : H == 2 ? 1 : 0;
+  if (!d.attr_set[ti][hi]) {
+    FE_CUDA_TRY(cudaFuncSetAttribute(paged_decode_noalloc_kernel<T, H>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
+    d.attr_set[ti][hi] = true;
+  }
+  dim3 grid(nsplit, groups, batch);
+  paged_decode_noalloc_kernel<T, H><<<grid, kDecThreads, C::kSmem, stream>>>(
+      km, vm, a, kv, pages, last, groups, nsplit, max_pages, num_blocks, rec, per_head ? 1 : 0);
+  FE_CUDA_TRY(cudaGetLastError());
+  return FE_OK;
+}
+
+template <typename T>
+int noalloc_dispatch(NoAllocDevice& d, int ti, int H, const CUtensorMap& km,
+                     const CUtensorMap& vm, const AttnArgs<T>& a, const int32_t* kv,
+                     const int32_t* pages, const int32_t* last, int batch, int groups, int nsplit,
+                     int max_pages, int num_blocks, int rec, bool per_head, cudaStream_t s) {
+  switch (H) {
+    case 8: return noalloc_launch<T, 8>(d, ti, km, vm, a, kv, pages, last, batch, groups, nsplit,
+                                        max_pages, num_blocks, rec, per_head, s);
+    case 4: return noalloc_launch<T, 4>(d, ti, km, vm, a, kv, pages, last, batch, groups, nsplit,
+                                        max_pages, num_blocks, rec, per_head, s);
+    case 2: return noalloc_launch<T, 2>(d, ti, km, vm, a, kv, pages, last, batch, groups, nsplit,
+                                        max_pages, num_blocks, rec, per_head, s);
+    default: return noalloc_launch<T, 1>(d, ti, km, vm, a, kv, pages, last, batch, groups, nsplit,
+                                         max_pages, num_blocks, rec, per_head, s);
+  }
+}
+
+}  // namespace
+}  // namespace fe
+
+extern "C" int fe_paged_decode_noalloc(const void* q, const void* k_pool, const void* v_pool,
+                                       void* out, const int32_t* kv, const int32_t* pages,
+                                       const int32_t* last, int batch, int hq, int hkv, int page,
+                                       int num_blocks, int max_pages, int dtype, void* stream) {
+  using namespace fe;
+  if (dtype != FE_DTYPE_F16 && dtype != FE_DTYPE_BF16)
+    return fail(FE_ERR_INVALID_ARGUMENT, "fe_paged_decode_noalloc: bad dtype");
+  if (hq <= 0 || hkv <= 0 || hq % hkv != 0 || hq / hkv > kRowBlock)
+    return fail(FE_ERR_UNSUPPORTED, "fe_paged_decode_noalloc: need hq % hkv == 0, hq/hkv <= 16");
+  if (page <= 0 || page % kTileTokens != 0)
+    return fail(FE_ERR_UNSUPPORTED, "fe_paged_decode_noalloc: page must be a multiple of 16");
+  if (batch < 0 || num_blocks <= 0 || max_pages <= 0 || batch > 65535 ||
+      int64_t(num_blocks + 1) * page >= INT32_MAX)
+    return fail(FE_ERR_INVALID_ARGUMENT, "fe_paged_decode_noalloc: bad sizes");
+  if (batch == 0) return FE_OK;
+  if (!q || !k_pool || !v_pool || !out || !kv || !pages || !last)
+    return fail(FE_ERR_INVALID_ARGUMENT, "fe_paged_decode_noalloc: null pointer");
+  if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out))
+    return fail(FE_ERR_INVALID_ARGUMENT, "fe_paged_decode_noalloc: buffers must be 16-byte aligned");
+  const int G = hq / hkv;
+  int H = 8;
+  while (hkv % H) H >>= 1;
+  const int groups = hkv / H;
+  const int units = batch * groups;
+  const int rec = partial_rec_floats(H * G);
+  const size_t unit_bytes = sizeof(float) * size_t(rec);
+  if (size_t(units) * unit_bytes > kNoAllocPartialBytes || units > kNoAllocCounters) {
+    // a single split per unit would still fit; more than this cannot be served
+    if (units > kNoAllocCounters)
+      return fail(FE_ERR_CAPACITY, "fe_paged_decode_noalloc: batch x KV-head groups exceeds " +
+                                       std::to_string(kNoAllocCounters));
+  }
+
+  int dev = 0;
+  FE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(FE_ERR_NO_DEVICE, "fe_paged_decode_noalloc: device id");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  if (!d.scratch) {
+    int major = 0;
+    FE_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    if (major != 10)
+      return fail(FE_ERR_NO_DEVICE, "fe_paged_decode_noalloc: needs an sm_100 (B200) device");
+    FE_CUDA_TRY(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+    void* p = nullptr;
+    FE_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    d.scratch = static_cast<unsigned char*>(p);
+  }
+  float* partials = reinterpret_cast<float*>(d.scratch);
+  int32_t* counters = reinterpret_cast<int32_t*>(d.scratch + kNoAllocPartialBytes);
+
+  // Splits per (sequence, head group): enough CTAs for about two per SM,
+  // at least 8 key tiles each, and no more records than the scratch holds.
+  const int64_t max_tiles = (int64_t(max_pages) * page + kTileTokens - 1) / kTileTokens;
+  int nsplit = static_cast<int>((2 * int64_t(d.sms) + units - 1) / units);
+  nsplit = static_cast<int>(std::min<int64_t>(nsplit, std::max<int64_t>(1, max_tiles / 8)));
+  nsplit = static_cast<int>(std::min<size_t>(nsplit, kNoAllocPartialBytes / (size_t(units) * unit_bytes)));
+  if (nsplit > 65535) nsplit = 65535;
+  if (nsplit < 1) nsplit = 1;
+
+  auto s = static_cast<cudaStream_t>(stream);
+  if (nsplit > 1) FE_CUDA_TRY(cudaMemsetAsync(counters, 0, sizeof(int32_t) * units, s));
+
+  // Tensor maps (host-side encoding only).
+  static NoAllocEncodeFn encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr) !=
+            cudaSuccess ||
+        qr != cudaDriverEntryPointSuccess)
+      return fail(FE_ERR_CUDA, "fe_paged_decode_noalloc: cuTensorMapEncodeTiled unavailable");
+    encode = reinterpret_cast<NoAllocEncodeFn>(fn);
+  }
+  const cuuint64_t cache_slots = cuuint64_t(num_blocks + 1) * page;
+  const CUtensorMapDataType et =
+      dtype == FE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUtensorMap km, vm;
+  bool per_head = false;
+  {
+    const cuuint64_t dims[3] = {64, cache_slots, cuuint64_t(hkv) * 2};
+    const cuuint64_t strides[2] = {cuuint64_t(hkv) * 256, 128};
+    const cuuint32_t box[3] = {64, kTileTokens, cuuint32_t(2 * H)};
+    CUresult r1 = encode(&km, et, 3, const_cast<void*>(k_pool), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r2 = encode(&vm, et, 3, const_cast<void*>(v_pool), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    per_head = r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS;
+  }
+  if (per_head) {
+    const cuuint64_t dims[3] = {64, cuuint64_t(hkv) * 2, cache_slots};
+    const cuuint64_t strides[2] = {128, cuuint64_t(hkv) * 256};
+    const cuuint32_t box[3] = {64, 1, kTileTokens};
+    if (encode(&km, et, 3, const_cast<void*>(k_pool), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        encode(&vm, et, 3, const_cast<void*>(v_pool), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return fail(FE_ERR_CUDA, "fe_paged_decode_noalloc: tensor map encoding failed");
+  }
+
+  const float scale_log2 = 1.4426950408889634f / sqrtf(float(kHeadDim));
+  if (dtype == FE_DTYPE_BF16) {
+    AttnArgs<__nv_bfloat16> a{nullptr, static_cast<const __nv_bfloat16*>(q),
+                              static_cast<__nv_bfloat16*>(out), partials, counters,
+                              device_error_word(), hq, G, page, 1, scale_log2};
+    return noalloc_dispatch<__nv_bfloat16>(d, 1, H, km, vm, a, kv, pages, last, batch, groups,
+                                           nsplit, max_pages, num_blocks, rec, per_head, s);
+  }
+  AttnArgs<__half> a{nullptr, static_cast<const __half*>(q), static_cast<__half*>(out), partials,
+                     counters, device_error_word(), hq, G, page, 1, scale_log2};
+  return noalloc_dispatch<__half>(d, 0, H, km, vm, a, kv, pages, last, batch, groups, nsplit,
+                                  max_pages, num_blocks, rec, per_head, s);
+}

@@ -12,4 +12,5 @@ from . import metadata, workloads  # noqa: F401
 from ._lib import (FE_DTYPE_BF16, FE_DTYPE_F16, FeError, LIB_PATH, SHIM_PATH,  # noqa: F401
                    load)
 from .ops import (AttentionPlan, HostPlan, attention, clear_pages, copy_blocks,  # noqa: F401
-                  create_plan, destroy_plan, device_errors, gather, prepare_plan, store)
+                  create_plan, destroy_plan, device_errors, gather, paged_decode_noalloc,
+                  prepare_plan, store)

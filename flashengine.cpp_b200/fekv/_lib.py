@@ -52,6 +52,7 @@ SIGNATURES = {
     "fe_attn_plan_get_info": (_I, [_P, _P]),
     "fe_attn_plan_create_host": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
     "fe_attn_plan_debug_meta": (_I, [_P, _P, _I64, ctypes.POINTER(_I64)]),
+    "fe_paged_decode_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
 }
 
 

@@ -109,6 +109,19 @@ def gather(pool, out, kv, pages, last, row_offset, batch, max_len, page, width, 
                            _stream(stream)), "gather")
 
 
+def paged_decode_noalloc(q, k_pool, v_pool, out, kv, pages, last, batch, hq, hkv, page,
+                        num_blocks, max_pages, dtype=None, stream=None):
+    """Decode attention through fe_paged_decode_noalloc: no plan and no
+    device allocation (split-K scratch is a fixed array inside the library).
+    kv/pages/last are int32 DEVICE tensors; one query row per sequence."""
+    lib = _lib.load()
+    dtype = dtype_code(q) if dtype is None else int(dtype)
+    check(lib.fe_paged_decode_noalloc(_ptr(q), _ptr(k_pool), _ptr(v_pool), _ptr(out), _ptr(kv),
+                                      _ptr(pages), _ptr(last), int(batch), int(hq), int(hkv),
+                                      int(page), int(num_blocks), int(max_pages), dtype,
+                                      _stream(stream)), "paged_decode_noalloc")
+
+
 def device_errors(stream=None) -> int:
     """Read and clear the device-side error bits (FE_DEVERR_*)."""
     lib = _lib.load()
@@ -261,6 +274,6 @@ class HostPlan:
             pass
 
 
-__all__ = ["store", "copy_blocks", "clear_pages", "gather", "device_errors", "AttentionPlan",
+__all__ = ["store", "copy_blocks", "paged_decode_noalloc", "clear_pages", "gather", "device_errors", "AttentionPlan",
            "create_plan", "destroy_plan", "prepare_plan", "attention", "HostPlan", "FeError",
            "dtype_code", "ITEM_DTYPE", "GROUP_DTYPE", "SEQ_DTYPE"]

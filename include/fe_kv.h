@@ -149,6 +149,25 @@ int fe_attn_plan_prepare(fe_attn_plan* plan, const int32_t* qo, const int32_t* k
 int fe_attn_run(fe_attn_plan* plan, const void* q, const void* k_pool, const void* v_pool,
                 void* out, int causal, void* stream);
 
+/* Decode attention that allocates nothing. No counterpart in the reference:
+ * it is for callers that cannot call cudaMalloc on their path (code running
+ * under CUDA stream capture, hosts that give all device memory to their own
+ * pool allocator, latency-critical loops). Same arithmetic as fe_attn_run
+ * for one query row per sequence (row b of q/out belongs to sequence b), but
+ * no plan: kv, pages and last are DEVICE int32 arrays laid out as in
+ * fe_attn_plan_prepare, and the work split is derived on the device.
+ * Split-K scratch is a fixed 16 MiB (+64 KiB counters) array inside the
+ * library that every GPU loading it holds until exit; batch x KV-head groups
+ * beyond 16384 is rejected with FE_ERR_CAPACITY. The first call on a device
+ * resolves that array's device address and sets kernel attributes — make it
+ * before any stream capture. Calls share the array: sequential calls are
+ * safe, calls that overlap on the GPU race. Out-of-range page ids or last
+ * values are reported through fe_device_errors. */
+int fe_paged_decode_noalloc(const void* q, const void* k_pool, const void* v_pool, void* out,
+                            const int32_t* kv, const int32_t* pages, const int32_t* last,
+                            int batch, int hq, int hkv, int page, int num_blocks, int max_pages,
+                            int dtype, void* stream);
+
 /* Introspection of the last prepare (host-side numbers, no sync). */
 typedef struct fe_attn_plan_info {
   int batch, rows;
