@@ -38,6 +38,16 @@ METRIC = "paged decode-attn achieved TB/s (% HBM peak); decode tokens/s at 1/2/4
 FALLBACK_HBM_GBS = 6650.0
 
 
+def measured_peak_tflops():
+    """Sustained bf16 dense peak (a kernel timed inside a long step)."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops_sustained"]), "measured (sustained)"
+    except Exception:
+        return 1400.0, "fallback (sustained)"
+
+
 def measured_peak_gbs():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -155,13 +165,33 @@ def make_workload(config, rank, world, total_steps):
         return workloads.c2(seed=1000 + rank, steps=total_steps)
     if config == "c5":
         return workloads.c5(rank=rank, world=world, steps=total_steps)
+    if config == "c3":
+        return workloads.c3(seed=1000 + rank)
+    if config == "c4":
+        return workloads.c4(seed=1000 + rank)
     raise ValueError(config)
+
+
+def is_decode(config):
+    return config in ("c2", "c5")
+
+
+def attention_flops(w, md):
+    """Useful FLOPs of one attention launch: 4 * hq * head_dim per visible
+    (query row, key) pair (QK^T and PV), with the workload's mask."""
+    lengths = md.lengths(w.page).astype(np.int64)
+    q = (md.qo[1:] - md.qo[:-1]).astype(np.int64)
+    if w.causal:
+        pairs = q * (lengths - q + 1) + q * (q - 1) // 2
+    else:
+        pairs = q * lengths
+    return float(4 * w.hq * w.dim * int(pairs.sum()))
 
 
 class DecodeState:
     """Device-resident pools and per-layer step inputs for one GPU."""
 
-    def __init__(self, w, physical_layers, seed):
+    def __init__(self, w, physical_layers, seed, rows):
         import torch
 
         self.w = w
@@ -175,7 +205,6 @@ class DecodeState:
                 t = torch.empty(w.cache_slots, w.width, dtype=dt, device="cuda")
                 t.normal_(0.0, w.scale, generator=g)
                 lst.append(t)
-        rows = w.batch
         L = w.layers
         self.q = torch.randn(L, rows, w.hq, w.dim, generator=g, device="cuda", dtype=dt) * w.scale
         self.knew = torch.randn(L, rows, w.width, generator=g, device="cuda", dtype=dt) * w.scale
@@ -201,19 +230,31 @@ def run_ours(args, rank, world, local):
     free, _ = torch.cuda.mem_get_info()
     budget = min(free * 0.85, args.pool_gb * 1e9)
     physical = int(min(w.layers, max(1, budget // per_layer)))
-    st = DecodeState(w, physical, seed=7 + rank)
+    rows = w.metadata(0).rows
+    st = DecodeState(w, physical, seed=7 + rank, rows=rows)
     plan = fekv.AttentionPlan(w.hq, w.hkv, w.dim, w.page, w.batch, w.max_pages(total_steps),
                               w.bf16, w.num_blocks)
     stream = torch.cuda.current_stream()
+    decode = is_decode(args.config)
+    cow = None
+    if w.cow is not None:
+        cow = tuple(torch.from_numpy(np.asarray(x, np.int32)).cuda() for x in w.cow)
 
     attn_ev = []
 
     def step(s, record=False, host_io=None):
-        md = w.metadata(s)
+        md = w.metadata(s if decode else 0)
         if host_io is not None:
             host_io["h2d"]()
         plan.prepare(md.qo, md.kv, md.pages, md.last, md.batch, md.rows, False, stream)
         st.slots.copy_(torch.from_numpy(md.slots).pin_memory(), non_blocking=True)
+        if cow is not None:
+            # copy-on-write of the forked sequences' shared partial tail pages,
+            # every layer in one launch (idempotent, so it can repeat per step)
+            for l0 in range(0, st.physical, fekv._lib.FE_MAX_LAYERS):
+                l1 = min(st.physical, l0 + fekv._lib.FE_MAX_LAYERS)
+                fekv.copy_blocks(st.kpools[l0:l1], st.vpools[l0:l1], cow[0], cow[1], cow[2],
+                                 w.page, w.width, w.num_blocks + 1, None, stream)
         for layer in range(w.layers):
             p = layer % st.physical
             fekv.store(st.knew[layer], st.vnew[layer], st.kpools[p], st.vpools[p], st.slots,
@@ -222,7 +263,8 @@ def run_ours(args, rank, world, local):
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-            plan.attention(st.q[layer], st.kpools[p], st.vpools[p], st.out[layer], True, stream)
+            plan.attention(st.q[layer], st.kpools[p], st.vpools[p], st.out[layer], w.causal,
+                           stream)
             if record:
                 e1.record(stream)
                 attn_ev.append((e0, e1))
@@ -244,13 +286,14 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    kv_bytes = 0
     keys = 0
+    flops = 0.0
     t0.record(stream)
     for i in range(args.steps):
         md = step(args.warmup + i, record=True)
         lengths = md.lengths(w.page)
         keys += int(lengths.sum())
+        flops += attention_flops(w, md)
     t1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
@@ -258,10 +301,12 @@ def run_ours(args, rank, world, local):
     attn_ms = [a.elapsed_time(b) for a, b in attn_ev]
     barrier(world)
 
-    # algorithmic bytes of one decode-attention launch (averaged over steps)
-    per_launch_bytes = (keys / args.steps) * 2 * w.width * 2 + 2 * w.batch * w.hq * w.dim * 2
+    # algorithmic bytes / FLOPs of one attention launch (averaged over steps)
+    per_launch_bytes = (keys / args.steps) * 2 * w.width * 2 + 2 * rows * w.hq * w.dim * 2
+    per_launch_flops = flops / args.steps
     attn_avg_ms = float(np.mean(attn_ms))
     achieved_gbs = per_launch_bytes / (attn_avg_ms * 1e-3) / 1e9
+    achieved_tflops = per_launch_flops / (attn_avg_ms * 1e-3) / 1e12
 
     # end-to-end through the C ABI with host buffers: per step, H2D of every
     # layer's q/k/v from pinned memory and D2H of every layer's output.
@@ -292,15 +337,15 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
 
-    stats = gather_floats([ms, e2e_ms, attn_avg_ms, achieved_gbs, keys], world)
+    stats = gather_floats([ms, e2e_ms, attn_avg_ms, achieved_gbs, keys, achieved_tflops], world)
     plan.close()
     if rank != 0:
         return None
     ms_max = float(stats[:, 0].max())
     e2e_max = float(stats[:, 1].max())
-    tokens = w.batch * args.steps * world
+    tokens = rows * args.steps * world
     value = tokens / (ms_max * 1e-3)
-    e2e_value = w.batch * args.e2e_steps * world / (e2e_max * 1e-3)
+    e2e_value = rows * args.e2e_steps * world / (e2e_max * 1e-3)
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -343,6 +388,28 @@ def run_ours(args, rank, world, local):
         "gpu_launches": 2 * w.layers * args.steps,
         "clocks": clk,
     }
+    if not decode:
+        # prefill / verify workloads: the attention is a tensor-core contraction
+        tpeak, tkind = measured_peak_tflops()
+        line["metric"] = f"{w.name} paged attention TFLOP/s (tensor pipe) and query rows/s"
+        line["unit"] = "rows/s"
+        line["config"]["workload"] = (
+            f"{w.name}: hq{w.hq}/hkv{w.hkv}/d{w.dim} page{w.page}, {w.layers} layers, "
+            f"{w.batch} seqs, {rows} query rows per layer-step, "
+            f"{'causal' if w.causal else 'non-causal'}"
+            + (", copy-on-write of shared tail pages each step" if w.cow is not None else ""))
+        line["config"]["attention_flops_per_step"] = per_launch_flops * w.layers
+        line.pop("decode_attn_tbs")
+        line.pop("decode_attn_frac_of_peak")
+        line["roofline"] = {
+            "bound": "tensor", "achieved": round(float(stats[0, 5]), 2), "peak": tpeak,
+            "unit": "TFLOP/s", "frac": round(float(stats[0, 5]) / tpeak, 4), "peak_kind": tkind,
+            "kernel": "paged attention (tcgen05 prefill/verify + decode rows)",
+            "algorithmic_flops_per_launch": per_launch_flops,
+            "avg_launch_ms": round(float(stats[0, 2]), 5), "traffic": None,
+        }
+        line["gpu_launches"] = (2 + (1 if w.name == "C3" else 0)) * w.layers * args.steps + (
+            args.steps if w.cow is not None else 0)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w, args)
     return line
@@ -357,7 +424,7 @@ def _ref_layer_step(ref, w, md, pools, inputs):
     q, kn, vn = inputs
     ref.store(kn, vn, kp, vp, md.slots)
     ref.prepare(md.qo, md.kv, md.pages, md.last)
-    return ref.attention(q, kp, vp, True)
+    return ref.attention(q, kp, vp, w.causal)
 
 
 def cpu_reference_setup(w, steps):
@@ -369,9 +436,10 @@ def cpu_reference_setup(w, steps):
     rng = np.random.default_rng(5)
     kp = workloads.random_bits(rng, (w.cache_slots, w.width), w.bf16, w.scale)
     vp = workloads.random_bits(rng, (w.cache_slots, w.width), w.bf16, w.scale)
-    q = workloads.random_bits(rng, (w.batch, w.hq, w.dim), w.bf16, w.scale)
-    kn = workloads.random_bits(rng, (w.batch, w.width), w.bf16, w.scale)
-    vn = workloads.random_bits(rng, (w.batch, w.width), w.bf16, w.scale)
+    rows = w.metadata(0).rows
+    q = workloads.random_bits(rng, (rows, w.hq, w.dim), w.bf16, w.scale)
+    kn = workloads.random_bits(rng, (rows, w.width), w.bf16, w.scale)
+    vn = workloads.random_bits(rng, (rows, w.width), w.bf16, w.scale)
     ref = oracle.RefAten(w.hq, w.hkv, w.dim, w.page, w.batch, w.max_pages(steps), w.bf16,
                          w.num_blocks)
     return ref, (kp, vp), (q, kn, vn), oracle.ref_get_threads()
@@ -396,9 +464,11 @@ def cpu_baseline(w, args):
         times.append(time.perf_counter() - t)
     ref.close()
     layer_s = statistics.median(times)
-    return {"value": round(w.batch / (layer_s * w.layers), 3), "unit": "tokens/s",
+    rows = md.rows
+    return {"value": round(rows / (layer_s * w.layers), 3),
+            "unit": "tokens/s" if rows == w.batch else "rows/s",
             "cores": threads, "kind": "reference",
-            "sample": f"{len(times)} layer-steps of {w.name} ({w.batch} seqs: store + prepare_plan "
+            "sample": f"{len(times)} layer-steps of {w.name} ({w.batch} seqs, {rows} rows: store + prepare_plan "
                       f"+ attention), median {layer_s*1e3:.1f} ms/layer, scaled to {w.layers} layers",
             "cpu_model": _cpu_model()}
 
@@ -458,7 +528,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c2", "c5"], default="c2")
+    ap.add_argument("--config", choices=["c2", "c3", "c4", "c5"], default="c2")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--pool-gb", type=float, default=150.0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

@@ -30,6 +30,7 @@
 //  * Every mbarrier wait is bounded (2 s of %globaltimer); on expiry the CTA
 //    records FE_DEVERR_TIMEOUT, drains its own in-flight copies (bounded)
 //    and returns.
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -41,6 +42,8 @@ namespace fe {
 
 int decode_launch(int dtype, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
+int prefill_tc_launch(int dtype, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                      const void* args, int grid, cudaStream_t stream);
 
 namespace {
 
@@ -515,6 +518,7 @@ struct fe_attn_plan {
   const void* kmap_ptr = nullptr;
   const void* vmap_ptr = nullptr;
   bool per_head_tma = false;  // decode falls back to per-head-half boxes
+  bool row_tc = true;         // row-mode work on the tcgen05 kernel
 };
 
 namespace {
@@ -553,6 +557,12 @@ int gcd8(int hkv) {
   return h;
 }
 
+// Row-mode engine: tcgen05 (default) or the mma.sync kernel (FE_ROW_ENGINE=mma).
+bool row_engine_tc() {
+  const char* e = getenv("FE_ROW_ENGINE");
+  return !(e && std::string(e) == "mma");
+}
+
 PlanConfig make_config(int hq, int hkv, int dim, int page, int max_batch, int max_pages,
                        int num_blocks, int grid_cap, int dec_grid_cap) {
   PlanConfig c{};
@@ -566,6 +576,8 @@ PlanConfig make_config(int hq, int hkv, int dim, int page, int max_batch, int ma
   c.grid_cap = grid_cap;
   c.dec_grid_cap = dec_grid_cap;
   c.dec_heads = gcd8(hkv);
+  c.row_group_blocks = row_engine_tc() ? 8 : kConsumerWarps;
+  c.row_split = !row_engine_tc();
   int64_t items = int64_t(max_batch) * hkv * 64;
   if (items < 8192) items = 8192;
   if (items > (1 << 20)) items = 1 << 20;
@@ -612,7 +624,9 @@ int fe_attn_plan_create(int hq, int hkv, int dim, int page, int max_batch, int m
   if (rc != FE_OK) return rc;
   auto* p = new (std::nothrow) fe_attn_plan();
   if (!p) return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_plan_create: out of host memory");
-  p->cfg = make_config(hq, hkv, dim, page, max_batch, max_pages, num_blocks, sms * per_sm, sms);
+  p->row_tc = row_engine_tc();
+  p->cfg = make_config(hq, hkv, dim, page, max_batch, max_pages, num_blocks,
+                       p->row_tc ? sms : sms * per_sm, sms);
   p->dtype = dtype;
   p->device = dev;
   p->meta_cap = meta_capacity(p->cfg);
@@ -741,9 +755,15 @@ int fe_attn_run(fe_attn_plan* p, const void* q, const void* k_pool, const void* 
       int rc = decode_launch(p->dtype, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
       if (rc != FE_OK) return rc;
     }
-    if (grid_rows > 0)
-      paged_attn_kernel<__nv_bfloat16><<<grid_rows, kThreadsAttn, kSmemBytes, s>>>(p->kmap,
-                                                                                  p->vmap, a);
+    if (grid_rows > 0) {
+      if (p->row_tc) {
+        int rc = prefill_tc_launch(p->dtype, p->kmap, p->vmap, &a, grid_rows, s);
+        if (rc != FE_OK) return rc;
+      } else {
+        paged_attn_kernel<__nv_bfloat16><<<grid_rows, kThreadsAttn, kSmemBytes, s>>>(p->kmap,
+                                                                                    p->vmap, a);
+      }
+    }
   } else {
     AttnArgs<__half> a{p->d_meta, static_cast<const __half*>(q), static_cast<__half*>(out),
                        p->d_partials, p->d_counters, device_error_word(), p->cfg.hq, G,
@@ -752,8 +772,14 @@ int fe_attn_run(fe_attn_plan* p, const void* q, const void* k_pool, const void* 
       int rc = decode_launch(p->dtype, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
       if (rc != FE_OK) return rc;
     }
-    if (grid_rows > 0)
-      paged_attn_kernel<__half><<<grid_rows, kThreadsAttn, kSmemBytes, s>>>(p->kmap, p->vmap, a);
+    if (grid_rows > 0) {
+      if (p->row_tc) {
+        int rc = prefill_tc_launch(p->dtype, p->kmap, p->vmap, &a, grid_rows, s);
+        if (rc != FE_OK) return rc;
+      } else {
+        paged_attn_kernel<__half><<<grid_rows, kThreadsAttn, kSmemBytes, s>>>(p->kmap, p->vmap, a);
+      }
+    }
   }
   FE_CUDA_TRY(cudaGetLastError());
   return FE_OK;

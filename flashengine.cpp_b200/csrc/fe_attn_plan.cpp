@@ -292,8 +292,9 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
       for (int h = 0; h < cfg.hkv; h += H)
         key_units.push_back(Unit{b, h, 1, 0, 1, tiles_full, H * P});
     } else {
-      for (int rb0 = 0; rb0 < RB; rb0 += kConsumerWarps) {
-        const int nrb = std::min(kConsumerWarps, RB - rb0);
+      const int grp = cfg.row_group_blocks;
+      for (int rb0 = 0; rb0 < RB; rb0 += grp) {
+        const int nrb = std::min(grp, RB - rb0);
         const int last_row = std::min(P, (rb0 + nrb) * kRowBlock) - 1;
         const int rows_valid = last_row + 1 - rb0 * kRowBlock;
         const int64_t i_max = last_row / G;
@@ -310,9 +311,10 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
   // List 0: row work, non-causal; 1: row work, causal (identical key ranges
   // when there is no row work); 2: decode work.
   View views[3];
-  int rc = build_view(cfg, row_units_full, cfg.grid_cap, 4, 16, fixed_grid, views[0], err);
+  const int row_min_chunk = cfg.row_split ? 16 : (1 << 29);
+  int rc = build_view(cfg, row_units_full, cfg.grid_cap, 4, row_min_chunk, fixed_grid, views[0], err);
   if (rc != FE_OK) return rc;
-  rc = build_view(cfg, row_units_causal, cfg.grid_cap, 4, 16, fixed_grid, views[1], err);
+  rc = build_view(cfg, row_units_causal, cfg.grid_cap, 4, row_min_chunk, fixed_grid, views[1], err);
   if (rc != FE_OK) return rc;
   rc = build_cut_view(cfg, key_units, cfg.dec_grid_cap, 8, fixed_grid, views[2], err);
   if (rc != FE_OK) return rc;

@@ -72,6 +72,8 @@ struct PlanConfig {
   int grid_cap;               // persistent CTAs of the row kernel (SMs x CTAs per SM)
   int dec_grid_cap;           // persistent CTAs of the decode kernel (one per SM)
   int dec_heads;              // KV heads per decode item: gcd(hkv, 8)
+  int row_group_blocks;       // 16-row blocks per row-mode item (8 = one 128-row tcgen05 tile)
+  bool row_split;             // row-mode key ranges may be split across CTAs
   int max_items;              // work-item capacity
   int64_t partial_capacity;   // floats in the split-K workspace
   int max_groups;             // split-counter capacity
