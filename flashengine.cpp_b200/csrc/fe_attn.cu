@@ -430,20 +430,38 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-int encode_3d(CUtensorMap* map, const void* pool, int dtype, const cuuint64_t dims[3],
-              const cuuint64_t strides[2], const cuuint32_t box[3]) {
+int encode_nd(CUtensorMap* map, const void* pool, int dtype, int rank, const cuuint64_t* dims,
+              const cuuint64_t* strides, const cuuint32_t* box) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return fail(FE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
-  cuuint32_t estr[3] = {1, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(map,
                   dtype == FE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                  3, const_cast<void*>(pool), dims, strides, box, estr,
+                  rank, const_cast<void*>(pool), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(FE_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(r));
   return FE_OK;
+}
+
+int encode_3d(CUtensorMap* map, const void* pool, int dtype, const cuuint64_t dims[3],
+              const cuuint64_t strides[2], const cuuint32_t box[3]) {
+  return encode_nd(map, pool, dtype, 3, dims, strides, box);
+}
+
+// tcgen05 row kernel: pool viewed as [cache_slots/8][hkv*2][8][64] (slot
+// groups of 8, head-halves, slots within the group, 64 elements); box =
+// 2 groups x 2 head-halves x 8 slots x 64 elements, so one TMA copies both
+// halves of a 16-token piece of one KV head and lays it out as
+// [group][half][8 rows of 128 B]: 1 KiB swizzle atoms, 8-key groups 2 KiB
+// apart, the two head-halves 1 KiB apart.
+int encode_tc_map(CUtensorMap* map, const void* pool, int dtype, int hkv, int64_t cache_slots) {
+  const cuuint64_t dims[4] = {64, 8, cuuint64_t(hkv) * 2, cuuint64_t(cache_slots / 8)};
+  const cuuint64_t strides[3] = {cuuint64_t(hkv) * 256, 128, cuuint64_t(hkv) * 256 * 8};
+  const cuuint32_t box[4] = {64, 8, 2, 2};
+  return encode_nd(map, pool, dtype, 4, dims, strides, box);
 }
 
 // Row kernel: pool viewed as [cache_slots][hkv*2][64] (64-element head-half
@@ -514,7 +532,7 @@ struct fe_attn_plan {
   PlanResult last;
   int grid_view[3] = {0, 0, 0};
   // cached tensor maps (row kernel, decode kernel)
-  CUtensorMap kmap, vmap, kmap_dec, vmap_dec;
+  CUtensorMap kmap, vmap, kmap_dec, vmap_dec, kmap_tc, vmap_tc;
   const void* kmap_ptr = nullptr;
   const void* vmap_ptr = nullptr;
   bool per_head_tma = false;  // decode falls back to per-head-half boxes
@@ -733,6 +751,8 @@ int fe_attn_run(fe_attn_plan* p, const void* q, const void* k_pool, const void* 
     if (rc != FE_OK) return rc;
     if (encode_decode_map(&p->kmap_dec, k_pool, p->dtype, p->cfg.hkv, H, cache_slots) != FE_OK)
       p->per_head_tma = true;
+    rc = encode_tc_map(&p->kmap_tc, k_pool, p->dtype, p->cfg.hkv, cache_slots);
+    if (rc != FE_OK) return rc;
     p->kmap_ptr = k_pool;
   }
   if (v_pool != p->vmap_ptr) {
@@ -740,6 +760,8 @@ int fe_attn_run(fe_attn_plan* p, const void* q, const void* k_pool, const void* 
     if (rc != FE_OK) return rc;
     if (encode_decode_map(&p->vmap_dec, v_pool, p->dtype, p->cfg.hkv, H, cache_slots) != FE_OK)
       p->per_head_tma = true;
+    rc = encode_tc_map(&p->vmap_tc, v_pool, p->dtype, p->cfg.hkv, cache_slots);
+    if (rc != FE_OK) return rc;
     p->vmap_ptr = v_pool;
   }
   const float scale_log2 = 1.4426950408889634f / sqrtf(float(p->cfg.dim));
@@ -757,7 +779,7 @@ int fe_attn_run(fe_attn_plan* p, const void* q, const void* k_pool, const void* 
     }
     if (grid_rows > 0) {
       if (p->row_tc) {
-        int rc = prefill_tc_launch(p->dtype, p->kmap, p->vmap, &a, grid_rows, s);
+        int rc = prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, &a, grid_rows, s);
         if (rc != FE_OK) return rc;
       } else {
         paged_attn_kernel<__nv_bfloat16><<<grid_rows, kThreadsAttn, kSmemBytes, s>>>(p->kmap,
@@ -774,7 +796,7 @@ int fe_attn_run(fe_attn_plan* p, const void* q, const void* k_pool, const void* 
     }
     if (grid_rows > 0) {
       if (p->row_tc) {
-        int rc = prefill_tc_launch(p->dtype, p->kmap, p->vmap, &a, grid_rows, s);
+        int rc = prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, &a, grid_rows, s);
         if (rc != FE_OK) return rc;
       } else {
         paged_attn_kernel<__half><<<grid_rows, kThreadsAttn, kSmemBytes, s>>>(p->kmap, p->vmap, a);

@@ -38,9 +38,8 @@ __device__ __forceinline__ uint64_t global_ns() {
 // Bounded mbarrier wait. Returns false when the phase did not complete
 // within kWaitLimitNs, or when another warp of the CTA already gave up
 // (abort flag), so that every warp of the CTA winds down together.
-__device__ __noinline__ inline bool wait_bounded(uint64_t* bar, uint32_t parity,
-                                                 volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
+__device__ __noinline__ inline bool wait_bounded_slow(uint64_t* bar, uint32_t parity,
+                                                      volatile int* abort_flag) {
   const uint64_t t0 = global_ns();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -50,6 +49,12 @@ __device__ __noinline__ inline bool wait_bounded(uint64_t* bar, uint32_t parity,
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity,
+                                             volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return wait_bounded_slow(bar, parity, abort_flag);
 }
 
 template <typename T>

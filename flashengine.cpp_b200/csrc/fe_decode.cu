@@ -251,14 +251,18 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       const WorkItem w = items[it];
       const SeqInfo si = seqs[w.seq];
       const int hh0 = w.kvh * 2;
+      // Slots of 32 tiles are fetched per batch (one per lane); the next
+      // batch is requested before the current one is consumed.
+      auto tile_slot = [&](int j) -> int {
+        if (j >= w.kt1) return 0;
+        const int t0 = j * kTileTokens;
+        return __ldg(pages + si.page_off + t0 / a.page) * a.page + (t0 % a.page);
+      };
+      int nxt = tile_slot(w.kt0 + lane);
       for (int j0 = w.kt0; j0 < w.kt1 && ok; j0 += 32) {
         const int n = min(32, w.kt1 - j0);
-        int slot0 = 0;
-        if (lane < n) {
-          const int t0 = (j0 + lane) * kTileTokens;
-          const int pid = __ldg(pages + si.page_off + t0 / a.page);
-          slot0 = pid * a.page + (t0 % a.page);
-        }
+        const int slot0 = nxt;
+        nxt = tile_slot(j0 + 32 + lane);
         for (int jj = 0; jj < n; ++jj) {
           const int s0 = __shfl_sync(0xffffffffu, slot0, jj);
           const int s = g % C::kStages;
