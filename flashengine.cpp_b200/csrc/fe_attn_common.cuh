@@ -57,6 +57,27 @@ __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity,
   return wait_bounded_slow(bar, parity, abort_flag);
 }
 
+// The same bound with short try_waits (no suspend hint): for pipelines whose
+// hand-offs each have one or a few waiters on the critical path.
+__device__ __noinline__ inline bool wait_bounded_short_slow(uint64_t* bar, uint32_t parity,
+                                                            volatile int* abort_flag) {
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    if (mbar_try_wait_short(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ bool wait_bounded_short(uint64_t* bar, uint32_t parity,
+                                                   volatile int* abort_flag) {
+  if (mbar_try_wait_short(bar, parity)) return true;
+  return wait_bounded_short_slow(bar, parity, abort_flag);
+}
+
 template <typename T>
 __device__ __forceinline__ void store4(T* dst, float a, float b, float c, float d) {
   uint2 v;

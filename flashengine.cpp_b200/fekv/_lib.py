@@ -29,6 +29,7 @@ FE_DEVERR_SLOT_RANGE = 0x1
 FE_DEVERR_PAGE_RANGE = 0x2
 FE_DEVERR_NTOK_RANGE = 0x4
 FE_DEVERR_TIMEOUT = 0x8
+FE_DEVERR_SMEM_ALIGN = 0x10
 
 FE_MAX_LAYERS = 128
 

@@ -52,6 +52,7 @@ typedef enum fe_dtype { FE_DTYPE_F16 = 0, FE_DTYPE_BF16 = 1 } fe_dtype;
 #define FE_DEVERR_PAGE_RANGE 0x2u  /* copy/clear: page index out of range (copy skipped) */
 #define FE_DEVERR_NTOK_RANGE 0x4u  /* copy: ntok outside [0, page] (copy skipped) */
 #define FE_DEVERR_TIMEOUT 0x8u     /* attention: a pipeline wait exceeded its bound */
+#define FE_DEVERR_SMEM_ALIGN 0x10u /* attention: dynamic shared memory not 1 KiB aligned (launch skipped) */
 
 const char* fe_status_string(int status);
 const char* fe_last_error(void);
