@@ -1,35 +1,18 @@
-// Paged GQA attention for sm_100a: one persistent kernel serves decode
-// (one query row per sequence), speculative verify and chunked prefill.
+// Paged GQA attention for sm_100a: the plan object, its host planner hand-off
+// and the launch of the two kernels that serve one fe_attn_run call.
 //
-// Reference behaviour: Cambridgebit/FlashEngine.cpp src/flashinfer_attention.cu:35-44
-// (FlashInfer FA2 paged kernel, NHD pages, scale 1/sqrt(128), causal or no
-// mask) and its arithmetic oracle src/portable_gpu_ops.cpp:39-44 (fp32
-// softmax(q k^T / sqrt(d)) v with the bottom-right causal mask of :31).
+// Reference behaviour: Cambridgebit/FlashEngine.cpp src/flashinfer_attention.cu:22-44
+// (create_plan / prepare_plan / attention over NHD pages, scale 1/sqrt(128),
+// causal or no mask) with the arithmetic oracle src/portable_gpu_ops.cpp:27-44.
 //
-// Design (B200):
-//  * Work: the host planner (fe_attn_plan.cpp) cuts every (sequence, KV
-//    head, query-row group) into key-range items of whole 16-token tiles and
-//    hands each CTA a balanced list. Grid = SMs x resident CTAs.
-//  * Data movement: one producer warp streams K and V tiles (16 tokens x 128
-//    dims of one KV head, two 2 KiB TMA boxes each) from the paged pool into
-//    an 8-stage shared-memory ring with cp.async.bulk.tensor, completion on
-//    mbarriers; page ids are fetched 32 tiles at a time, one per lane.
-//  * Math: four consumer warps. Query rows are packed (query row, head of
-//    the GQA group) into 16-row blocks so one K/V tile serves the whole
-//    group. S = Q K^T and O += P V run on mma.m16n8k16 with fp32
-//    accumulation; P is split into a 16-bit high part and a 16-bit residual
-//    so P V keeps ~16 significant bits (fp32-softmax accuracy). Online softmax
-//    in base 2 with quad shuffles.
-//      key mode  (one row block, e.g. decode): warps take alternate key tiles
-//                 and merge (m, l, O) in shared memory.
-//      row mode  (prefill / long verify): each warp owns a row block and
-//                 walks every key tile of the item.
-//  * Split-K: items of a split unit write (O, m, l) partial records; the last
-//    CTA to finish (atomic ticket, no waiting) merges them and writes the
-//    output, then re-arms the counter, so a replayed CUDA graph needs no reset.
-//  * Every mbarrier wait is bounded (2 s of %globaltimer); on expiry the CTA
-//    records FE_DEVERR_TIMEOUT, drains its own in-flight copies (bounded)
-//    and returns.
+//  * fe_attn_plan_prepare: the host planner (fe_attn_plan.cpp) cuts every
+//    (sequence, KV head, query-row group) into key-range work items and
+//    balances them over the CTAs of each kernel; the metadata block is copied
+//    from pinned memory into a fixed device buffer (graph-replayable).
+//  * fe_attn_run: decode items (one query row per sequence) go to the
+//    split-K decode kernel (fe_decode.cu); multi-row items (chunked prefill,
+//    speculative verify) go to the tcgen05/TMEM kernel (fe_prefill_tc.cu).
+//    Tensor maps of the K and V pools are encoded once per pool address.
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -46,366 +29,6 @@ int prefill_tc_launch(int dtype, const CUtensorMap& kmap, const CUtensorMap& vma
                       const void* args, int grid, cudaStream_t stream);
 
 namespace {
-
-constexpr int kStages = 8;
-constexpr int kStageBytes = 4 * kHalfBytes;  // K lo, K hi, V lo, V hi of one head
-constexpr int kThreadsAttn = (kConsumerWarps + 1) * 32;
-constexpr int kCombBytes = kConsumerWarps * kRowBlock * kCombStride * 4;
-constexpr int kBarBytes = 2 * kStages * 8 + 16;
-constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCombBytes + kBarBytes;
-
-struct ConsumerCtx {
-  uint8_t* stages;
-  uint64_t* full;
-  uint64_t* empty;
-  volatile int* flags;
-  float* comb;
-  int w, lane;
-  bool causal;
-};
-
-// Wait for a tile's full barrier; false once the CTA has given up.
-__device__ __forceinline__ bool acquire_tile(const ConsumerCtx& cx, uint32_t gg, bool& aborted) {
-  if (aborted) return false;
-  const int s = gg % kStages;
-  if (cx.flags[0] || !wait_bounded(&cx.full[s], (gg / kStages) & 1u, cx.flags)) aborted = true;
-  return !aborted;
-}
-
-// Row mode: warp w owns packed-row block rb0 + w (if any) and walks every key
-// tile of the item. S = Q K^T with the rows on the mma M side. Each active
-// warp releases a stage with one arrival; warp 0 also arrives for the
-// warps that have no block, so every stage still completes with four.
-template <typename T>
-__device__ __forceinline__ void row_item(const AttnArgs<T>& a, const WorkItem& wi,
-                                         const SeqInfo& si, const ConsumerCtx& cx, uint32_t& g,
-                                         bool& aborted) {
-  const int lane = cx.lane, w = cx.w;
-  const int ntiles = wi.kt1 - wi.kt0;
-  if (w >= wi.nrb) {
-    g += ntiles;
-    return;
-  }
-  const int r_lo = lane >> 2, cq = lane & 3, mi = lane >> 3, li = lane & 7;
-  const int G = a.G;
-  const int P = si.qrows * G;
-  const int my_rb = wi.rb0 + w;
-  const int p_lo = my_rb * kRowBlock + r_lo, p_hi = p_lo + 8;
-  const uint32_t arrivals = w == 0 ? 1u + kConsumerWarps - wi.nrb : 1u;
-
-  uint32_t qa[8][4];
-  {
-    const T* q_lo = nullptr;
-    const T* q_hi = nullptr;
-    if (p_lo < P)
-      q_lo = a.q + (static_cast<int64_t>(si.q_row0 + p_lo / G) * a.hq + wi.kvh * G + p_lo % G) *
-                       kHeadDim;
-    if (p_hi < P)
-      q_hi = a.q + (static_cast<int64_t>(si.q_row0 + p_hi / G) * a.hq + wi.kvh * G + p_hi % G) *
-                       kHeadDim;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const int col = kk * 16 + 2 * cq;
-      qa[kk][0] = q_lo ? ldg32(q_lo + col) : 0u;
-      qa[kk][1] = q_hi ? ldg32(q_hi + col) : 0u;
-      qa[kk][2] = q_lo ? ldg32(q_lo + col + 8) : 0u;
-      qa[kk][3] = q_hi ? ldg32(q_hi + col + 8) : 0u;
-    }
-  }
-  const int lim_lo = (cx.causal && p_lo < P) ? si.length - si.qrows + p_lo / G + 1 : si.length;
-  const int lim_hi = (cx.causal && p_hi < P) ? si.length - si.qrows + p_hi / G + 1 : si.length;
-  const int lim_min = min(lim_lo, lim_hi);
-
-  float m_r[2] = {-INFINITY, -INFINITY};
-  float l_r[2] = {0.f, 0.f};
-  float o[16][4];
-#pragma unroll
-  for (int dn = 0; dn < 16; ++dn) o[dn][0] = o[dn][1] = o[dn][2] = o[dn][3] = 0.f;
-
-  for (int jt = 0; jt < ntiles; ++jt) {
-    const uint32_t gg = g + jt;
-    if (!acquire_tile(cx, gg, aborted)) break;
-    const int s = gg % kStages;
-    const uint32_t kb0 = smem_u32(cx.stages + s * kStageBytes);
-    const uint32_t kb1 = kb0 + kHalfBytes, vb0 = kb0 + 2 * kHalfBytes, vb1 = kb0 + 3 * kHalfBytes;
-    const int tbase = (wi.kt0 + jt) * kTileTokens;
-
-    // ---- S = Q K^T (16 packed rows x 16 tokens)
-    float sc[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-#pragma unroll
-      for (int sp = 0; sp < 2; ++sp) {
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const int tok = nt * 8 + li;
-          const int c = sp * 4 + mi;
-          const uint32_t addr = (h ? kb1 : kb0) + tok * 128 + ((c ^ li) << 4);
-          uint32_t b0, b1, b2, b3;
-          ldmatrix_x4(addr, b0, b1, b2, b3);
-          const int kk = h * 4 + sp * 2;
-          mma_16816<T>(sc[nt], qa[kk], b0, b1);
-          mma_16816<T>(sc[nt], qa[kk + 1], b2, b3);
-        }
-      }
-    }
-    if (tbase + kTileTokens > lim_min) {
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int t = tbase + nt * 8 + 2 * cq + e;
-          if (t >= lim_lo) sc[nt][e] = -INFINITY;
-          if (t >= lim_hi) sc[nt][2 + e] = -INFINITY;
-        }
-    }
-    float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
-    float mx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float mn0 = fmaxf(m_r[0], mx0 * a.scale_log2);
-    const float mn1 = fmaxf(m_r[1], mx1 * a.scale_log2);
-    const float base0 = mn0 == -INFINITY ? 0.f : mn0;
-    const float base1 = mn1 == -INFINITY ? 0.f : mn1;
-    const float al0 = fast_exp2(m_r[0] - base0), al1 = fast_exp2(m_r[1] - base1);
-    m_r[0] = mn0;
-    m_r[1] = mn1;
-    float p[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      p[nt][0] = fast_exp2(fmaf(sc[nt][0], a.scale_log2, -base0));
-      p[nt][1] = fast_exp2(fmaf(sc[nt][1], a.scale_log2, -base0));
-      p[nt][2] = fast_exp2(fmaf(sc[nt][2], a.scale_log2, -base1));
-      p[nt][3] = fast_exp2(fmaf(sc[nt][3], a.scale_log2, -base1));
-    }
-    l_r[0] = l_r[0] * al0 + (p[0][0] + p[0][1]) + (p[1][0] + p[1][1]);
-    l_r[1] = l_r[1] * al1 + (p[0][2] + p[0][3]) + (p[1][2] + p[1][3]);
-#pragma unroll
-    for (int dn = 0; dn < 16; ++dn) {
-      o[dn][0] *= al0;
-      o[dn][1] *= al0;
-      o[dn][2] *= al1;
-      o[dn][3] *= al1;
-    }
-    uint32_t phi[4], plo[4];
-    {
-      const float pv[4][2] = {{p[0][0], p[0][1]}, {p[0][2], p[0][3]},
-                              {p[1][0], p[1][1]}, {p[1][2], p[1][3]}};
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        phi[r] = pack2<T>(pv[r][0], pv[r][1]);
-        const float2 f = unpack2<T>(phi[r]);
-        plo[r] = pack2<T>(pv[r][0] - f.x, pv[r][1] - f.y);
-      }
-    }
-    uint32_t vm0 = 0xffffffffu, vm1 = 0xffffffffu;
-    if (tbase + kTileTokens > si.length) {
-      const int ta = tbase + 2 * cq;
-      vm0 = (ta < si.length ? 0x0000ffffu : 0u) | (ta + 1 < si.length ? 0xffff0000u : 0u);
-      vm1 = (ta + 8 < si.length ? 0x0000ffffu : 0u) | (ta + 9 < si.length ? 0xffff0000u : 0u);
-    }
-#pragma unroll
-    for (int qd = 0; qd < 8; ++qd) {
-      const int tok = (mi & 1) * 8 + li;
-      const int c = 2 * qd + (mi >> 1);
-      const uint32_t addr = ((c >> 3) ? vb1 : vb0) + tok * 128 + (((c & 7) ^ li) << 4);
-      uint32_t r0, r1, r2, r3;
-      ldmatrix_x4_trans(addr, r0, r1, r2, r3);
-      r0 &= vm0;
-      r1 &= vm1;
-      r2 &= vm0;
-      r3 &= vm1;
-      mma_16816<T>(o[2 * qd], phi, r0, r1);
-      mma_16816<T>(o[2 * qd], plo, r0, r1);
-      mma_16816<T>(o[2 * qd + 1], phi, r2, r3);
-      mma_16816<T>(o[2 * qd + 1], plo, r2, r3);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive_cnt(&cx.empty[s], arrivals);
-  }
-  g += ntiles;
-
-  l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 1);
-  l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 2);
-  l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 1);
-  l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 2);
-  float* cw = cx.comb + w * kRowBlock * kCombStride;
-#pragma unroll
-  for (int dn = 0; dn < 16; ++dn) {
-    *reinterpret_cast<float2*>(cw + r_lo * kCombStride + dn * 8 + 2 * cq) =
-        make_float2(o[dn][0], o[dn][1]);
-    *reinterpret_cast<float2*>(cw + (r_lo + 8) * kCombStride + dn * 8 + 2 * cq) =
-        make_float2(o[dn][2], o[dn][3]);
-  }
-  if (cq == 0) {
-    cw[r_lo * kCombStride + kHeadDim] = m_r[0];
-    cw[r_lo * kCombStride + kHeadDim + 1] = l_r[0];
-    cw[(r_lo + 8) * kCombStride + kHeadDim] = m_r[1];
-    cw[(r_lo + 8) * kCombStride + kHeadDim + 1] = l_r[1];
-  }
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kThreadsAttn, 2)
-    paged_attn_kernel(const __grid_constant__ CUtensorMap kmap,
-                      const __grid_constant__ CUtensorMap vmap, const AttnArgs<T> a) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
-  uint8_t* stages = smem;
-  float* comb = reinterpret_cast<float*>(smem + kStages * kStageBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kCombBytes);
-  uint64_t* empty = full + kStages;
-  volatile int* flags = reinterpret_cast<volatile int*>(empty + kStages);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const MetaHeader* hdr = reinterpret_cast<const MetaHeader*>(a.meta);
-  const int view = a.view;
-  if (static_cast<int>(blockIdx.x) >= hdr->grid[view]) return;
-  const int32_t* cta_off = reinterpret_cast<const int32_t*>(a.meta + hdr->cta_off_off[view]);
-  const WorkItem* items = reinterpret_cast<const WorkItem*>(a.meta + hdr->items_off[view]);
-  const SplitGroup* groups = reinterpret_cast<const SplitGroup*>(a.meta + hdr->groups_off[view]);
-  const SeqInfo* seqs = reinterpret_cast<const SeqInfo*>(a.meta + hdr->seqs_off);
-  const int32_t* pages = reinterpret_cast<const int32_t*>(a.meta + hdr->pages_off);
-  const int it0 = cta_off[blockIdx.x], it1 = cta_off[blockIdx.x + 1];
-  if (it0 >= it1) return;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
-    }
-    flags[0] = 0;
-    flags[1] = 0;
-    fence_barrier_init();
-  }
-  __syncthreads();
-
-  if (warp == kConsumerWarps) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      prefetch_tensormap(&kmap);
-      prefetch_tensormap(&vmap);
-    }
-    uint32_t g = 0;
-    bool ok = true;
-    for (int it = it0; it < it1 && ok; ++it) {
-      const WorkItem w = items[it];
-      const SeqInfo si = seqs[w.seq];
-      const int h2 = w.kvh * 2;
-      for (int j0 = w.kt0; j0 < w.kt1 && ok; j0 += 32) {
-        const int n = min(32, w.kt1 - j0);
-        int slot0 = 0;
-        if (lane < n) {
-          const int t0 = (j0 + lane) * kTileTokens;
-          const int pid = __ldg(pages + si.page_off + t0 / a.page);
-          slot0 = pid * a.page + (t0 % a.page);
-        }
-        for (int jj = 0; jj < n; ++jj) {
-          const int s0 = __shfl_sync(0xffffffffu, slot0, jj);
-          const int s = g % kStages;
-          const uint32_t ph = (g / kStages) & 1u;
-          int good = 1;
-          if (lane == 0) {
-            if (flags[0] || !wait_bounded(&empty[s], ph ^ 1u, flags)) {
-              good = 0;
-            } else {
-              mbar_arrive_expect_tx(&full[s], kStageBytes);
-              uint8_t* st = stages + s * kStageBytes;
-              tma_load_3d(st, &kmap, &full[s], 0, h2, s0);
-              tma_load_3d(st + kHalfBytes, &kmap, &full[s], 0, h2 + 1, s0);
-              tma_load_3d(st + 2 * kHalfBytes, &vmap, &full[s], 0, h2, s0);
-              tma_load_3d(st + 3 * kHalfBytes, &vmap, &full[s], 0, h2 + 1, s0);
-            }
-          }
-          good = __shfl_sync(0xffffffffu, good, 0);
-          if (!good) {
-            ok = false;
-            break;
-          }
-          ++g;
-        }
-      }
-    }
-    if (!ok && lane == 0) {
-      raise_device_error(a.err, FE_DEVERR_TIMEOUT);
-      flags[0] = 1;
-      // Drain: wait (bounded) for the copies this CTA issued into its own
-      // shared memory before the CTA exits.
-      const uint32_t pending = g < kStages ? g : kStages;
-      for (uint32_t k = 1; k <= pending; ++k) {
-        const uint32_t gg = g - k;
-        volatile int never = 0;
-        (void)wait_bounded(&full[gg % kStages], (gg / kStages) & 1u, &never);
-      }
-    }
-    return;
-  }
-
-  // -------------------------------------------------------------- consumers
-  const int tid = threadIdx.x;  // 0..127
-  const int G = a.G;
-  ConsumerCtx cx{stages, full, empty, flags, comb, warp, lane, view == 1};
-  uint32_t g = 0;
-  bool aborted = false;
-
-  for (int it = it0; it < it1; ++it) {
-    const WorkItem wi = items[it];
-    const SeqInfo si = seqs[wi.seq];
-    const int P = si.qrows * G;
-    row_item<T>(a, wi, si, cx, g, aborted);
-    named_barrier_sync(1, kConsumerWarps * 32);
-
-    const int nrows = min(wi.nrb * kRowBlock, P - wi.rb0 * kRowBlock);
-    const int d4 = (tid & 31) * 4;
-    for (int r = tid >> 5; r < nrows; r += kConsumerWarps) {
-      const float* row = comb + r * kCombStride;  // warp r/16, row r%16: contiguous
-      const float M = row[kHeadDim], L = row[kHeadDim + 1];
-      const float4 acc = *reinterpret_cast<const float4*>(row + d4);
-      const int pr = wi.rb0 * kRowBlock + r;
-      if (wi.group < 0) {
-        const float inv = 1.f / L;
-        T* dst = a.out + (static_cast<int64_t>(si.q_row0 + pr / G) * a.hq + wi.kvh * G + pr % G) *
-                             kHeadDim + d4;
-        store4<T>(dst, acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-      } else {
-        float* rec = a.partials + wi.part;
-        *reinterpret_cast<float4*>(rec + r * kHeadDim + d4) = acc;
-        if ((tid & 31) == 0) {
-          rec[nrows * kHeadDim + r] = M;
-          rec[nrows * (kHeadDim + 1) + r] = L;
-        }
-      }
-    }
-
-    if (wi.group >= 0) {
-      __threadfence();
-      named_barrier_sync(1, kConsumerWarps * 32);
-      if (tid == 0) {
-        const int nsplit = groups[wi.group].nsplit;
-        const int prev = atomicAdd(a.counters + wi.group, 1);
-        flags[1] = prev == nsplit - 1 ? 1 : 0;
-      }
-      named_barrier_sync(1, kConsumerWarps * 32);
-      if (flags[1]) {
-        __threadfence();
-        const SplitGroup gi = groups[wi.group];
-        merge_partials<T>(a.partials, gi, tid, kConsumerWarps * 32, [&](int r) {
-          const int pr = wi.rb0 * kRowBlock + r;
-          return a.out +
-                 (static_cast<int64_t>(si.q_row0 + pr / G) * a.hq + wi.kvh * G + pr % G) * kHeadDim;
-        });
-        if (tid == 0) a.counters[wi.group] = 0;
-      }
-    }
-    named_barrier_sync(1, kConsumerWarps * 32);
-  }
-  if (aborted && lane == 0) raise_device_error(a.err, FE_DEVERR_TIMEOUT);
-}
 
 // ---------------------------------------------------------------------------
 // host side
@@ -485,26 +108,6 @@ int encode_decode_map(CUtensorMap* map, const void* pool, int dtype, int hkv, in
   return encode_3d(map, pool, dtype, dims, strides, box);
 }
 
-template <typename T>
-int kernel_setup(int* ctas_per_sm) {
-  static int cached = -1;
-  static cudaError_t err = cudaSuccess;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    err = cudaFuncSetAttribute(paged_attn_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kSmemBytes);
-    if (err == cudaSuccess) {
-      int n = 0;
-      err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, paged_attn_kernel<T>, kThreadsAttn,
-                                                          kSmemBytes);
-      cached = n;
-    }
-  });
-  if (err != cudaSuccess) return cuda_fail(err, "paged_attn_kernel setup");
-  *ctas_per_sm = cached > 0 ? cached : 1;
-  return FE_OK;
-}
-
 }  // namespace
 }  // namespace fe
 
@@ -536,7 +139,6 @@ struct fe_attn_plan {
   const void* kmap_ptr = nullptr;
   const void* vmap_ptr = nullptr;
   bool per_head_tma = false;  // decode falls back to per-head-half boxes
-  bool row_tc = true;         // row-mode work on the tcgen05 kernel
 };
 
 namespace {
@@ -575,12 +177,6 @@ int gcd8(int hkv) {
   return h;
 }
 
-// Row-mode engine: tcgen05 (default) or the mma.sync kernel (FE_ROW_ENGINE=mma).
-bool row_engine_tc() {
-  const char* e = getenv("FE_ROW_ENGINE");
-  return !(e && std::string(e) == "mma");
-}
-
 PlanConfig make_config(int hq, int hkv, int dim, int page, int max_batch, int max_pages,
                        int num_blocks, int grid_cap, int dec_grid_cap) {
   PlanConfig c{};
@@ -594,8 +190,8 @@ PlanConfig make_config(int hq, int hkv, int dim, int page, int max_batch, int ma
   c.grid_cap = grid_cap;
   c.dec_grid_cap = dec_grid_cap;
   c.dec_heads = gcd8(hkv);
-  c.row_group_blocks = row_engine_tc() ? 8 : kConsumerWarps;
-  c.row_split = !row_engine_tc();
+  c.row_group_blocks = 8;  // 128 packed rows per tcgen05 work item
+  c.row_split = false;      // the tcgen05 kernel walks an item's whole key range
   int64_t items = int64_t(max_batch) * hkv * 64;
   if (items < 8192) items = 8192;
   if (items > (1 << 20)) items = 1 << 20;
@@ -637,14 +233,9 @@ int fe_attn_plan_create(int hq, int hkv, int dim, int page, int max_batch, int m
   FE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   if (major != 10)
     return fail(FE_ERR_NO_DEVICE, "fe_attn_plan_create: needs an sm_100 (B200) device");
-  int per_sm = 1;
-  rc = dtype == FE_DTYPE_BF16 ? kernel_setup<__nv_bfloat16>(&per_sm) : kernel_setup<__half>(&per_sm);
-  if (rc != FE_OK) return rc;
   auto* p = new (std::nothrow) fe_attn_plan();
   if (!p) return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_plan_create: out of host memory");
-  p->row_tc = row_engine_tc();
-  p->cfg = make_config(hq, hkv, dim, page, max_batch, max_pages, num_blocks,
-                       p->row_tc ? sms : sms * per_sm, sms);
+  p->cfg = make_config(hq, hkv, dim, page, max_batch, max_pages, num_blocks, sms, sms);
   p->dtype = dtype;
   p->device = dev;
   p->meta_cap = meta_capacity(p->cfg);
@@ -778,13 +369,8 @@ int fe_attn_run(fe_attn_plan* p, const void* q, const void* k_pool, const void* 
       if (rc != FE_OK) return rc;
     }
     if (grid_rows > 0) {
-      if (p->row_tc) {
-        int rc = prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, &a, grid_rows, s);
-        if (rc != FE_OK) return rc;
-      } else {
-        paged_attn_kernel<__nv_bfloat16><<<grid_rows, kThreadsAttn, kSmemBytes, s>>>(p->kmap,
-                                                                                    p->vmap, a);
-      }
+      int rc = prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, &a, grid_rows, s);
+      if (rc != FE_OK) return rc;
     }
   } else {
     AttnArgs<__half> a{p->d_meta, static_cast<const __half*>(q), static_cast<__half*>(out),
@@ -795,12 +381,8 @@ int fe_attn_run(fe_attn_plan* p, const void* q, const void* k_pool, const void* 
       if (rc != FE_OK) return rc;
     }
     if (grid_rows > 0) {
-      if (p->row_tc) {
-        int rc = prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, &a, grid_rows, s);
-        if (rc != FE_OK) return rc;
-      } else {
-        paged_attn_kernel<__half><<<grid_rows, kThreadsAttn, kSmemBytes, s>>>(p->kmap, p->vmap, a);
-      }
+      int rc = prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, &a, grid_rows, s);
+      if (rc != FE_OK) return rc;
     }
   }
   FE_CUDA_TRY(cudaGetLastError());

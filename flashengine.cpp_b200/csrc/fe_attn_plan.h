@@ -20,7 +20,6 @@ namespace fe {
 constexpr int kHeadDim = 128;
 constexpr int kTileTokens = 16;   // key tokens per tile (one TMA box per K/V half)
 constexpr int kRowBlock = 16;     // packed query rows per mma row block
-constexpr int kConsumerWarps = 4; // row blocks per row-mode item / key-tile lanes in key mode
 
 struct SeqInfo {  // 16 bytes
   int32_t q_row0;    // first query row (qo[b])
