@@ -142,16 +142,9 @@ def barrier(world):
 
 def gather_floats(values, world):
     """All-gather a small float64 vector per rank (after timing only)."""
-    import torch
+    from fekv.dist import gather_floats as _gather
 
-    t = torch.tensor(values, dtype=torch.float64, device="cuda")
-    if world == 1:
-        return t.unsqueeze(0).cpu().numpy()
-    import torch.distributed as dist
-
-    out = [torch.empty_like(t) for _ in range(world)]
-    dist.all_gather(out, t)
-    return torch.stack(out).cpu().numpy()
+    return _gather(values, world, device="cuda")
 
 
 # ---------------------------------------------------------------------------
@@ -218,6 +211,7 @@ def run_ours(args, rank, world, local):
     import torch
 
     import fekv
+    from fekv.dist import job_rate
 
     fekv.load()
     peak, peak_kind = measured_peak_gbs()
@@ -343,9 +337,8 @@ def run_ours(args, rank, world, local):
         return None
     ms_max = float(stats[:, 0].max())
     e2e_max = float(stats[:, 1].max())
-    tokens = rows * args.steps * world
-    value = tokens / (ms_max * 1e-3)
-    e2e_value = rows * args.e2e_steps * world / (e2e_max * 1e-3)
+    value = job_rate([rows * args.steps] * world, stats[:, 0])
+    e2e_value = job_rate([rows * args.e2e_steps] * world, stats[:, 1])
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -377,7 +370,7 @@ def run_ours(args, rank, world, local):
             "unit": "GB/s",
             "frac": round(float(stats[0, 3]) / peak, 4),
             "peak_kind": peak_kind,
-            "kernel": "paged_attn_kernel (decode)",
+            "kernel": "paged_decode_kernel",
             "algorithmic_bytes_per_launch": float(per_launch_bytes),
             "avg_launch_ms": round(float(stats[0, 2]), 5),
             "traffic": None,

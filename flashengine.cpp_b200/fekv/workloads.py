@@ -198,8 +198,11 @@ def c5_contexts(seed: int = 0, total: int = 1024, median: float = 8192.0, sigma:
 
 
 def c5(rank: int = 0, world: int = 1, seed: int = 0, steps: int = 32, per_gpu: int = 128):
+    from .dist import shard_range
+
     ctx_all = c5_contexts(seed, per_gpu * max(world, 8))
-    ctx = ctx_all[rank * per_gpu:(rank + 1) * per_gpu]
+    own = shard_range(rank, per_gpu)
+    ctx = ctx_all[own.start:own.stop]
     w = decode_workload("C5", 64, 8, ctx, True, seed + 1000 + rank, steps=steps, scale=0.5,
                         layers=64)
     w.notes["sigma"] = 0.5
