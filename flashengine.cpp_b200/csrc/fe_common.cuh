@@ -112,8 +112,8 @@ __device__ __forceinline__ bool mbar_try_wait_short(uint64_t* bar, uint32_t pari
   return ok != 0;
 }
 
-// 3-D tiled TMA load global -> shared (this CTA's own shared memory; no
-// multicast), completion signalled on `bar` via complete_tx.
+// 3-D tiled TMA load global -> shared (this CTA's own shared memory only),
+// completion signalled on `bar` via complete_tx.
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2) {
   asm volatile(

@@ -77,8 +77,8 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       : "memory");
 }
 
-// Arrive once on `bar` when every tcgen05 operation this thread issued so far
-// has completed (no multicast).
+// Arrive once on `bar` (this CTA's own barrier) when every tcgen05 operation
+// this thread issued so far has completed.
 __device__ __forceinline__ void commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_u32(bar))
