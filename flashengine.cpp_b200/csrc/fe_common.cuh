@@ -15,6 +15,8 @@
 
 namespace fe {
 
+inline bool valid_dtype(int dtype) { return dtype == FE_DTYPE_F16 || dtype == FE_DTYPE_BF16; }
+
 // ---- host-side error reporting ------------------------------------------
 
 void set_error(const std::string& msg);

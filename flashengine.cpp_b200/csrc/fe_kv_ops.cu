@@ -196,7 +196,6 @@ int sm_count() {
   return cached;
 }
 
-bool valid_dtype(int dtype) { return dtype == FE_DTYPE_F16 || dtype == FE_DTYPE_BF16; }
 
 }  // namespace
 }  // namespace fe

@@ -59,6 +59,26 @@ void store(const void* k, const void* v, void* kc, void* vc, const int64_t* slot
         "store");
 }
 
+void rope(void* q, void* k, const int64_t* pos, const float* cache, int rows, int hq, int hkv,
+          int dim, bool bf16, void* stream, int max_positions) {
+  check(fe_rope(q, k, pos, cache, rows, hq, hkv, dim, max_positions,
+                bf16 ? FE_DTYPE_BF16 : FE_DTYPE_F16, stream),
+        "rope");
+}
+
+void accept(const int64_t* draft, const int64_t* verify, int64_t* committed, int batch, int k,
+            void* stream) {
+  check(fe_accept(draft, verify, committed, batch, k, stream), "accept");
+}
+
+void rope_store(void* q, void* k, const void* v, void* kc, void* vc, const int64_t* slots,
+                const int64_t* pos, const float* cache, int rows, int hq, int hkv, int dim,
+                bool bf16, void* stream, int max_positions, int cache_slots) {
+  check(fe_rope_append(q, k, v, k, kc, vc, slots, pos, cache, rows, hq, hkv, dim, max_positions,
+                       bf16 ? FE_DTYPE_BF16 : FE_DTYPE_F16, cache_slots, stream),
+        "rope_store");
+}
+
 void copy_blocks(void* const* k_pools, void* const* v_pools, int layers, const int32_t* src,
                  const int32_t* dst, const int32_t* ntok, int num_copies, int page, int width,
                  int blocks, bool bf16, void* stream) {

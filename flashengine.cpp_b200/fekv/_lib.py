@@ -30,6 +30,7 @@ FE_DEVERR_PAGE_RANGE = 0x2
 FE_DEVERR_NTOK_RANGE = 0x4
 FE_DEVERR_TIMEOUT = 0x8
 FE_DEVERR_SMEM_ALIGN = 0x10
+FE_DEVERR_POS_RANGE = 0x20
 
 FE_MAX_LAYERS = 128
 
@@ -54,6 +55,9 @@ SIGNATURES = {
     "fe_attn_plan_create_host": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
     "fe_attn_plan_debug_meta": (_I, [_P, _P, _I64, ctypes.POINTER(_I64)]),
     "fe_paged_decode_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
+    "fe_rope": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
+    "fe_rope_append": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I64, _P]),
+    "fe_accept": (_I, [_P, _P, _P, _I, _I, _P]),
 }
 
 

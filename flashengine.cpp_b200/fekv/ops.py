@@ -70,6 +70,45 @@ def store(k, v, kc, vc, slots, rows=None, width=None, bf16=None, stream=None, ca
 
 
 # ---------------------------------------------------------------------------
+# fe::cuda::rope / accept  (include/fe/native_cuda.hpp:13,15) and the fused
+# rope + store (no reference counterpart)
+# ---------------------------------------------------------------------------
+
+def rope(q, k, pos, cache, stream=None):
+    """Rotate q [rows, hq, dim] and k [rows, hkv, dim] in place with the fp32
+    cache [max_positions, dim] (cos | sin); pos: int64 [rows] (device)."""
+    lib = _lib.load()
+    rows, hkv, dim = (int(x) for x in k.shape)
+    hq = int(q.shape[1]) if q is not None else 0
+    check(lib.fe_rope(_ptr(q) if q is not None else None, _ptr(k), _ptr(pos), _ptr(cache), rows,
+                      hq, hkv, dim, int(cache.shape[0]), dtype_code(k), _stream(stream)), "rope")
+
+
+def rope_append(q, k, v, kc, vc, slots, pos, cache, k_out=None, stream=None):
+    """rope + store in one launch: q rotated in place, rotated k (and v) written
+    to the pools [cache_slots, hkv*dim] through `slots`; the rotated keys also
+    go to `k_out` when given (it may be `k`)."""
+    lib = _lib.load()
+    rows, hkv, dim = (int(x) for x in k.shape)
+    hq = int(q.shape[1])
+    cache_slots = int(kc.numel() // (hkv * dim))
+    check(lib.fe_rope_append(_ptr(q), _ptr(k), _ptr(v), _ptr(k_out) if k_out is not None else None,
+                             _ptr(kc), _ptr(vc), _ptr(slots), _ptr(pos), _ptr(cache), rows, hq, hkv,
+                             dim, int(cache.shape[0]), dtype_code(k), cache_slots,
+                             _stream(stream)), "rope_append")
+
+
+def accept(draft, verify, out, stream=None):
+    """Greedy acceptance: draft int64 [batch, k], verify [batch, k+1],
+    out [batch, k+2] (device)."""
+    lib = _lib.load()
+    batch = int(verify.shape[0])
+    k = int(verify.shape[1]) - 1
+    check(lib.fe_accept(_ptr(draft), _ptr(verify), _ptr(out), batch, k, _stream(stream)),
+          "accept")
+
+
+# ---------------------------------------------------------------------------
 # block copy / copy-on-write and page clearing (no reference counterpart)
 # ---------------------------------------------------------------------------
 

@@ -53,6 +53,7 @@ typedef enum fe_dtype { FE_DTYPE_F16 = 0, FE_DTYPE_BF16 = 1 } fe_dtype;
 #define FE_DEVERR_NTOK_RANGE 0x4u  /* copy: ntok outside [0, page] (copy skipped) */
 #define FE_DEVERR_TIMEOUT 0x8u     /* attention: a pipeline wait exceeded its bound */
 #define FE_DEVERR_SMEM_ALIGN 0x10u /* attention: dynamic shared memory not 1 KiB aligned (launch skipped) */
+#define FE_DEVERR_POS_RANGE 0x20u  /* rope: position outside [0, max_positions) (row skipped) */
 
 const char* fe_status_string(int status);
 const char* fe_last_error(void);
@@ -108,6 +109,44 @@ int fe_kv_clear_pages(void* const* pools, int num_pools, const int32_t* pages, i
 int fe_kv_gather(const void* pool, void* out, const int32_t* kv, const int32_t* pages,
                  const int32_t* last, const int32_t* row_offset, int batch, int max_len, int page,
                  int width, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Rotary embedding. Replaces fe::cuda::rope (include/fe/native_cuda.hpp:13;
+ * src/cuda_kernels.cu:19-23 rope_kernel and :33 its launcher), bit-exact:
+ * for each head and pair (j, j + dim/2), with c = cache[pos*dim + j] and
+ * s = cache[pos*dim + dim/2 + j] (fp32 cache [max_positions, dim], cos then
+ * sin), x[j] = a*c - b*s and x[j + dim/2] = b*c + a*s, each product and sum
+ * rounded to fp32 separately, the result rounded to the 16-bit type.
+ *   q: [rows, hq, dim], k: [rows, hkv, dim] (rotated in place; hq may be 0)
+ *   pos: int64 [rows] (device). A position outside [0, max_positions) leaves
+ *        its row unrotated and raises FE_DEVERR_POS_RANGE (the reference
+ *        reads out of bounds there).
+ * dim a multiple of 4; q/k 4-byte aligned, cache 8-byte aligned.
+ * ------------------------------------------------------------------------ */
+int fe_rope(void* q, void* k, const int64_t* pos, const float* cache, int rows, int hq, int hkv,
+            int dim, int max_positions, int dtype, void* stream);
+
+/* Fused RoPE + K/V append (one launch): rotates q in place, and writes the
+ * rotated keys and the values to the pools through the slot mapping exactly
+ * as fe_rope followed by fe_kv_append would (slot < 0 skipped, slot >=
+ * cache_slots skipped and flagged). k and v ([rows, hkv, dim]) are read
+ * only; when k_out is not NULL the rotated keys are also written there (k_out
+ * may equal k). Pools are [cache_slots, hkv*dim]. */
+int fe_rope_append(void* q, const void* k, const void* v, void* k_out, void* k_pool,
+                   void* v_pool, const int64_t* slots, const int64_t* pos, const float* cache,
+                   int rows, int hq, int hkv, int dim, int max_positions, int dtype,
+                   int64_t cache_slots, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Greedy speculative acceptance. Replaces fe::cuda::accept
+ * (include/fe/native_cuda.hpp:15; src/cuda_kernels.cu:25 accept_kernel and
+ * :35 its launcher). For each row b: m = the number of leading draft tokens
+ * draft[b, i] equal to verify[b, i]; out[b, 0..m) = those drafts,
+ * out[b, m] = verify[b, m], out[b, k+1] = m + 1; out[b, m+1..k] untouched.
+ *   draft: int64 [batch, k], verify: int64 [batch, k+1], out: int64 [batch, k+2]
+ * ------------------------------------------------------------------------ */
+int fe_accept(const int64_t* draft, const int64_t* verify, int64_t* out, int batch, int k,
+              void* stream);
 
 /* ------------------------------------------------------------------------
  * Paged attention plan. Replaces fe::cuda::create_plan / destroy_plan /

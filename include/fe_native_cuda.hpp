@@ -3,13 +3,14 @@
 //
 // The KV / attention declarations keep the exact signatures of the
 // reference's namespace fe::cuda (Cambridgebit/FlashEngine.cpp
-// include/fe/native_cuda.hpp:6-10,14), so src/cuda_model.cpp compiles
+// include/fe/native_cuda.hpp:6-10,13-15), so src/cuda_model.cpp compiles
 // unchanged against this library in place of src/flashinfer_attention.cu and
-// the store() of src/cuda_kernels.cu. Errors surface as std::runtime_error,
+// the rope(), store() and accept() of src/cuda_kernels.cu. Errors surface as std::runtime_error,
 // as check() does in the reference (src/cuda_kernels.cu:10,
 // src/flashinfer_attention.cu:13). No LibTorch types.
 //
-// copy_blocks / clear_pages are additions with no reference counterpart.
+// rope_store, copy_blocks and clear_pages are additions with no reference
+// counterpart.
 #pragma once
 #include <cstddef>
 #include <cstdint>
@@ -27,9 +28,25 @@ void prepare_plan(AttentionPlan* plan, const int32_t* qo, const int32_t* kv, con
 // include/fe/native_cuda.hpp:10 — device pointers.
 void attention(AttentionPlan* plan, void* q, void* k, void* v, void* output, bool causal,
                void* stream);
+// include/fe/native_cuda.hpp:13 — q [rows, hq, dim] and k [rows, hkv, dim]
+// rotated in place with the fp32 cache [max_positions, dim]; pos is a device
+// int64 array. Bit-identical to the reference kernel.
+void rope(void* q, void* k, const int64_t* pos, const float* cache, int rows, int hq, int hkv,
+          int dim, bool bf16, void* stream, int max_positions);
 // include/fe/native_cuda.hpp:14 — slots is a device int64 array.
 void store(const void* k, const void* v, void* kc, void* vc, const int64_t* slots, int rows,
            int width, bool bf16, void* stream, int cache_slots);
+// include/fe/native_cuda.hpp:15 — draft [batch, k], verify [batch, k+1],
+// committed [batch, k+2], all device int64.
+void accept(const int64_t* draft, const int64_t* verify, int64_t* committed, int batch, int k,
+            void* stream);
+
+// rope() followed by store() in one launch: q rotated in place, rotated keys
+// written back to k and, with v, to the pools through `slots` (no reference
+// counterpart; same results as the two calls).
+void rope_store(void* q, void* k, const void* v, void* kc, void* vc, const int64_t* slots,
+                const int64_t* pos, const float* cache, int rows, int hq, int hkv, int dim,
+                bool bf16, void* stream, int max_positions, int cache_slots);
 
 // Block copy / copy-on-write across layers (no reference counterpart):
 // k_pools/v_pools are host arrays of per-layer device pool pointers,

@@ -48,6 +48,7 @@ def c_oracle():
         lib.fe_oracle_attention.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _P,
                                             _I, _I, _I, _I, _I, _I, _I]
         lib.fe_oracle_attention.restype = _I
+        lib.fe_oracle_rope.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I]
         lib.fe_oracle_float_to_half.argtypes = [ctypes.c_float]
         lib.fe_oracle_float_to_half.restype = ctypes.c_uint16
         lib.fe_oracle_float_to_bf16.argtypes = [ctypes.c_float]
@@ -91,6 +92,39 @@ def copy_blocks(k_pools, v_pools, src, dst, ntok, page, width):
     src, dst, ntok = _i32(src), _i32(dst), _i32(ntok)
     c_oracle().fe_oracle_copy_blocks(kp, vp, n, _ptr(src), _ptr(dst), _ptr(ntok), src.shape[0],
                                      int(page), int(width))
+
+
+def rope(q, k, pos, cache, dtype):
+    """RoPE restated (src/cuda_kernels.cu:19-23) on uint16 bit arrays
+    q [rows, hq, dim] and k [rows, hkv, dim] (returned rotated copies);
+    cache: float32 [max_positions, dim]."""
+    q = np.ascontiguousarray(q, dtype=np.uint16).copy()
+    k = np.ascontiguousarray(k, dtype=np.uint16).copy()
+    pos = _i64(pos)
+    cache = np.ascontiguousarray(cache, dtype=np.float32)
+    rows, hkv, dim = k.shape
+    hq = q.shape[1] if q.ndim == 3 else 0
+    c_oracle().fe_oracle_rope(_ptr(q), _ptr(k), _ptr(pos), _ptr(cache), rows, hq, hkv, dim,
+                              cache.shape[0], dtype)
+    return q, k
+
+
+def accept(draft, verify):
+    """Greedy acceptance restated (src/cuda_kernels.cu:25): returns the
+    [batch, k+2] rows the kernel writes (entries it leaves untouched are -1)."""
+    draft = np.asarray(draft, np.int64)
+    verify = np.asarray(verify, np.int64)
+    batch, k1 = verify.shape
+    k = k1 - 1
+    out = np.full((batch, k + 2), -1, np.int64)
+    for b in range(batch):
+        m = 0
+        while m < k and draft[b, m] == verify[b, m]:
+            out[b, m] = draft[b, m]
+            m += 1
+        out[b, m] = verify[b, m]
+        out[b, k + 1] = m + 1
+    return out
 
 
 def seq_lengths(kv, last, page):
@@ -147,6 +181,35 @@ def from_float(x: np.ndarray, dtype: int) -> np.ndarray:
 # ---------------------------------------------------------------------------
 # The reference's own ATen path, compiled for the CPU.
 # ---------------------------------------------------------------------------
+
+_ref_cuda_lib = None
+
+
+def ref_cuda_available() -> bool:
+    return os.path.exists(build_oracle.REF_CUDA_LIB)
+
+
+def ref_cuda():
+    """The reference's own CUDA kernels (src/cuda_kernels.cu) compiled from its
+    source: ref_cuda_rope / ref_cuda_store / ref_cuda_accept, device pointers.
+    GPU tests only."""
+    global _ref_cuda_lib
+    if _ref_cuda_lib is None:
+        path = build_oracle.REF_CUDA_LIB
+        if not os.path.exists(path):
+            built = build_oracle.build_reference_cuda()
+            if built is None:
+                raise FileNotFoundError("oracle/_ref/libfe_ref_cuda.so is not built and the "
+                                        "reference source tree is absent")
+        lib = ctypes.CDLL(path)
+        lib.ref_cuda_rope.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I]
+        lib.ref_cuda_store.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _P, _I]
+        lib.ref_cuda_accept.argtypes = [_P, _P, _P, _I, _I, _P]
+        for f in (lib.ref_cuda_rope, lib.ref_cuda_store, lib.ref_cuda_accept):
+            f.restype = _I
+        _ref_cuda_lib = lib
+    return _ref_cuda_lib
+
 
 def ref_library_path() -> str:
     return build_oracle.REF_LIB

@@ -7,6 +7,11 @@
   the CPU LibTorch that ships with the PyTorch wheel. Built only where the
   reference tree exists (it is not present on the GPU box, which uses the
   prebuilt file that travels with the repository snapshot).
+* ``oracle/_ref/libfe_ref_cuda.so`` — the reference's own CUDA kernels
+  (``src/cuda_kernels.cu``: rope, store, accept) for sm_100a through
+  ``oracle/ref_cuda_wrap.cu``; the GPU tests run them as the comparator for the
+  fused RoPE+append and accept kernels. Built the same way (reference tree
+  only; the GPU box uses the prebuilt file).
 
 Run directly: ``python oracle/build_oracle.py [--reference-root DIR]``.
 """
@@ -25,6 +30,8 @@ C_ORACLE_LIB = os.path.join(HERE, "libfe_oracle.so")
 REF_WRAP_SRC = os.path.join(HERE, "ref_aten_wrap.cpp")
 REF_DIR = os.path.join(HERE, "_ref")
 REF_LIB = os.path.join(REF_DIR, "libfe_ref_aten.so")
+REF_CUDA_WRAP_SRC = os.path.join(HERE, "ref_cuda_wrap.cu")
+REF_CUDA_LIB = os.path.join(REF_DIR, "libfe_ref_cuda.so")
 
 
 def _stale(target: str, *sources: str) -> bool:
@@ -36,7 +43,7 @@ def _stale(target: str, *sources: str) -> bool:
 
 def build_c_oracle(force: bool = False) -> str:
     if force or _stale(C_ORACLE_LIB, C_ORACLE_SRC):
-        cmd = ["gcc", "-O2", "-std=c11", "-fPIC", "-shared", "-Wall", "-Wextra",
+        cmd = ["gcc", "-O2", "-std=c11", "-ffp-contract=off", "-fPIC", "-shared", "-Wall", "-Wextra",
                C_ORACLE_SRC, "-o", C_ORACLE_LIB, "-lm"]
         subprocess.run(cmd, check=True)
     return C_ORACLE_LIB
@@ -70,6 +77,23 @@ def build_reference(reference_root: str = DEFAULT_REFERENCE_ROOT, force: bool = 
     return REF_LIB
 
 
+def build_reference_cuda(reference_root: str = DEFAULT_REFERENCE_ROOT,
+                         force: bool = False) -> str | None:
+    """Compile the reference's CUDA kernels (src/cuda_kernels.cu) for sm_100a
+    with nvcc (no GPU needed to build). None when the tree is absent."""
+    src = os.path.join(reference_root, "src", "cuda_kernels.cu")
+    if not os.path.exists(src):
+        return REF_CUDA_LIB if os.path.exists(REF_CUDA_LIB) else None
+    if not (force or _stale(REF_CUDA_LIB, REF_CUDA_WRAP_SRC, src)):
+        return REF_CUDA_LIB
+    os.makedirs(REF_DIR, exist_ok=True)
+    cmd = ["nvcc", "-gencode", "arch=compute_100a,code=sm_100a", "-std=c++17", "-O2",
+           "-Xcompiler", "-fPIC", "-shared", "-I", os.path.join(reference_root, "include"),
+           REF_CUDA_WRAP_SRC, "-o", REF_CUDA_LIB]
+    subprocess.run(cmd, check=True)
+    return REF_CUDA_LIB
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-root", default=DEFAULT_REFERENCE_ROOT)
@@ -77,6 +101,7 @@ def main(argv=None) -> int:
     a = ap.parse_args(argv)
     print(build_c_oracle(a.force))
     print(build_reference(a.reference_root, a.force))
+    print(build_reference_cuda(a.reference_root, a.force))
     return 0
 
 

@@ -47,7 +47,7 @@ def test_every_declared_function_is_exported():
 
 def test_shim_exports_reference_signatures():
     """The C++ shim keeps the reference's fe::cuda signatures
-    (include/fe/native_cuda.hpp:7-10,14) so src/cuda_model.cpp links unchanged."""
+    (include/fe/native_cuda.hpp:7-10,13-15) so src/cuda_model.cpp links unchanged."""
     syms = exported(_lib.SHIM_PATH, demangle=True)
     for sig in [
         "fe::cuda::create_plan(int, int, int, int, int, int, bool, int)",
@@ -57,6 +57,9 @@ def test_shim_exports_reference_signatures():
         "fe::cuda::attention(fe::cuda::AttentionPlan*, void*, void*, void*, void*, bool, void*)",
         "fe::cuda::store(void const*, void const*, void*, void*, long const*, int, int, bool, "
         "void*, int)",
+        "fe::cuda::rope(void*, void*, long const*, float const*, int, int, int, int, bool, void*, "
+        "int)",
+        "fe::cuda::accept(long const*, long const*, long*, int, int, void*)",
     ]:
         assert sig in syms, sig
     ctypes.CDLL(_lib.SHIM_PATH)

@@ -1,0 +1,74 @@
+"""CPU checks of the RoPE and greedy-accept restatements (oracle), pinned to
+the reference: RoPE against an independent float32 numpy evaluation of
+src/cuda_kernels.cu:19-23, accept against the known answers of the
+reference's own test (tests/gpu_ops_tests.cpp:55-79: batch 1/2/4/8, k 1..15,
+every accepted length)."""
+import numpy as np
+import pytest
+
+import oracle
+
+
+def rope_cache(max_pos, dim, theta=1.0e6):
+    inv = 1.0 / (theta ** (np.arange(0, dim, 2, dtype=np.float64) / dim))
+    ang = np.arange(max_pos, dtype=np.float64)[:, None] * inv[None, :]
+    return np.concatenate([np.cos(ang), np.sin(ang)], axis=1).astype(np.float32)
+
+
+def numpy_rope(x_bits, pos, cache, dtype):
+    x = oracle.to_float(x_bits, dtype).astype(np.float32)
+    half = x.shape[-1] // 2
+    c = cache[pos][:, None, :half]
+    s = cache[pos][:, None, half:]
+    a, b = x[..., :half], x[..., half:]
+    with np.errstate(over="ignore"):
+        lo = (a * c) - (b * s)  # float32 products and sums, each rounded
+        hi = (b * c) + (a * s)
+    return oracle.from_float(np.concatenate([lo, hi], axis=-1), dtype)
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_oracle_rope_matches_float32_numpy(dtype):
+    rng = np.random.default_rng(5 + dtype)
+    rows, hq, hkv, dim, max_pos = 37, 8, 2, 128, 4096
+    cache = rope_cache(max_pos, dim)
+    q = oracle.from_float(rng.standard_normal((rows, hq, dim)).astype(np.float32) * 3, dtype)
+    k = oracle.from_float(rng.standard_normal((rows, hkv, dim)).astype(np.float32) * 3, dtype)
+    pos = rng.integers(0, max_pos, rows)
+    qo, ko = oracle.rope(q, k, pos, cache, dtype)
+    np.testing.assert_array_equal(qo, numpy_rope(q, pos, cache, dtype))
+    np.testing.assert_array_equal(ko, numpy_rope(k, pos, cache, dtype))
+
+
+def test_oracle_rope_skips_out_of_range_positions():
+    rng = np.random.default_rng(1)
+    cache = rope_cache(64, 128)
+    k = oracle.from_float(rng.standard_normal((3, 2, 128)).astype(np.float32), 1)
+    pos = np.array([5, 64, -1])
+    _, ko = oracle.rope(np.zeros((3, 0, 128), np.uint16), k, pos, cache, 1)
+    np.testing.assert_array_equal(ko[1:], k[1:])
+    assert not np.array_equal(ko[0], k[0])
+
+
+def test_oracle_accept_reference_known_answers():
+    """The reference test's matrix: drafts 10+j, the verifier agrees up to
+    position `accepted` where it says 99."""
+    checks = 0
+    for batch in (1, 2, 4, 8):
+        for k in range(1, 16):
+            for first in range(k + 1):
+                d = np.zeros((batch, k), np.int64)
+                v = np.zeros((batch, k + 1), np.int64)
+                for b in range(batch):
+                    acc = (first + b) % (k + 1)
+                    d[b] = 10 + np.arange(k)
+                    v[b, :k] = 10 + np.arange(k)
+                    v[b, acc] = 99
+                out = oracle.accept(d, v)
+                for b in range(batch):
+                    acc = (first + b) % (k + 1)
+                    assert out[b, k + 1] == acc + 1 and out[b, acc] == 99
+                    assert list(out[b, :acc]) == list(range(10, 10 + acc))
+                    assert (out[b, acc + 1:k + 1] == -1).all()  # untouched
+                    checks += 1
+    assert checks == (1 + 2 + 4 + 8) * sum(k + 1 for k in range(1, 16))  # 2025, as in the reference
