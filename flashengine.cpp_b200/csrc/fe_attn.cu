@@ -25,6 +25,7 @@ namespace fe {
 
 int decode_launch(int dtype, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
+int decode_merge_launch(int dtype, const void* args, int grid, cudaStream_t stream);
 int prefill_tc_launch(int dtype, const CUtensorMap& kmap, const CUtensorMap& vmap,
                       const void* args, int grid, cudaStream_t stream);
 
@@ -355,6 +356,17 @@ int fe_attn_run(fe_attn_plan* p, const void* q, const void* k_pool, const void* 
     if (rc != FE_OK) return rc;
     p->vmap_ptr = v_pool;
   }
+  // split units of the decode list are merged by a second, dependent kernel
+  int grid_merge = 0;
+  if (grid_dec > 0) {
+    if (p->fixed_grid) {
+      grid_merge = p->cfg.dec_grid_cap;
+    } else {
+      MetaHeader h;
+      std::memcpy(&h, p->last.meta.data(), sizeof(h));
+      grid_merge = h.n_groups[2];
+    }
+  }
   const float scale_log2 = 1.4426950408889634f / sqrtf(float(p->cfg.dim));
   auto s = static_cast<cudaStream_t>(stream);
   const int G = p->cfg.hq / p->cfg.hkv;
@@ -366,6 +378,7 @@ int fe_attn_run(fe_attn_plan* p, const void* q, const void* k_pool, const void* 
                               device_error_word(), p->cfg.hq, G, p->cfg.page, view, scale_log2};
     if (grid_dec > 0) {
       int rc = decode_launch(p->dtype, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
+      if (rc == FE_OK) rc = decode_merge_launch(p->dtype, &a, grid_merge, s);
       if (rc != FE_OK) return rc;
     }
     if (grid_rows > 0) {
@@ -378,6 +391,7 @@ int fe_attn_run(fe_attn_plan* p, const void* q, const void* k_pool, const void* 
                        p->cfg.page, view, scale_log2};
     if (grid_dec > 0) {
       int rc = decode_launch(p->dtype, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
+      if (rc == FE_OK) rc = decode_merge_launch(p->dtype, &a, grid_merge, s);
       if (rc != FE_OK) return rc;
     }
     if (grid_rows > 0) {

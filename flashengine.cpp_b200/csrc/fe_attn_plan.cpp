@@ -50,7 +50,7 @@ int build_view(const PlanConfig& cfg, const std::vector<Unit>& units, int grid_c
       if (nsplit > 1) {
         group = static_cast<int>(v.groups.size());
         part0 = static_cast<int>(v.partial_floats);
-        v.groups.push_back(SplitGroup{nsplit, part0, rec, u.rows});
+        v.groups.push_back(SplitGroup{nsplit, part0, rec, u.rows, u.seq, u.kvh, {0, 0}});
         v.partial_floats += int64_t(rec) * nsplit;
         ++v.split_units;
       }
@@ -124,8 +124,9 @@ int build_view(const PlanConfig& cfg, const std::vector<Unit>& units, int grid_c
 // Decode lists are bandwidth-bound and their cost is proportional to key
 // tiles, so they are balanced exactly: the units' tile ranges are laid end to
 // end and cut into `grid` equal contiguous pieces, one per CTA. A unit cut
-// into several pieces becomes a split unit (merged by the last piece to
-// finish). Every CTA streams the same number of tiles, to within one.
+// into several pieces becomes a split unit (its pieces write partial records,
+// merged by a separate kernel). Every CTA streams the same number of tiles, to
+// within one.
 int build_cut_view(const PlanConfig& cfg, const std::vector<Unit>& units, int grid_cap_in,
                    int min_tiles_per_cta, bool fixed_grid, View& v, std::string& err) {
   v = View{};
@@ -161,7 +162,8 @@ int build_cut_view(const PlanConfig& cfg, const std::vector<Unit>& units, int gr
       const int rec = partial_rec_floats(units[i].rows);
       group_of[i] = static_cast<int>(v.groups.size());
       part0_of[i] = static_cast<int>(v.partial_floats);
-      v.groups.push_back(SplitGroup{pieces[i], part0_of[i], rec, units[i].rows});
+      v.groups.push_back(SplitGroup{pieces[i], part0_of[i], rec, units[i].rows, units[i].seq,
+                                    units[i].kvh, {0, 0}});
       v.partial_floats += int64_t(rec) * pieces[i];
       ++v.split_units;
     }

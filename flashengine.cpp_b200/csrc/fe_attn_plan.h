@@ -47,11 +47,13 @@ struct WorkItem {  // 32 bytes
   int32_t group;  // split group id, -1 if unsplit
 };
 
-struct SplitGroup {  // 16 bytes
-  int32_t nsplit;
+struct SplitGroup {  // 32 bytes
+  int32_t nsplit;      // 0 for the placeholder entries that keep row and decode ids apart
   int32_t part0;       // float offset of split 0's record; split s at part0 + s*rec_floats
   int32_t rec_floats;  // rows*130 rounded up to a multiple of 4
   int32_t rows;        // valid packed rows in each record
+  int32_t seq, kvh;    // the unit's sequence and first KV head (where merged rows go)
+  int32_t pad[2];
 };
 
 // Byte offsets are from the start of the metadata buffer. Index [c] of the

@@ -16,8 +16,12 @@
 //  * Consumer warp w serves head w % H; when H < 8, the 8/H warps of a head
 //    take alternate tiles and merge in shared memory. Tile math: KeyState
 //    (S^T = K Q^T and O^T = V^T P^T on mma.m16n8k16, fp32 accumulation).
-//  * Split-K across CTAs: partial records + last-arriving CTA merges
-//    (atomic ticket, no waiting), counter re-armed for graph replay.
+//  * Split-K across CTAs: the pieces of a split unit write partial (O, m, l)
+//    records; decode_merge_kernel, launched as a programmatic dependent of
+//    this kernel, merges every split unit once the whole grid has finished,
+//    so no streaming CTA carries merge work into the tail. (The allocation-free
+//    entry point keeps the in-kernel merge: the last piece to arrive merges,
+//    atomic ticket, counter re-armed for graph replay.)
 //  * Bounded waits as in fe_attn.cu; a CTA that gives up records
 //    FE_DEVERR_TIMEOUT and drains its own copies before exiting.
 #include <mutex>
@@ -29,6 +33,7 @@ namespace fe {
 
 int decode_launch(int dtype, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
+int decode_merge_launch(int dtype, const void* args, int grid, cudaStream_t stream);
 int decode_smem_bytes(int heads);
 
 namespace {
@@ -58,7 +63,7 @@ __device__ __forceinline__ __half to_elem<__half>(float x) {
   return __float2half_rn(x);
 }
 
-template <typename T, int H, int NT>
+template <typename T, int H, int NT, bool kInlineMerge>
 __device__ __forceinline__ void decode_item(const AttnArgs<T>& a, const WorkItem& wi,
                                             const SeqInfo& si, const SplitGroup* groups,
                                             uint8_t* stages, uint64_t* full, uint64_t* empty,
@@ -179,7 +184,7 @@ __device__ __forceinline__ void decode_item(const AttnArgs<T>& a, const WorkItem
     named_barrier_sync(1, kDecWarps * 32);
   }
 
-  if (wi.group >= 0) {
+  if (kInlineMerge && wi.group >= 0) {
     __threadfence();
     named_barrier_sync(1, kDecWarps * 32);
     if (tid == 0) {
@@ -216,6 +221,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   uint64_t* empty = full + C::kStages;
   volatile int* flags = reinterpret_cast<volatile int*>(empty + C::kStages);
 
+  // the merge kernel may be scheduled now; it waits for this grid's completion
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const MetaHeader* hdr = reinterpret_cast<const MetaHeader*>(a.meta);
   constexpr int kView = 2;  // decode work list
@@ -314,11 +321,11 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     const WorkItem wi = items[it];
     const SeqInfo si = seqs[wi.seq];
     if (si.qrows * a.G <= 8)
-      decode_item<T, H, 1>(a, wi, si, groups, stages, full, empty, flags, comb, warp, lane, g,
-                           aborted);
+      decode_item<T, H, 1, false>(a, wi, si, groups, stages, full, empty, flags, comb, warp, lane,
+                                  g, aborted);
     else
-      decode_item<T, H, 2>(a, wi, si, groups, stages, full, empty, flags, comb, warp, lane, g,
-                           aborted);
+      decode_item<T, H, 2, false>(a, wi, si, groups, stages, full, empty, flags, comb, warp, lane,
+                                  g, aborted);
   }
   if (aborted && lane == 0) raise_device_error(a.err, FE_DEVERR_TIMEOUT);
 }
@@ -349,6 +356,116 @@ int decode_smem_bytes(int heads) {
     case 2: return DecCfg<2>::kSmem;
     default: return DecCfg<1>::kSmem;
   }
+}
+
+namespace {
+
+// Merge the partial records of every split unit of the decode list: one CTA
+// per unit (striding when the grid is smaller, as under graph replay, where
+// the grid is fixed and the unit count comes from the metadata), one warp per
+// merged row. A row's loads are issued together (the split records' O vectors
+// four at a time, m and l one split per lane), so a row costs about one L2
+// round trip. Launched with programmatic stream serialization after
+// paged_decode_kernel: its CTAs become resident on the SMs the decode grid's
+// early finishers free and start when that grid has completed.
+constexpr int kMergeThreads = 1024;
+
+template <typename T>
+__device__ __forceinline__ void merge_row_warp(const float* partials, const SplitGroup& gi, int r,
+                                               int lane, T* out_row) {
+  const int ns = gi.nsplit;
+  const int d4 = lane * 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float M = -INFINITY, L = 0.f;
+  for (int s0 = 0; s0 < ns; s0 += 32) {
+    // this chunk's maxima and sums: split s0 + lane per lane
+    const int sl = s0 + lane;
+    float m = -INFINITY, l = 0.f;
+    if (sl < ns) {
+      const float* rec = partials + gi.part0 + static_cast<int64_t>(sl) * gi.rec_floats;
+      m = __ldcg(rec + gi.rows * kHeadDim + r);
+      l = __ldcg(rec + gi.rows * (kHeadDim + 1) + r);
+    }
+    float mc = m;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, o));
+    const float M_new = fmaxf(M, mc);
+    const float base = M_new == -INFINITY ? 0.f : M_new;
+    // rescale what the earlier chunks accumulated
+    const float resc = M == -INFINITY ? 0.f : fast_exp2(M - base);
+    acc.x *= resc;
+    acc.y *= resc;
+    acc.z *= resc;
+    acc.w *= resc;
+    L *= resc;
+    M = M_new;
+    const float sc = sl < ns ? fast_exp2(m - base) : 0.f;
+    float lw = l * sc;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o);
+    L += lw;
+    const int n = min(32, ns - s0);
+#pragma unroll 4
+    for (int j = 0; j < n; ++j) {
+      const float* rec = partials + gi.part0 + static_cast<int64_t>(s0 + j) * gi.rec_floats;
+      const float4 x = __ldcg(reinterpret_cast<const float4*>(rec + r * kHeadDim + d4));
+      const float w = __shfl_sync(0xffffffffu, sc, j);
+      acc.x = fmaf(x.x, w, acc.x);
+      acc.y = fmaf(x.y, w, acc.y);
+      acc.z = fmaf(x.z, w, acc.z);
+      acc.w = fmaf(x.w, w, acc.w);
+    }
+  }
+  const float inv = 1.f / L;
+  store4<T>(out_row + d4, acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const AttnArgs<T> a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const MetaHeader* hdr = reinterpret_cast<const MetaHeader*>(a.meta);
+  const int n = hdr->n_groups[2];
+  const SplitGroup* groups = reinterpret_cast<const SplitGroup*>(a.meta + hdr->groups_off[2]);
+  const SeqInfo* seqs = reinterpret_cast<const SeqInfo*>(a.meta + hdr->seqs_off);
+  const int G = a.G;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int gidx = blockIdx.x; gidx < n; gidx += gridDim.x) {
+    const SplitGroup gi = groups[gidx];
+    if (gi.nsplit < 2) continue;  // placeholder ids of the row lists
+    const SeqInfo si = seqs[gi.seq];
+    const int P = si.qrows * G;
+    for (int r = warp; r < gi.rows; r += kMergeThreads / 32) {
+      const int rh = r / P, p = r % P;
+      T* dst = a.out + (static_cast<int64_t>(si.q_row0 + p / G) * a.hq + (gi.kvh + rh) * G +
+                        p % G) * kHeadDim;
+      merge_row_warp<T>(a.partials, gi, r, lane, dst);
+    }
+  }
+}
+
+template <typename T>
+int launch_merge_t(const AttnArgs<T>& args, int grid, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kMergeThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FE_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_merge_kernel<T>, args));
+  return FE_OK;
+}
+
+}  // namespace
+
+int decode_merge_launch(int dtype, const void* args, int grid, cudaStream_t stream) {
+  if (grid <= 0) return FE_OK;
+  if (dtype == FE_DTYPE_BF16)
+    return launch_merge_t(*static_cast<const AttnArgs<__nv_bfloat16>*>(args), grid, stream);
+  return launch_merge_t(*static_cast<const AttnArgs<__half>*>(args), grid, stream);
 }
 
 int decode_launch(int dtype, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
@@ -530,9 +647,11 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   uint32_t g = 0;
   bool aborted = false;
   if (a.G <= 8)
-    decode_item<T, H, 1>(a, wi, si, &sg, stages, full, empty, flags, comb, warp, lane, g, aborted);
+    decode_item<T, H, 1, true>(a, wi, si, &sg, stages, full, empty, flags, comb, warp, lane, g,
+                               aborted);
   else
-    decode_item<T, H, 2>(a, wi, si, &sg, stages, full, empty, flags, comb, warp, lane, g, aborted);
+    decode_item<T, H, 2, true>(a, wi, si, &sg, stages, full, empty, flags, comb, warp, lane, g,
+                               aborted);
   if (aborted && lane == 0) raise_device_error(a.err, FE_DEVERR_TIMEOUT);
 }
 
