@@ -10,12 +10,42 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "fe_kv.h"
 
 namespace fe {
 
 inline bool valid_dtype(int dtype) { return dtype == FE_DTYPE_F16 || dtype == FE_DTYPE_BF16; }
+
+// ---- programmatic dependent launch ----------------------------------------
+// Kernels of the hot path are launched with programmatic stream
+// serialization: a kernel may become resident while its predecessor in the
+// stream is still running, and calls pdl_wait() before it touches anything
+// the predecessor produced (griddepcontrol.wait returns once the predecessor
+// grid has completed and its writes are visible; it is a no-op for a kernel
+// launched without the attribute). pdl_trigger() lets the successor be
+// scheduled as soon as every CTA of this grid has started.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---- host-side error reporting ------------------------------------------
 

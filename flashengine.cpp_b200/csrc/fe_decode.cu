@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   volatile int* flags = reinterpret_cast<volatile int*>(empty + C::kStages);
 
   // the merge kernel may be scheduled now; it waits for this grid's completion
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const MetaHeader* hdr = reinterpret_cast<const MetaHeader*>(a.meta);
   constexpr int kView = 2;  // decode work list
@@ -245,6 +245,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     fence_barrier_init();
   }
   __syncthreads();
+  // q, the pools and the split workspace belong to earlier kernels until here
+  // (a no-op when launched without programmatic serialization)
+  pdl_wait();
 
   if (warp == kDecWarps) {
     // ------------------------------------------------------------ producer
@@ -341,9 +344,8 @@ int launch_t(const CUtensorMap& kmap, const CUtensorMap& vmap, bool per_head_tma
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "paged_decode_kernel attribute");
-  paged_decode_kernel<T, H><<<grid, kDecThreads, C::kSmem, stream>>>(kmap, vmap, args,
-                                                                     per_head_tma ? 1 : 0);
-  FE_CUDA_TRY(cudaGetLastError());
+  FE_CUDA_TRY(launch_pdl(paged_decode_kernel<T, H>, dim3(grid), dim3(kDecThreads), C::kSmem,
+                         stream, kmap, vmap, args, per_head_tma ? 1 : 0));
   return FE_OK;
 }
 
@@ -422,7 +424,8 @@ __device__ __forceinline__ void merge_row_warp(const float* partials, const Spli
 
 template <typename T>
 __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const AttnArgs<T> a) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  pdl_trigger();
+  pdl_wait();
   const MetaHeader* hdr = reinterpret_cast<const MetaHeader*>(a.meta);
   const int n = hdr->n_groups[2];
   const SplitGroup* groups = reinterpret_cast<const SplitGroup*>(a.meta + hdr->groups_off[2]);
@@ -445,17 +448,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const AttnA
 
 template <typename T>
 int launch_merge_t(const AttnArgs<T>& args, int grid, cudaStream_t stream) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kMergeThreads);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  FE_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_merge_kernel<T>, args));
+  FE_CUDA_TRY(launch_pdl(decode_merge_kernel<T>, dim3(grid), dim3(kMergeThreads), 0, stream, args));
   return FE_OK;
 }
 
@@ -580,6 +573,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     fence_barrier_init();
   }
   __syncthreads();
+  // q, the pools and the split workspace belong to earlier kernels until here
+  // (a no-op when launched without programmatic serialization)
+  pdl_wait();
 
   if (warp == kDecWarps) {
     if (lane == 0) {

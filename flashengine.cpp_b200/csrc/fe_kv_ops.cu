@@ -61,6 +61,8 @@ __global__ void __launch_bounds__(kThreads) append_kernel(const uint4* __restric
                                                           const int64_t* __restrict__ slots,
                                                           int rows, int chunks_per_row,
                                                           int64_t cache_slots) {
+  pdl_trigger();
+  pdl_wait();  // k, v come from, and the pools are read by, earlier kernels
   const int64_t per_tensor = static_cast<int64_t>(rows) * chunks_per_row;
   const int64_t total = per_tensor * 2;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -253,10 +255,11 @@ int fe_kv_append(const void* k, const void* v, void* k_pool, void* v_pool, const
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  append_kernel<<<static_cast<int>(blocks), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint4*>(k), static_cast<const uint4*>(v), static_cast<uint4*>(k_pool),
-      static_cast<uint4*>(v_pool), slots, rows, chunks, cache_slots);
-  FE_CUDA_TRY(cudaGetLastError());
+  FE_CUDA_TRY(launch_pdl(append_kernel, dim3(static_cast<int>(blocks)), dim3(kThreads), 0,
+                         static_cast<cudaStream_t>(stream), static_cast<const uint4*>(k),
+                         static_cast<const uint4*>(v), static_cast<uint4*>(k_pool),
+                         static_cast<uint4*>(v_pool), slots, rows, chunks,
+                         static_cast<int64_t>(cache_slots)));
   return FE_OK;
 }
 

@@ -152,6 +152,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // [group][row]; group 0 reloads Q only after both groups read them.
   float* xsum = reinterpret_cast<float*>(smem + kOffQ);
 
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const MetaHeader* hdr = reinterpret_cast<const MetaHeader*>(a.meta);
   const int view = a.view;
@@ -197,6 +198,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   bool aborted = false;
+  // q and the pools belong to earlier kernels until here (a no-op when
+  // launched without programmatic serialization)
+  pdl_wait();
   // Registers are allocated per warpgroup, so the kernel runs three full
   // warpgroups (168 registers each thread).
 
@@ -573,8 +577,8 @@ int launch_t(const CUtensorMap& kmap, const CUtensorMap& vmap, const AttnArgs<T>
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "paged_prefill_tc_kernel attribute");
-  paged_prefill_tc_kernel<T><<<grid, kTcThreads, kTcSmem, stream>>>(kmap, vmap, args);
-  FE_CUDA_TRY(cudaGetLastError());
+  FE_CUDA_TRY(launch_pdl(paged_prefill_tc_kernel<T>, dim3(grid), dim3(kTcThreads), kTcSmem, stream,
+                         kmap, vmap, args));
   return FE_OK;
 }
 

@@ -67,6 +67,8 @@ __global__ void __launch_bounds__(kRopeThreads)
                 const float* __restrict__ cache, int rows, int hq, int hkv, int dim,
                 int max_positions, int64_t cache_slots, unsigned int* err) {
   using V = typename Pair2<T>::V;
+  pdl_trigger();
+  pdl_wait();  // q, k, v come from, and the pools are read by, earlier kernels
   const int per_head = dim / 4;
   const int heads = hq + hkv;
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -145,11 +147,11 @@ int launch_rope(void* q, const void* k, const void* v, void* k_out, void* kc, vo
   const int64_t threads = static_cast<int64_t>(rows) * (hq + hkv) * (dim / 4);
   const int64_t blocks = (threads + kRopeThreads - 1) / kRopeThreads;
   if (blocks > INT32_MAX) return fail(FE_ERR_CAPACITY, "rope: too many rows");
-  rope_kernel<T><<<static_cast<int>(blocks), kRopeThreads, 0, stream>>>(
-      static_cast<T*>(q), static_cast<const T*>(k), static_cast<const T*>(v),
-      static_cast<T*>(k_out), static_cast<T*>(kc), static_cast<T*>(vc), slots, pos, cache, rows,
-      hq, hkv, dim, max_positions, cache_slots, device_error_word());
-  FE_CUDA_TRY(cudaGetLastError());
+  FE_CUDA_TRY(launch_pdl(rope_kernel<T>, dim3(static_cast<int>(blocks)), dim3(kRopeThreads), 0,
+                         stream, static_cast<T*>(q), static_cast<const T*>(k),
+                         static_cast<const T*>(v), static_cast<T*>(k_out), static_cast<T*>(kc),
+                         static_cast<T*>(vc), slots, pos, cache, rows, hq, hkv, dim,
+                         max_positions, cache_slots, device_error_word()));
   return FE_OK;
 }
 
