@@ -61,7 +61,7 @@ void store(const void* k, const void* v, void* kc, void* vc, const int64_t* slot
 
 void rope(void* q, void* k, const int64_t* pos, const float* cache, int rows, int hq, int hkv,
           int dim, bool bf16, void* stream, int max_positions) {
-  check(fe_rope(q, k, pos, cache, rows, hq, hkv, dim, max_positions,
+  check(fe_rope(q, k, pos, cache, rows, hq, hkv, dim, dim, max_positions,
                 bf16 ? FE_DTYPE_BF16 : FE_DTYPE_F16, stream),
         "rope");
 }
@@ -73,8 +73,9 @@ void accept(const int64_t* draft, const int64_t* verify, int64_t* committed, int
 
 void rope_store(void* q, void* k, const void* v, void* kc, void* vc, const int64_t* slots,
                 const int64_t* pos, const float* cache, int rows, int hq, int hkv, int dim,
-                bool bf16, void* stream, int max_positions, int cache_slots) {
-  check(fe_rope_append(q, k, v, k, kc, vc, slots, pos, cache, rows, hq, hkv, dim, max_positions,
+                bool bf16, void* stream, int max_positions, int cache_slots, int rotary_dim) {
+  check(fe_rope_append(q, k, v, k, kc, vc, slots, pos, cache, rows, hq, hkv, dim,
+                       rotary_dim <= 0 ? dim : rotary_dim, max_positions,
                        bf16 ? FE_DTYPE_BF16 : FE_DTYPE_F16, cache_slots, stream),
         "rope_store");
 }

@@ -42,7 +42,8 @@ struct Pair2<__nv_bfloat16> {
   }
 };
 
-// Rotate the pairs (j, j+half) and (j+1, j+half+1) of one head in registers.
+// Rotate the pairs (j, j+r) and (j+1, j+r+1) of one head in registers (r =
+// half the rotary dims), given cos c and sin s of both.
 template <typename T>
 __device__ __forceinline__ void rotate(typename Pair2<T>::V& lo, typename Pair2<T>::V& hi,
                                        float2 c, float2 s) {
@@ -53,18 +54,21 @@ __device__ __forceinline__ void rotate(typename Pair2<T>::V& lo, typename Pair2<
                             __fadd_rn(__fmul_rn(b.y, c.y), __fmul_rn(a.y, s.y)));
 }
 
-// Thread -> (row, head, pair of pairs). k and k_out may be the same buffer
-// (in-place RoPE). Heads [0, hq) are query heads, rotated
-// in place in q. Heads [hq, hq + hkv) are key heads: rotated, then written to
-// k_out (if given) and, when kc is given, to the pool row of the row's slot
-// together with the unrotated value head (slot < 0: skipped, as the reference
-// store does; slot >= cache_slots: skipped and flagged).
+// Thread -> (row, head, jp) with jp in [0, dim/4). k and k_out may be the
+// same buffer (in-place RoPE). With rot = rotary_dim: threads jp < rot/4 own
+// the rotation pairs (2jp, 2jp+1) <-> (rot/2 + 2jp, rot/2 + 2jp + 1); threads
+// jp >= rot/4 own four unrotated dims starting at rot + 4(jp - rot/4) (the
+// partial-rotary heads of Qwen3.5, src/hybrid_model.cpp:44). Heads [0, hq) are
+// query heads, rotated in place in q. Heads [hq, hq + hkv) are key heads:
+// rotated, then written to k_out (if given) and, when kc is given, to the pool
+// row of the row's slot together with the value head (slot < 0: skipped, as
+// the reference store does; slot >= cache_slots: skipped and flagged).
 template <typename T>
 __global__ void __launch_bounds__(kRopeThreads)
     rope_kernel(T* __restrict__ q, const T* k, const T* __restrict__ v, T* k_out,
                 T* __restrict__ kc, T* __restrict__ vc,
                 const int64_t* __restrict__ slots, const int64_t* __restrict__ pos,
-                const float* __restrict__ cache, int rows, int hq, int hkv, int dim,
+                const float* __restrict__ cache, int rows, int hq, int hkv, int dim, int rot,
                 int max_positions, int64_t cache_slots, unsigned int* err) {
   using V = typename Pair2<T>::V;
   pdl_trigger();
@@ -76,32 +80,39 @@ __global__ void __launch_bounds__(kRopeThreads)
   const int jp = static_cast<int>(idx % per_head);
   const int head = static_cast<int>((idx / per_head) % heads);
   const int row = static_cast<int>(idx / (static_cast<int64_t>(per_head) * heads));
-  const int half = dim / 2, j = 2 * jp;
   const int64_t p = pos[row];
   if (p < 0 || p >= max_positions) {
     if (jp == 0 && head == 0) raise_device_error(err, FE_DEVERR_POS_RANGE);
     return;
   }
-  const float* cs = cache + p * dim;
-  const float2 c = *reinterpret_cast<const float2*>(cs + j);
-  const float2 s = *reinterpret_cast<const float2*>(cs + half + j);
+  const bool rotating = jp < rot / 4;
+  // element offsets (in pairs of elements) of this thread's two pairs
+  const int i0 = rotating ? jp : (rot + 4 * (jp - rot / 4)) / 2;
+  const int i1 = rotating ? (rot / 2 + 2 * jp) / 2 : i0 + 1;
+  float2 c = make_float2(0.f, 0.f), s = c;
+  if (rotating) {
+    const float* cs = cache + p * rot;
+    c = *reinterpret_cast<const float2*>(cs + 2 * jp);
+    s = *reinterpret_cast<const float2*>(cs + rot / 2 + 2 * jp);
+  }
   if (head < hq) {
+    if (!rotating) return;  // q's unrotated dims stay as they are
     V* base = reinterpret_cast<V*>(q + (static_cast<int64_t>(row) * hq + head) * dim);
-    V lo = base[jp], hi = base[(half + j) / 2];
+    V lo = base[i0], hi = base[i1];
     rotate<T>(lo, hi, c, s);
-    base[jp] = lo;
-    base[(half + j) / 2] = hi;
+    base[i0] = lo;
+    base[i1] = hi;
     return;
   }
   const int h = head - hq;
   const int64_t off = (static_cast<int64_t>(row) * hkv + h) * dim;
   const V* kb = reinterpret_cast<const V*>(k + off);
-  V lo = kb[jp], hi = kb[(half + j) / 2];
-  rotate<T>(lo, hi, c, s);
-  if (k_out) {
+  V lo = kb[i0], hi = kb[i1];
+  if (rotating) rotate<T>(lo, hi, c, s);
+  if (k_out && (rotating || k_out != k)) {
     V* ko = reinterpret_cast<V*>(k_out + off);
-    ko[jp] = lo;
-    ko[(half + j) / 2] = hi;
+    ko[i0] = lo;
+    ko[i1] = hi;
   }
   if (!kc) return;
   const int64_t slot = slots[row];
@@ -112,12 +123,12 @@ __global__ void __launch_bounds__(kRopeThreads)
   }
   const int64_t dst = (slot * hkv + h) * dim;
   V* kd = reinterpret_cast<V*>(kc + dst);
-  kd[jp] = lo;
-  kd[(half + j) / 2] = hi;
+  kd[i0] = lo;
+  kd[i1] = hi;
   const V* vb = reinterpret_cast<const V*>(v + off);
   V* vd = reinterpret_cast<V*>(vc + dst);
-  vd[jp] = vb[jp];
-  vd[(half + j) / 2] = vb[(half + j) / 2];
+  vd[i0] = vb[i0];
+  vd[i1] = vb[i1];
 }
 
 // One thread per batch row: accept drafts while they equal the verifier's
@@ -143,26 +154,28 @@ __global__ void accept_kernel(const int64_t* __restrict__ draft,
 template <typename T>
 int launch_rope(void* q, const void* k, const void* v, void* k_out, void* kc, void* vc,
                 const int64_t* slots, const int64_t* pos, const float* cache, int rows, int hq,
-                int hkv, int dim, int max_positions, int64_t cache_slots, cudaStream_t stream) {
+                int hkv, int dim, int rot, int max_positions, int64_t cache_slots,
+                cudaStream_t stream) {
   const int64_t threads = static_cast<int64_t>(rows) * (hq + hkv) * (dim / 4);
   const int64_t blocks = (threads + kRopeThreads - 1) / kRopeThreads;
   if (blocks > INT32_MAX) return fail(FE_ERR_CAPACITY, "rope: too many rows");
   FE_CUDA_TRY(launch_pdl(rope_kernel<T>, dim3(static_cast<int>(blocks)), dim3(kRopeThreads), 0,
                          stream, static_cast<T*>(q), static_cast<const T*>(k),
                          static_cast<const T*>(v), static_cast<T*>(k_out), static_cast<T*>(kc),
-                         static_cast<T*>(vc), slots, pos, cache, rows, hq, hkv, dim,
+                         static_cast<T*>(vc), slots, pos, cache, rows, hq, hkv, dim, rot,
                          max_positions, cache_slots, device_error_word()));
   return FE_OK;
 }
 
 int check_rope(const char* what, const void* q, const void* k, const int64_t* pos,
-               const float* cache, int rows, int hq, int hkv, int dim, int max_positions,
+               const float* cache, int rows, int hq, int hkv, int dim, int rot, int max_positions,
                int dtype) {
   if (!valid_dtype(dtype)) return fail(FE_ERR_INVALID_ARGUMENT, std::string(what) + ": bad dtype");
   if (rows < 0 || hq < 0 || hkv <= 0 || dim <= 0 || max_positions <= 0)
     return fail(FE_ERR_INVALID_ARGUMENT, std::string(what) + ": sizes out of range");
-  if (dim % 4 != 0)
-    return fail(FE_ERR_UNSUPPORTED, std::string(what) + ": dim must be a multiple of 4");
+  if (dim % 4 != 0 || rot < 0 || rot > dim || rot % 4 != 0)
+    return fail(FE_ERR_UNSUPPORTED,
+                std::string(what) + ": dim and rotary_dim must be multiples of 4, rotary_dim <= dim");
   if (rows > 0 && (!k || !pos || !cache || (hq > 0 && !q)))
     return fail(FE_ERR_INVALID_ARGUMENT, std::string(what) + ": null pointer");
   auto a4 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; };
@@ -181,23 +194,24 @@ using namespace fe;
 extern "C" {
 
 int fe_rope(void* q, void* k, const int64_t* pos, const float* cache, int rows, int hq, int hkv,
-            int dim, int max_positions, int dtype, void* stream) {
-  int rc = check_rope("fe_rope", q, k, pos, cache, rows, hq, hkv, dim, max_positions, dtype);
+            int dim, int rotary_dim, int max_positions, int dtype, void* stream) {
+  int rc = check_rope("fe_rope", q, k, pos, cache, rows, hq, hkv, dim, rotary_dim, max_positions,
+                      dtype);
   if (rc != FE_OK || rows == 0) return rc;
   auto s = static_cast<cudaStream_t>(stream);
   if (dtype == FE_DTYPE_BF16)
     return launch_rope<__nv_bfloat16>(q, k, nullptr, k, nullptr, nullptr, nullptr, pos, cache,
-                                      rows, hq, hkv, dim, max_positions, 0, s);
+                                      rows, hq, hkv, dim, rotary_dim, max_positions, 0, s);
   return launch_rope<__half>(q, k, nullptr, k, nullptr, nullptr, nullptr, pos, cache, rows, hq,
-                             hkv, dim, max_positions, 0, s);
+                             hkv, dim, rotary_dim, max_positions, 0, s);
 }
 
 int fe_rope_append(void* q, const void* k, const void* v, void* k_out, void* k_pool,
                    void* v_pool, const int64_t* slots, const int64_t* pos, const float* cache,
-                   int rows, int hq, int hkv, int dim, int max_positions, int dtype,
-                   int64_t cache_slots, void* stream) {
-  int rc = check_rope("fe_rope_append", q, k, pos, cache, rows, hq, hkv, dim, max_positions,
-                      dtype);
+                   int rows, int hq, int hkv, int dim, int rotary_dim, int max_positions,
+                   int dtype, int64_t cache_slots, void* stream) {
+  int rc = check_rope("fe_rope_append", q, k, pos, cache, rows, hq, hkv, dim, rotary_dim,
+                      max_positions, dtype);
   if (rc != FE_OK || rows == 0) return rc;
   if (cache_slots <= 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_rope_append: cache_slots <= 0");
   if (!v || !k_pool || !v_pool || !slots)
@@ -208,9 +222,9 @@ int fe_rope_append(void* q, const void* k, const void* v, void* k_out, void* k_p
   auto s = static_cast<cudaStream_t>(stream);
   if (dtype == FE_DTYPE_BF16)
     return launch_rope<__nv_bfloat16>(q, k, v, k_out, k_pool, v_pool, slots, pos, cache, rows, hq,
-                                      hkv, dim, max_positions, cache_slots, s);
+                                      hkv, dim, rotary_dim, max_positions, cache_slots, s);
   return launch_rope<__half>(q, k, v, k_out, k_pool, v_pool, slots, pos, cache, rows, hq, hkv,
-                             dim, max_positions, cache_slots, s);
+                             dim, rotary_dim, max_positions, cache_slots, s);
 }
 
 int fe_accept(const int64_t* draft, const int64_t* verify, int64_t* out, int batch, int k,

@@ -55,8 +55,9 @@ SIGNATURES = {
     "fe_attn_plan_create_host": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
     "fe_attn_plan_debug_meta": (_I, [_P, _P, _I64, ctypes.POINTER(_I64)]),
     "fe_paged_decode_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
-    "fe_rope": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
-    "fe_rope_append": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I64, _P]),
+    "fe_rope": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
+    "fe_rope_append": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I64,
+                            _P]),
     "fe_accept": (_I, [_P, _P, _P, _I, _I, _P]),
 }
 

@@ -79,3 +79,14 @@ def build_step_metadata(block_tables, starts, rows, page, pad_to=None, pad_rows=
     return StepMetadata(slots=cat(slots, np.int64), positions=cat(positions, np.int64),
                         qo=np.asarray(qo, np.int32), kv=np.asarray(kv, np.int32),
                         pages=cat(pages, np.int32), last=np.asarray(last, np.int32))
+
+
+def draft_block_metadata(blocks, start, rows, page) -> StepMetadata:
+    """A DFlash draft block of one sequence as paged metadata: `rows` new
+    positions [start, start + rows) that attend, with the full (non-causal)
+    mask, to every position < start + rows. This is the read_ / valid_ of the
+    reference's ReferenceBlockDraft::propose (src/block_draft.cpp:50-53), which
+    gathers max_model_len slots and masks those at or beyond `valid`; here the
+    same keys come from the block table, so the attention reads only them."""
+    return build_step_metadata([np.asarray(blocks, np.int64)], [int(start)], [int(rows)], page)
+

@@ -76,26 +76,29 @@ def store(k, v, kc, vc, slots, rows=None, width=None, bf16=None, stream=None, ca
 
 def rope(q, k, pos, cache, stream=None):
     """Rotate q [rows, hq, dim] and k [rows, hkv, dim] in place with the fp32
-    cache [max_positions, dim] (cos | sin); pos: int64 [rows] (device)."""
+    cache [max_positions, rotary_dim] (cos | sin); rotary_dim = the cache's
+    width (dim for full rotary, less for partial rotary); pos: int64 [rows]."""
     lib = _lib.load()
     rows, hkv, dim = (int(x) for x in k.shape)
     hq = int(q.shape[1]) if q is not None else 0
     check(lib.fe_rope(_ptr(q) if q is not None else None, _ptr(k), _ptr(pos), _ptr(cache), rows,
-                      hq, hkv, dim, int(cache.shape[0]), dtype_code(k), _stream(stream)), "rope")
+                      hq, hkv, dim, int(cache.shape[1]), int(cache.shape[0]), dtype_code(k),
+                      _stream(stream)), "rope")
 
 
 def rope_append(q, k, v, kc, vc, slots, pos, cache, k_out=None, stream=None):
     """rope + store in one launch: q rotated in place, rotated k (and v) written
     to the pools [cache_slots, hkv*dim] through `slots`; the rotated keys also
-    go to `k_out` when given (it may be `k`)."""
+    go to `k_out` when given (it may be `k`). The rotary width is the cache's
+    width, as in rope()."""
     lib = _lib.load()
     rows, hkv, dim = (int(x) for x in k.shape)
     hq = int(q.shape[1])
     cache_slots = int(kc.numel() // (hkv * dim))
     check(lib.fe_rope_append(_ptr(q), _ptr(k), _ptr(v), _ptr(k_out) if k_out is not None else None,
                              _ptr(kc), _ptr(vc), _ptr(slots), _ptr(pos), _ptr(cache), rows, hq, hkv,
-                             dim, int(cache.shape[0]), dtype_code(k), cache_slots,
-                             _stream(stream)), "rope_append")
+                             dim, int(cache.shape[1]), int(cache.shape[0]), dtype_code(k),
+                             cache_slots, _stream(stream)), "rope_append")
 
 
 def accept(draft, verify, out, stream=None):

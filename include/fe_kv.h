@@ -113,18 +113,22 @@ int fe_kv_gather(const void* pool, void* out, const int32_t* kv, const int32_t* 
 /* ------------------------------------------------------------------------
  * Rotary embedding. Replaces fe::cuda::rope (include/fe/native_cuda.hpp:13;
  * src/cuda_kernels.cu:19-23 rope_kernel and :33 its launcher), bit-exact:
- * for each head and pair (j, j + dim/2), with c = cache[pos*dim + j] and
- * s = cache[pos*dim + dim/2 + j] (fp32 cache [max_positions, dim], cos then
- * sin), x[j] = a*c - b*s and x[j + dim/2] = b*c + a*s, each product and sum
- * rounded to fp32 separately, the result rounded to the 16-bit type.
+ * with r = rotary_dim / 2, for each head and pair (j, j + r), j < r, with
+ * c = cache[pos*rotary_dim + j] and s = cache[pos*rotary_dim + r + j] (fp32
+ * cache [max_positions, rotary_dim], cos then sin), x[j] = a*c - b*s and
+ * x[j + r] = b*c + a*s, each product and sum rounded to fp32 separately, the
+ * result rounded to the 16-bit type. rotary_dim = dim is the reference's
+ * rope; rotary_dim < dim rotates only the leading dims (the partial rotary of
+ * Qwen3.5 full-attention layers, src/hybrid_model.cpp:44) and leaves the rest.
  *   q: [rows, hq, dim], k: [rows, hkv, dim] (rotated in place; hq may be 0)
  *   pos: int64 [rows] (device). A position outside [0, max_positions) leaves
  *        its row unrotated and raises FE_DEVERR_POS_RANGE (the reference
  *        reads out of bounds there).
- * dim a multiple of 4; q/k 4-byte aligned, cache 8-byte aligned.
+ * dim and rotary_dim multiples of 4, rotary_dim <= dim; q/k 4-byte aligned,
+ * cache 8-byte aligned.
  * ------------------------------------------------------------------------ */
 int fe_rope(void* q, void* k, const int64_t* pos, const float* cache, int rows, int hq, int hkv,
-            int dim, int max_positions, int dtype, void* stream);
+            int dim, int rotary_dim, int max_positions, int dtype, void* stream);
 
 /* Fused RoPE + K/V append (one launch): rotates q in place, and writes the
  * rotated keys and the values to the pools through the slot mapping exactly
@@ -134,8 +138,8 @@ int fe_rope(void* q, void* k, const int64_t* pos, const float* cache, int rows, 
  * may equal k). Pools are [cache_slots, hkv*dim]. */
 int fe_rope_append(void* q, const void* k, const void* v, void* k_out, void* k_pool,
                    void* v_pool, const int64_t* slots, const int64_t* pos, const float* cache,
-                   int rows, int hq, int hkv, int dim, int max_positions, int dtype,
-                   int64_t cache_slots, void* stream);
+                   int rows, int hq, int hkv, int dim, int rotary_dim, int max_positions,
+                   int dtype, int64_t cache_slots, void* stream);
 
 /* ------------------------------------------------------------------------
  * Greedy speculative acceptance. Replaces fe::cuda::accept

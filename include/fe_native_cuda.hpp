@@ -44,9 +44,12 @@ void accept(const int64_t* draft, const int64_t* verify, int64_t* committed, int
 // rope() followed by store() in one launch: q rotated in place, rotated keys
 // written back to k and, with v, to the pools through `slots` (no reference
 // counterpart; same results as the two calls).
+// rotary_dim <= 0 rotates all dims (the cache is [max_positions, dim]);
+// 0 < rotary_dim < dim rotates the leading rotary_dim dims with a
+// [max_positions, rotary_dim] cache (Qwen3.5 partial rotary).
 void rope_store(void* q, void* k, const void* v, void* kc, void* vc, const int64_t* slots,
                 const int64_t* pos, const float* cache, int rows, int hq, int hkv, int dim,
-                bool bf16, void* stream, int max_positions, int cache_slots);
+                bool bf16, void* stream, int max_positions, int cache_slots, int rotary_dim = 0);
 
 // Block copy / copy-on-write across layers (no reference counterpart):
 // k_pools/v_pools are host arrays of per-layer device pool pointers,

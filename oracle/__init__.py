@@ -48,7 +48,7 @@ def c_oracle():
         lib.fe_oracle_attention.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _P,
                                             _I, _I, _I, _I, _I, _I, _I]
         lib.fe_oracle_attention.restype = _I
-        lib.fe_oracle_rope.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I]
+        lib.fe_oracle_rope.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I]
         lib.fe_oracle_float_to_half.argtypes = [ctypes.c_float]
         lib.fe_oracle_float_to_half.restype = ctypes.c_uint16
         lib.fe_oracle_float_to_bf16.argtypes = [ctypes.c_float]
@@ -97,7 +97,7 @@ def copy_blocks(k_pools, v_pools, src, dst, ntok, page, width):
 def rope(q, k, pos, cache, dtype):
     """RoPE restated (src/cuda_kernels.cu:19-23) on uint16 bit arrays
     q [rows, hq, dim] and k [rows, hkv, dim] (returned rotated copies);
-    cache: float32 [max_positions, dim]."""
+    cache: float32 [max_positions, rotary_dim] (cos | sin), rotary_dim <= dim."""
     q = np.ascontiguousarray(q, dtype=np.uint16).copy()
     k = np.ascontiguousarray(k, dtype=np.uint16).copy()
     pos = _i64(pos)
@@ -105,7 +105,7 @@ def rope(q, k, pos, cache, dtype):
     rows, hkv, dim = k.shape
     hq = q.shape[1] if q.ndim == 3 else 0
     c_oracle().fe_oracle_rope(_ptr(q), _ptr(k), _ptr(pos), _ptr(cache), rows, hq, hkv, dim,
-                              cache.shape[0], dtype)
+                              cache.shape[1], cache.shape[0], dtype)
     return q, k
 
 

@@ -126,18 +126,20 @@ void fe_oracle_append(const uint16_t* k, const uint16_t* v, uint16_t* kc, uint16
 /* ---- rotary embedding -------------------------------------------------- */
 
 /* Restates src/cuda_kernels.cu:19-23 (rope_kernel): q [rows, hq, dim] and
- * k [rows, hkv, dim] rotated in place; for each head and j < dim/2, with
- * c = cache[pos*dim + j] and s = cache[pos*dim + dim/2 + j],
- * x[j] = a*c - b*s, x[j + dim/2] = b*c + a*s, every product and sum rounded
+ * k [rows, hkv, dim] rotated in place; with half = rot/2, for each head and
+ * j < half, c = cache[pos*rot + j] and s = cache[pos*rot + half + j],
+ * x[j] = a*c - b*s, x[j + half] = b*c + a*s, every product and sum rounded
  * to float separately (this file is compiled with -ffp-contract=off), the
- * result rounded to the 16-bit type. Rows whose position is outside
+ * result rounded to the 16-bit type; dims >= rot are left as they are (rot =
+ * dim for the reference's rope, rot < dim for the partial rotary of
+ * src/hybrid_model.cpp:44). Rows whose position is outside
  * [0, max_positions) are left unchanged (the product skips them too). */
 void fe_oracle_rope(uint16_t* q, uint16_t* k, const int64_t* pos, const float* cache, int rows,
-                    int hq, int hkv, int dim, int max_positions, int dtype) {
-  const int half = dim / 2;
+                    int hq, int hkv, int dim, int rot, int max_positions, int dtype) {
+  const int half = rot / 2;
   for (int row = 0; row < rows; ++row) {
     if (pos[row] < 0 || pos[row] >= max_positions) continue;
-    const float* cs = cache + pos[row] * dim;
+    const float* cs = cache + pos[row] * rot;
     for (int head = 0; head < hq + hkv; ++head) {
       uint16_t* base = head < hq ? q + ((int64_t)row * hq + head) * dim
                                  : k + ((int64_t)row * hkv + (head - hq)) * dim;

@@ -40,6 +40,23 @@ def test_oracle_rope_matches_float32_numpy(dtype):
     np.testing.assert_array_equal(ko, numpy_rope(k, pos, cache, dtype))
 
 
+@pytest.mark.parametrize("rot", [32, 64, 0])
+def test_oracle_partial_rope_matches_float32_numpy(rot):
+    """Partial rotary (src/hybrid_model.cpp:44): the leading `rot` dims rotate
+    with a [positions, rot] cache, the rest pass through."""
+    rng = np.random.default_rng(rot + 1)
+    rows, hq, hkv, dim, max_pos = 9, 4, 2, 128, 512
+    cache = rope_cache(max_pos, rot) if rot else np.zeros((max_pos, 0), np.float32)
+    q = oracle.from_float(rng.standard_normal((rows, hq, dim)).astype(np.float32), 1)
+    k = oracle.from_float(rng.standard_normal((rows, hkv, dim)).astype(np.float32), 1)
+    pos = rng.integers(0, max_pos, rows)
+    qo, ko = oracle.rope(q, k, pos, cache, 1)
+    for x, xo in ((q, qo), (k, ko)):
+        np.testing.assert_array_equal(xo[..., rot:], x[..., rot:])
+        if rot:
+            np.testing.assert_array_equal(xo[..., :rot], numpy_rope(x[..., :rot], pos, cache, 1))
+
+
 def test_oracle_rope_skips_out_of_range_positions():
     rng = np.random.default_rng(1)
     cache = rope_cache(64, 128)
