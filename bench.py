@@ -169,16 +169,26 @@ def is_decode(config):
     return config in ("c2", "c5")
 
 
-def attention_flops(w, md):
+def attention_flops(w, md, select=None):
     """Useful FLOPs of one attention launch: 4 * hq * head_dim per visible
-    (query row, key) pair (QK^T and PV), with the workload's mask."""
+    (query row, key) pair (QK^T and PV), with the workload's mask; `select`
+    (bool per sequence) restricts the sum."""
     lengths = md.lengths(w.page).astype(np.int64)
     q = (md.qo[1:] - md.qo[:-1]).astype(np.int64)
     if w.causal:
         pairs = q * (lengths - q + 1) + q * (q - 1) // 2
     else:
         pairs = q * lengths
+    if select is not None:
+        pairs = pairs[select]
     return float(4 * w.hq * w.dim * int(pairs.sum()))
+
+
+def decode_rows_mask(w, md):
+    """Sequences served by the decode kernel: query rows x GQA group <= 16
+    (the rest run on the tcgen05 kernel)."""
+    q = (md.qo[1:] - md.qo[:-1]).astype(np.int64)
+    return q * (w.hq // w.hkv) <= 16
 
 
 class DecodeState:
@@ -235,6 +245,12 @@ def run_ours(args, rank, world, local):
         cow = tuple(torch.from_numpy(np.asarray(x, np.int32)).cuda() for x in w.cow)
 
     attn_ev = []
+    md0 = w.metadata(0)
+    dmask0 = decode_rows_mask(w, md0)
+    # a step with both decode rows and multi-row sequences is timed in two
+    # parts (decode kernel + merge, then the tcgen05 kernel): the same kernels
+    # in the same order as one fe_attn_run, with an event between them
+    mixed = (not is_decode(args.config)) and bool(dmask0.any()) and bool((~dmask0).any())
 
     def step(s, record=False, host_io=None):
         md = w.metadata(s if decode else 0)
@@ -255,13 +271,21 @@ def run_ours(args, rank, world, local):
                        md.rows, w.width, w.bf16, stream, w.cache_slots)
             if record:
                 e0 = torch.cuda.Event(enable_timing=True)
+                em = torch.cuda.Event(enable_timing=True) if mixed else None
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-            plan.attention(st.q[layer], st.kpools[p], st.vpools[p], st.out[layer], w.causal,
-                           stream)
+            if record and mixed:
+                plan.attention(st.q[layer], st.kpools[p], st.vpools[p], st.out[layer], w.causal,
+                               stream, lists=fekv._lib.FE_ATTN_LISTS_DECODE)
+                em.record(stream)
+                plan.attention(st.q[layer], st.kpools[p], st.vpools[p], st.out[layer], w.causal,
+                               stream, lists=fekv._lib.FE_ATTN_LISTS_ROWS)
+            else:
+                plan.attention(st.q[layer], st.kpools[p], st.vpools[p], st.out[layer], w.causal,
+                               stream)
             if record:
                 e1.record(stream)
-                attn_ev.append((e0, e1))
+                attn_ev.append((e0, em, e1))
         if host_io is not None:
             host_io["d2h"]()
         return md
@@ -282,17 +306,26 @@ def run_ours(args, rank, world, local):
     t1 = torch.cuda.Event(enable_timing=True)
     keys = 0
     flops = 0.0
+    rows_flops = 0.0
+    dec_keys = 0
+    dec_qrows = 0
     t0.record(stream)
     for i in range(args.steps):
         md = step(args.warmup + i, record=True)
         lengths = md.lengths(w.page)
         keys += int(lengths.sum())
         flops += attention_flops(w, md)
+        dm = decode_rows_mask(w, md)
+        rows_flops += attention_flops(w, md, ~dm)
+        dec_keys += int(lengths[dm].sum())
+        dec_qrows += int((md.qo[1:] - md.qo[:-1])[dm].sum())
     t1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = t0.elapsed_time(t1)
-    attn_ms = [a.elapsed_time(b) for a, b in attn_ev]
+    attn_ms = [a.elapsed_time(b) for a, _, b in attn_ev]
+    dec_part_ms = [a.elapsed_time(m) for a, m, _ in attn_ev] if mixed else [0.0]
+    rows_part_ms = [m.elapsed_time(b) for _, m, b in attn_ev] if mixed else [0.0]
     barrier(world)
 
     # algorithmic bytes / FLOPs of one attention launch (averaged over steps)
@@ -301,6 +334,12 @@ def run_ours(args, rank, world, local):
     attn_avg_ms = float(np.mean(attn_ms))
     achieved_gbs = per_launch_bytes / (attn_avg_ms * 1e-3) / 1e9
     achieved_tflops = per_launch_flops / (attn_avg_ms * 1e-3) / 1e12
+    rows_ms = float(np.mean(rows_part_ms))
+    dec_ms = float(np.mean(dec_part_ms))
+    rows_tflops = (rows_flops / args.steps) / (rows_ms * 1e-3) / 1e12 if mixed else 0.0
+    dec_bytes = ((dec_keys / args.steps) * 2 * w.width * 2 +
+                 2 * (dec_qrows / args.steps) * w.hq * w.dim * 2)
+    dec_gbs = dec_bytes / (dec_ms * 1e-3) / 1e9 if mixed else 0.0
 
     # end-to-end through the C ABI with host buffers: per step, H2D of every
     # layer's q/k/v from pinned memory and D2H of every layer's output.
@@ -331,7 +370,14 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
 
-    stats = gather_floats([ms, e2e_ms, attn_avg_ms, achieved_gbs, keys, achieved_tflops], world)
+    # this repo's kernels per layer-step: the append, the decode kernel and its
+    # split-K merge when the step has decode rows, the tcgen05 kernel when it
+    # has multi-row sequences
+    inf = plan.info()
+    launches_per_layer = (1 + (1 if inf["decode_items"] else 0) +
+                          (1 if inf["split_sequences"] else 0) + (1 if inf["prefill_items"] else 0))
+    stats = gather_floats([ms, e2e_ms, attn_avg_ms, achieved_gbs, keys, achieved_tflops,
+                           rows_ms, rows_tflops, dec_ms, dec_gbs], world)
     plan.close()
     if rank != 0:
         return None
@@ -378,7 +424,7 @@ def run_ours(args, rank, world, local):
         "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": int(d2h_bytes),
                 "steps": args.e2e_steps},
-        "gpu_launches": 2 * w.layers * args.steps,
+        "gpu_launches": launches_per_layer * w.layers * args.steps,
         "clocks": clk,
     }
     if not decode:
@@ -397,11 +443,28 @@ def run_ours(args, rank, world, local):
         line["roofline"] = {
             "bound": "tensor", "achieved": round(float(stats[0, 5]), 2), "peak": tpeak,
             "unit": "TFLOP/s", "frac": round(float(stats[0, 5]) / tpeak, 4), "peak_kind": tkind,
-            "kernel": "paged attention (tcgen05 prefill/verify + decode rows)",
+            "kernel": "paged_prefill_tc_kernel",
             "algorithmic_flops_per_launch": per_launch_flops,
             "avg_launch_ms": round(float(stats[0, 2]), 5), "traffic": None,
         }
-        line["gpu_launches"] = (2 + (1 if w.name == "C3" else 0)) * w.layers * args.steps + (
+        if mixed:
+            # the step's multi-row sequences on the tcgen05 kernel, and its
+            # decode rows on the decode kernel, each against its own roof
+            line["roofline"].update({
+                "achieved": round(float(stats[0, 7]), 2),
+                "frac": round(float(stats[0, 7]) / tpeak, 4),
+                "algorithmic_flops_per_launch": rows_flops / args.steps,
+                "avg_launch_ms": round(float(stats[0, 6]), 5),
+            })
+            line["roofline_decode_rows"] = {
+                "bound": "hbm", "achieved": round(float(stats[0, 9]), 1), "peak": peak,
+                "unit": "GB/s", "frac": round(float(stats[0, 9]) / peak, 4),
+                "peak_kind": peak_kind, "kernel": "paged_decode_kernel + decode_merge_kernel",
+                "algorithmic_bytes_per_launch": dec_bytes,
+                "avg_launch_ms": round(float(stats[0, 8]), 5),
+            }
+            line["attention_call_tflops"] = round(float(achieved_tflops), 2)
+        line["gpu_launches"] = launches_per_layer * w.layers * args.steps + (
             args.steps if w.cow is not None else 0)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w, args)

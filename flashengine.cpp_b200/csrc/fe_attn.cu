@@ -322,6 +322,11 @@ int fe_attn_plan_prepare(fe_attn_plan* p, const int32_t* qo, const int32_t* kv,
 
 int fe_attn_run(fe_attn_plan* p, const void* q, const void* k_pool, const void* v_pool, void* out,
                 int causal, void* stream) {
+  return fe_attn_run_lists(p, q, k_pool, v_pool, out, causal, FE_ATTN_LISTS_ALL, stream);
+}
+
+int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const void* v_pool,
+                      void* out, int causal, int lists, void* stream) {
   if (!p) return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_run: plan is null");
   if (p->host_only) return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_run: host-only plan");
   if (!p->prepared) return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_run: plan not prepared");
@@ -329,8 +334,10 @@ int fe_attn_run(fe_attn_plan* p, const void* q, const void* k_pool, const void* 
   // A plan prepared for graph capture launches both kernels at full width
   // every time (CTAs without work exit at once), so the captured launches
   // stay valid for any later metadata.
-  const int grid_rows = p->fixed_grid ? p->cfg.grid_cap : p->grid_view[view];
-  const int grid_dec = p->fixed_grid ? p->cfg.dec_grid_cap : p->grid_view[2];
+  const int grid_rows =
+      (lists & FE_ATTN_LISTS_ROWS) ? (p->fixed_grid ? p->cfg.grid_cap : p->grid_view[view]) : 0;
+  const int grid_dec =
+      (lists & FE_ATTN_LISTS_DECODE) ? (p->fixed_grid ? p->cfg.dec_grid_cap : p->grid_view[2]) : 0;
   if (grid_rows == 0 && grid_dec == 0) return FE_OK;
   if (!q || !k_pool || !v_pool || !out)
     return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_run: null pointer");

@@ -34,6 +34,10 @@ FE_DEVERR_POS_RANGE = 0x20
 
 FE_MAX_LAYERS = 128
 
+FE_ATTN_LISTS_DECODE = 1
+FE_ATTN_LISTS_ROWS = 2
+FE_ATTN_LISTS_ALL = 3
+
 # Every function the header declares, with (restype, argtypes).
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -51,6 +55,7 @@ SIGNATURES = {
     "fe_attn_plan_destroy": (_I, [_P]),
     "fe_attn_plan_prepare": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "fe_attn_run": (_I, [_P, _P, _P, _P, _P, _I, _P]),
+    "fe_attn_run_lists": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
     "fe_attn_plan_get_info": (_I, [_P, _P]),
     "fe_attn_plan_create_host": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
     "fe_attn_plan_debug_meta": (_I, [_P, _P, _I64, ctypes.POINTER(_I64)]),

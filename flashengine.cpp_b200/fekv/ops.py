@@ -201,9 +201,16 @@ class AttentionPlan:
                                             last.ctypes.data_as(_P), batch, rows, int(bool(graph)),
                                             _stream(stream)), "prepare_plan")
 
-    def attention(self, q, k, v, out, causal=True, stream=None):
-        check(self.lib.fe_attn_run(self.handle, _ptr(q), _ptr(k), _ptr(v), _ptr(out),
-                                   int(bool(causal)), _stream(stream)), "attention")
+    def attention(self, q, k, v, out, causal=True, stream=None, lists=None):
+        """fe_attn_run; `lists` (FE_ATTN_LISTS_DECODE / _ROWS) runs only part
+        of the prepared work (fe_attn_run_lists)."""
+        if lists is None:
+            check(self.lib.fe_attn_run(self.handle, _ptr(q), _ptr(k), _ptr(v), _ptr(out),
+                                       int(bool(causal)), _stream(stream)), "attention")
+        else:
+            check(self.lib.fe_attn_run_lists(self.handle, _ptr(q), _ptr(k), _ptr(v), _ptr(out),
+                                             int(bool(causal)), int(lists), _stream(stream)),
+                  "attention")
 
     def info(self) -> dict:
         inf = _lib.PlanInfo()

@@ -193,6 +193,17 @@ int fe_attn_plan_prepare(fe_attn_plan* plan, const int32_t* qo, const int32_t* k
 int fe_attn_run(fe_attn_plan* plan, const void* q, const void* k_pool, const void* v_pool,
                 void* out, int causal, void* stream);
 
+/* fe_attn_run restricted to some of the prepared work: FE_ATTN_LISTS_DECODE
+ * (the rows that run on the decode kernel, and their split-K merge) and/or
+ * FE_ATTN_LISTS_ROWS (multi-row sequences on the tcgen05 kernel).
+ * fe_attn_run is FE_ATTN_LISTS_ALL. Calling the two parts back to back on one
+ * stream does the same work as one fe_attn_run (used to time each kernel). */
+#define FE_ATTN_LISTS_DECODE 1
+#define FE_ATTN_LISTS_ROWS 2
+#define FE_ATTN_LISTS_ALL 3
+int fe_attn_run_lists(fe_attn_plan* plan, const void* q, const void* k_pool, const void* v_pool,
+                      void* out, int causal, int lists, void* stream);
+
 /* Decode attention that allocates nothing. No counterpart in the reference:
  * it is for callers that cannot call cudaMalloc on their path (code running
  * under CUDA stream capture, hosts that give all device memory to their own

@@ -150,6 +150,30 @@ def test_c3_layer_full_size(fk):
     assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, (res, info)
 
 
+def test_run_lists_parts_equal_one_call(fk):
+    """fe_attn_run_lists(decode) then (rows) writes exactly what one fe_attn_run
+    does (C3: decode rows and prefill chunks in one step)."""
+    import torch
+    import fekv.workloads as wl
+    w = wl.c3(seed=1)
+    md = w.metadata()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    kc = torch.randn(w.cache_slots, w.width, generator=g, device="cuda").to(torch.bfloat16)
+    vc = torch.randn(w.cache_slots, w.width, generator=g, device="cuda").to(torch.bfloat16)
+    q = torch.randn(md.rows, w.hq, w.dim, generator=g, device="cuda").to(torch.bfloat16)
+    plan = fk.AttentionPlan(w.hq, w.hkv, w.dim, w.page, md.batch, w.max_pages(), True,
+                            w.num_blocks)
+    plan.prepare(md.qo, md.kv, md.pages, md.last)
+    one, parts = torch.empty_like(q), torch.full_like(q, float("nan"))
+    plan.attention(q, kc, vc, one, w.causal)
+    plan.attention(q, kc, vc, parts, w.causal, lists=fk._lib.FE_ATTN_LISTS_DECODE)
+    plan.attention(q, kc, vc, parts, w.causal, lists=fk._lib.FE_ATTN_LISTS_ROWS)
+    torch.cuda.synchronize()
+    plan.close()
+    assert torch.equal(one.view(torch.int16), parts.view(torch.int16))
+
+
 def test_c4_layer_full_size(fk):
     import fekv.workloads as wl
     res, info = _full_size(fk, wl.c4(seed=0))
