@@ -27,7 +27,7 @@ int decode_launch(int dtype, int heads, const CUtensorMap& kmap, const CUtensorM
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
 int decode_merge_launch(int dtype, const void* args, int grid, cudaStream_t stream);
 int prefill_tc_launch(int dtype, const CUtensorMap& kmap, const CUtensorMap& vmap,
-                      const void* args, int grid, cudaStream_t stream);
+                      const CUtensorMap& qmap, const void* args, int grid, cudaStream_t stream);
 
 namespace {
 
@@ -86,6 +86,17 @@ int encode_tc_map(CUtensorMap* map, const void* pool, int dtype, int hkv, int64_
   const cuuint64_t strides[3] = {cuuint64_t(hkv) * 256, 128, cuuint64_t(hkv) * 256 * 8};
   const cuuint32_t box[4] = {64, 8, 2, 2};
   return encode_nd(map, pool, dtype, 4, dims, strides, box);
+}
+
+// tcgen05 row kernel, queries: q [rows][hq][128] viewed as [rows][hq][128]
+// with box (128/G rows) x (G heads) x 64 elements: one box is the 64-dim half
+// of a 128-row packed Q tile (packed row p = query row p / G, head p % G of
+// the KV head's group), landing in packed-row order.
+int encode_q_map(CUtensorMap* map, const void* q, int dtype, int hq, int rows, int G) {
+  const cuuint64_t dims[3] = {128, cuuint64_t(hq), cuuint64_t(rows)};
+  const cuuint64_t strides[2] = {256, cuuint64_t(hq) * 256};
+  const cuuint32_t box[3] = {64, cuuint32_t(G), cuuint32_t(128 / G)};
+  return encode_nd(map, q, dtype, 3, dims, strides, box);
 }
 
 // Row kernel: pool viewed as [cache_slots][hkv*2][64] (64-element head-half
@@ -363,16 +374,20 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
     if (rc != FE_OK) return rc;
     p->vmap_ptr = v_pool;
   }
+  MetaHeader h;
+  std::memcpy(&h, p->last.meta.data(), sizeof(h));
   // split units of the decode list are merged by a second, dependent kernel
   int grid_merge = 0;
-  if (grid_dec > 0) {
-    if (p->fixed_grid) {
-      grid_merge = p->cfg.dec_grid_cap;
-    } else {
-      MetaHeader h;
-      std::memcpy(&h, p->last.meta.data(), sizeof(h));
-      grid_merge = h.n_groups[2];
-    }
+  if (grid_dec > 0) grid_merge = p->fixed_grid ? p->cfg.dec_grid_cap : h.n_groups[2];
+  // the row kernel's Q tiles come from a tensor map over this call's q
+  // (the prepared step's query rows, which a graph plan keeps fixed)
+  CUtensorMap qmap;
+  std::memset(&qmap, 0, sizeof(qmap));  // unused when G does not divide 128
+  int q_map_rows = 0;
+  if (grid_rows > 0 && 128 % (p->cfg.hq / p->cfg.hkv) == 0 && h.rows > 0) {
+    int rc = encode_q_map(&qmap, q, p->dtype, p->cfg.hq, h.rows, p->cfg.hq / p->cfg.hkv);
+    if (rc != FE_OK) return rc;
+    q_map_rows = h.rows;
   }
   const float scale_log2 = 1.4426950408889634f / sqrtf(float(p->cfg.dim));
   auto s = static_cast<cudaStream_t>(stream);
@@ -382,27 +397,28 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
   if (p->dtype == FE_DTYPE_BF16) {
     AttnArgs<__nv_bfloat16> a{p->d_meta, static_cast<const __nv_bfloat16*>(q),
                               static_cast<__nv_bfloat16*>(out), p->d_partials, p->d_counters,
-                              device_error_word(), p->cfg.hq, G, p->cfg.page, view, scale_log2};
+                              device_error_word(), p->cfg.hq, G, p->cfg.page, view, scale_log2,
+                              q_map_rows};
     if (grid_dec > 0) {
       int rc = decode_launch(p->dtype, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
       if (rc == FE_OK) rc = decode_merge_launch(p->dtype, &a, grid_merge, s);
       if (rc != FE_OK) return rc;
     }
     if (grid_rows > 0) {
-      int rc = prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, &a, grid_rows, s);
+      int rc = prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, qmap, &a, grid_rows, s);
       if (rc != FE_OK) return rc;
     }
   } else {
     AttnArgs<__half> a{p->d_meta, static_cast<const __half*>(q), static_cast<__half*>(out),
                        p->d_partials, p->d_counters, device_error_word(), p->cfg.hq, G,
-                       p->cfg.page, view, scale_log2};
+                       p->cfg.page, view, scale_log2, q_map_rows};
     if (grid_dec > 0) {
       int rc = decode_launch(p->dtype, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
       if (rc == FE_OK) rc = decode_merge_launch(p->dtype, &a, grid_merge, s);
       if (rc != FE_OK) return rc;
     }
     if (grid_rows > 0) {
-      int rc = prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, &a, grid_rows, s);
+      int rc = prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, qmap, &a, grid_rows, s);
       if (rc != FE_OK) return rc;
     }
   }

@@ -27,6 +27,7 @@ struct AttnArgs {
   unsigned int* err;
   int hq, G, page, view;
   float scale_log2;
+  int q_map_rows;  // query rows the row kernel's Q tensor map covers (0: none)
 };
 
 __device__ __forceinline__ uint64_t global_ns() {

@@ -10,11 +10,14 @@
 // 128 packed query rows (row p = query row p / G, head kvh*G + p % G) of one
 // sequence and KV head against a range of keys, processed in 128-key tiles.
 //  warps 8/11 producers of K / of V: gather each key tile (eight 16-token
-//             page pieces, one 4 KiB TMA box each) into 3-stage rings (32 KiB
-//             of K or of V per stage); a K stage is released when its S MMA
-//             completed, a V stage when its PV did, so K runs ahead of V. The
-//             page ids of the next 32 pieces are fetched ahead by the warp's
-//             lanes.
+//             page pieces, one 4 KiB TMA box each) into a 2-stage K ring and a
+//             3-stage V ring (32 KiB per stage); a K stage is released when its
+//             S MMA completed, a V stage when its PV did. The page ids of the
+//             next 32 pieces are fetched ahead by the warp's lanes. The K
+//             producer also loads each item's Q tile with two TMA boxes (query
+//             rows x GQA heads x 64 dims, which lands in packed-row order) into
+//             one of two Q buffers, as soon as the item two back has released
+//             it, so S of the next item starts while the current one finishes.
 //  warp 9     S issuer (one thread) and TMEM owner (512 columns):
 //               S_t = Q K_t^T (M = 128, N = 128, K = 128, both operands in
 //                     shared memory) into one of three 128-column TMEM slots,
@@ -44,7 +47,7 @@
 namespace fe {
 
 int prefill_tc_launch(int dtype, const CUtensorMap& kmap, const CUtensorMap& vmap,
-                      const void* args, int grid, cudaStream_t stream);
+                      const CUtensorMap& qmap, const void* args, int grid, cudaStream_t stream);
 int prefill_tc_smem_bytes();
 
 namespace {
@@ -53,25 +56,27 @@ constexpr int kTcM = 128;                   // packed rows per work item
 constexpr int kTcN = 128;                   // keys per tile (S MMA N)
 constexpr int kHalfN = kTcN / 2;            // keys per softmax group and tile
 constexpr int kPiecesPerTile = kTcN / kTileTokens;
-constexpr int kTcStages = 3;
+constexpr int kKStages = 2;
+constexpr int kVStages = 3;
 constexpr int kTcThreads = 12 * 32;         // 3 warpgroups: softmax 0, softmax 1, producers/MMA
 constexpr int kProducerWarp = 8, kMmaWarp = 9, kPvWarp = 10, kVProducerWarp = 11;
 constexpr int kQHalf = kTcM * 128;          // 16 KiB: 128 rows x 64 dims
-// A stage holds the K tile then the V tile, each as eight 4 KiB pieces laid
-// out [8-key group][head-half][8 rows x 128 B] (swizzled 1 KiB atoms): the
-// 8-key groups of one head-half are 2 KiB apart, the two halves 1 KiB apart.
+constexpr int kQBytes = 2 * kQHalf;         // one Q tile
+// A K (or V) stage holds one tile as eight 4 KiB pieces laid out
+// [8-key group][head-half][8 rows x 128 B] (swizzled 1 KiB atoms): the 8-key
+// groups of one head-half are 2 KiB apart, the two halves 1 KiB apart.
 constexpr int kPieceBytes = kTileTokens * 256;  // 16 keys x 128 dims x 2 B
 constexpr int kKVTile = kPiecesPerTile * kPieceBytes;  // 32 KiB
-constexpr int kKVStage = 2 * kKVTile;                   // K tile, V tile
-constexpr int kOffQ = 0;
-constexpr int kOffKV = 2 * kQHalf;
-constexpr int kOffX = kOffKV + kTcStages * kKVStage;    // half-row maxima
+constexpr int kOffQ = 0;                                // two Q tiles
+constexpr int kOffK = 2 * kQBytes;
+constexpr int kOffV = kOffK + kKStages * kKVTile;
+constexpr int kOffX = kOffV + kVStages * kKVTile;       // half-row maxima
 constexpr int kXBytes = 2 * 2 * kTcM * 4;               // [tile parity][group][128 rows]
 constexpr int kOffBar = kOffX + kXBytes;
 constexpr int kSlots = 3;
-// q_full, o_free, l_done, k_full[3], v_full[3], k_empty[3], v_empty[3],
-// s_full[3], s_free[3], p_full[3][2], mma_drain, xmax[2][4]
-constexpr int kNumBars = 3 + 4 * kTcStages + kSlots + kSlots + 2 * kSlots + 1 + 8;
+// q_full[2], q_empty[2], o_free, l_done, k_full[2], k_empty[2], v_full[3],
+// v_empty[3], s_full[3], s_free[3], p_full[3][2], mma_drain, xmax[2][4]
+constexpr int kNumBars = 4 + 2 + 2 * kKStages + 2 * kVStages + kSlots + kSlots + 2 * kSlots + 1 + 8;
 // The dynamic shared memory base is 1 KiB aligned (no static shared memory;
 // checked at entry), as the 128-byte swizzle atoms require.
 constexpr int kTcSmem = kOffBar + kNumBars * 8 + 32;
@@ -127,18 +132,20 @@ __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volati
 template <typename T>
 __global__ void __launch_bounds__(kTcThreads, 1)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
-                            const __grid_constant__ CUtensorMap vmap, const AttnArgs<T> a) {
+                            const __grid_constant__ CUtensorMap vmap,
+                            const __grid_constant__ CUtensorMap qmap, const AttnArgs<T> a) {
   // declared 16-byte aligned so that the 1 KiB check below is not folded away
   extern __shared__ __align__(16) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* q_full = bars + 0;
-  uint64_t* o_free = bars + 1;
-  uint64_t* l_done = bars + 2;
-  uint64_t* k_full = bars + 3;
-  uint64_t* v_full = k_full + kTcStages;
-  uint64_t* k_empty = v_full + kTcStages;
-  uint64_t* v_empty = k_empty + kTcStages;
-  uint64_t* s_full = v_empty + kTcStages;   // [slot]: S written
+  uint64_t* q_full = bars + 0;   // [buffer]: Q tile landed
+  uint64_t* q_empty = bars + 2;  // [buffer]: both groups done with the item
+  uint64_t* o_free = bars + 4;
+  uint64_t* l_done = bars + 5;
+  uint64_t* k_full = bars + 6;
+  uint64_t* k_empty = k_full + kKStages;
+  uint64_t* v_full = k_empty + kKStages;
+  uint64_t* v_empty = v_full + kVStages;
+  uint64_t* s_full = v_empty + kVStages;    // [slot]: S written
   // s_free[slot] completes when the PV that read the slot's P has completed,
   // and with it every MMA the PV thread issued before.
   uint64_t* s_free = s_full + kSlots;
@@ -148,9 +155,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 2);
   float* xmax = reinterpret_cast<float*>(smem + kOffX);  // [parity][group][row]
-  // Row weight sums at the end of an item go to the Q tile (dead by then):
-  // [group][row]; group 0 reloads Q only after both groups read them.
-  float* xsum = reinterpret_cast<float*>(smem + kOffQ);
+  // Row weight sums at the end of an item go to the item's Q buffer (dead by
+  // then, [group][row]); the buffer is released for the item two ahead only
+  // after both groups have read them.
 
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -169,13 +176,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 128);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&q_full[b], 1);
+      mbar_init(&q_empty[b], 8);  // one arrival per softmax warp
+    }
     mbar_init(o_free, 256);
     mbar_init(l_done, 256);
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       mbar_init(&k_full[s], 1);
-      mbar_init(&v_full[s], 1);
       mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
     for (int s = 0; s < kSlots; ++s) {
@@ -210,13 +222,65 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const CUtensorMap* map = is_v ? &vmap : &kmap;
     uint64_t* full = is_v ? v_full : k_full;
     uint64_t* empty = is_v ? v_empty : k_empty;
-    uint8_t* region = smem + kOffKV + (is_v ? kKVTile : 0);
-    if (lane == 0) prefetch_tensormap(map);
+    const int stages = is_v ? kVStages : kKStages;
+    uint8_t* region = smem + (is_v ? kOffV : kOffK);
+    // Q tiles by TMA when a tile is whole query rows (G divides 128) inside
+    // the rows the Q map covers, else by the warp's lanes
+    const bool q_tma = (kTcM % a.G) == 0 && a.q_map_rows > 0;
+    if (lane == 0) {
+      prefetch_tensormap(map);
+      if (!is_v && q_tma) prefetch_tensormap(&qmap);
+    }
     uint32_t g = 0;
-    for (int it = it0; it < it1 && !aborted; ++it) {
+    int unit = 0;
+    for (int it = it0; it < it1 && !aborted; ++it, ++unit) {
       const WorkItem w = items[it];
       const SeqInfo si = seqs[w.seq];
       const int h2 = w.kvh * 2;
+      if (!is_v) {
+        // the item's Q tile: packed row p = query row p / G, head kvh*G + p % G,
+        // i.e. 128/G query rows x G heads x 64 dims per box (rows past the
+        // sequence are other sequences' q or zero fill; their output is
+        // never stored)
+        const int b = unit & 1;
+        uint8_t* dst = smem + kOffQ + b * kQBytes;
+        const int G = a.G, P = si.qrows * G;
+        const bool tma_item =
+            q_tma && si.q_row0 + (min(P, w.rb0 * kRowBlock + kTcM) - 1) / G < a.q_map_rows;
+        int good = 1;
+        if (lane == 0) {
+          if (!wait_or_abort(&q_empty[b], ((unit >> 1) & 1u) ^ 1u, flags, aborted)) {
+            good = 0;
+          } else if (tma_item) {
+            mbar_arrive_expect_tx(&q_full[b], kQBytes);
+            const int row0 = si.q_row0 + (w.rb0 * kRowBlock) / a.G;
+            tma_load_3d(dst, &qmap, &q_full[b], 0, w.kvh * a.G, row0);
+            tma_load_3d(dst + kQHalf, &qmap, &q_full[b], 64, w.kvh * a.G, row0);
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, good, 0)) {
+          aborted = true;
+          break;
+        }
+        if (!tma_item) {
+          // copy with the lanes into the swizzled K-major tile (zeros past the
+          // sequence), then publish
+          for (int i = lane; i < kTcM * 16; i += 32) {
+            const int r = i >> 4, c = i & 15;
+            const int pr = w.rb0 * kRowBlock + r;
+            uint4 val = make_uint4(0, 0, 0, 0);
+            if (pr < P)
+              val = __ldg(reinterpret_cast<const uint4*>(
+                            a.q + (static_cast<int64_t>(si.q_row0 + pr / G) * a.hq + w.kvh * G +
+                                   pr % G) * kHeadDim) + c);
+            const int half = c >> 3, cc = c & 7;
+            *reinterpret_cast<uint4*>(dst + half * kQHalf + r * 128 + ((cc ^ (r & 7)) << 4)) = val;
+          }
+          tc::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&q_full[b]);
+        }
+      }
       const int npieces = w.kt1 - w.kt0;
       const int ntiles = (npieces + kPiecesPerTile - 1) / kPiecesPerTile;
       // Slot of 16-token piece `i` of the item; lanes fetch 32 pieces (4
@@ -234,17 +298,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           nxt = piece_slot(kPiecesPerTile * j + 32 + lane);
         }
         const int pieces = min(kPiecesPerTile, npieces - kPiecesPerTile * j);
-        const int st = g % kTcStages;
+        const int st = g % stages;
         int sl[kPiecesPerTile];
 #pragma unroll
         for (int u = 0; u < kPiecesPerTile; ++u) sl[u] = __shfl_sync(0xffffffffu, cur, pb + u);
         int good = 1;
         if (lane == 0) {
-          if (!wait_or_abort(&empty[st], ((g / kTcStages) & 1u) ^ 1u, flags, aborted)) {
+          if (!wait_or_abort(&empty[st], ((g / stages) & 1u) ^ 1u, flags, aborted)) {
             good = 0;
           } else {
             mbar_arrive_expect_tx(&full[st], pieces * kPieceBytes);
-            uint8_t* dst = region + st * kKVStage;
+            uint8_t* dst = region + st * kKVTile;
             // piece start slots are multiples of 16: coordinates (0, 0,
             // head-half pair, slot / 8)
 #pragma unroll
@@ -263,8 +327,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (aborted) raise_device_error(a.err, FE_DEVERR_TIMEOUT);
       // The last load into each stage has landed before the CTA may exit
       // (consumed stages return at once; bounded for an aborted run).
-      for (uint32_t t = g > kTcStages ? g - kTcStages : 0; t < g; ++t)
-        wait_bounded_short(&full[t % kTcStages], (t / kTcStages) & 1u, flags + 1);
+      for (uint32_t t = g > uint32_t(stages) ? g - stages : 0; t < g; ++t)
+        wait_bounded_short(&full[t % stages], (t / stages) & 1u, flags + 1);
+      if (!is_v && unit > 0) {  // and the last Q tiles
+        for (int u = unit > 2 ? unit - 2 : 0; u < unit; ++u)
+          wait_bounded_short(&q_full[u & 1], (u >> 1) & 1u, flags + 1);
+      }
     }
   } else if (warp == kMmaWarp || warp == kPvWarp) {
     // ------------------------------------------- MMA issuers (S and PV streams)
@@ -280,9 +348,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // K: K-major, 8-key groups 2 KiB apart, dims 64..127 at +1 KiB.
       // V: MN-major, 64-dim halves 1 KiB apart (leading), 8-key groups 2 KiB
       // apart (stride), 16 keys per 4 KiB.
-      const uint64_t q_desc = tc::smem_desc_sw128(smem_u32(smem + kOffQ), 16, 1024);
-      const uint64_t k_desc0 = tc::smem_desc_sw128(smem_u32(smem + kOffKV), 16, 2048);
-      const uint64_t v_desc0 = tc::smem_desc_sw128(smem_u32(smem + kOffKV + kKVTile), 1024, 2048);
+      const uint64_t q_desc0 = tc::smem_desc_sw128(smem_u32(smem + kOffQ), 16, 1024);
+      const uint64_t k_desc0 = tc::smem_desc_sw128(smem_u32(smem + kOffK), 16, 2048);
+      const uint64_t v_desc0 = tc::smem_desc_sw128(smem_u32(smem + kOffV), 1024, 2048);
       const bool s_stream = warp == kMmaWarp;
       uint32_t tbase = 0;  // global index of the item's first tile
       uint32_t n = 0;      // tiles issued (slot and phase)
@@ -293,15 +361,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (s_stream) {
           // S_t = Q K_t^T into the next slot once both PVs that read the
           // slot's P have completed.
-          if (!wait_or_abort(q_full, unit & 1, flags, aborted)) break;
+          if (!wait_or_abort(&q_full[unit & 1], (unit >> 1) & 1u, flags, aborted)) break;
+          const uint64_t q_desc = q_desc0 + uint64_t(((unit & 1) * kQBytes) >> 4);
           for (int t = 0; t < ntiles && !aborted; ++t, ++n) {
             const int slot = n % kSlots;
             const uint32_t tg = tbase + t;
-            const int st = tg % kTcStages;
+            const int st = tg % kKStages;
             if (!wait_or_abort(&s_free[slot], ((n / kSlots) & 1u) ^ 1u, flags, aborted)) break;
-            if (!wait_or_abort(&k_full[st], (tg / kTcStages) & 1u, flags, aborted)) break;
+            if (!wait_or_abort(&k_full[st], (tg / kKStages) & 1u, flags, aborted)) break;
             tc::fence_after_sync();
-            const uint64_t k_desc = k_desc0 + uint64_t((st * kKVStage) >> 4);
+            const uint64_t k_desc = k_desc0 + uint64_t((st * kKVTile) >> 4);
             const uint32_t d = tmem + slot * kTcN;
 #pragma unroll
             for (int kk = 0; kk < kHeadDim / 16; ++kk) {
@@ -318,16 +387,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int j = 0; j < ntiles && !aborted; ++j, ++n) {
             const int slot = n % kSlots;
             const uint32_t tg = tbase + j;
-            const int st = tg % kTcStages;
+            const int st = tg % kVStages;
             if (j == 0 && unit > 0) {
               // O is free once both groups stored the last item's output
               if (!wait_or_abort(o_free, (unit - 1) & 1, flags, aborted)) break;
             }
-            if (!wait_or_abort(&v_full[st], (tg / kTcStages) & 1u, flags, aborted)) break;
+            if (!wait_or_abort(&v_full[st], (tg / kVStages) & 1u, flags, aborted)) break;
             if (!wait_or_abort(&p_full[slot * 2], (n / kSlots) & 1u, flags, aborted)) break;
             if (!wait_or_abort(&p_full[slot * 2 + 1], (n / kSlots) & 1u, flags, aborted)) break;
             tc::fence_after_sync();
-            const uint64_t v_desc = v_desc0 + uint64_t((st * kKVStage) >> 4);
+            const uint64_t v_desc = v_desc0 + uint64_t((st * kKVTile) >> 4);
             const uint32_t d = tmem + kOCol;
 #pragma unroll
             for (int gi = 0; gi < 2; ++gi) {
@@ -377,27 +446,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int P = si.qrows * G;
       const int p = w.rb0 * kRowBlock + r;
       const bool row_valid = p < P;
-      if (gi == 0) {
-        // Q row -> swizzled K-major shared tile (zeros for padding rows); the
-        // previous item's S MMAs have all completed (their S was consumed)
-        // and both groups have read the sums kept in the tile
-        if (unit > 0 && !wait_warp(o_free, (unit - 1) & 1, flags, aborted)) break;
-        const uint4* src = row_valid
-                               ? reinterpret_cast<const uint4*>(
-                                     a.q + (static_cast<int64_t>(si.q_row0 + p / G) * a.hq +
-                                            w.kvh * G + p % G) * kHeadDim)
-                               : nullptr;
-        uint8_t* qrow = smem + kOffQ + r * 128;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const uint4 v = src ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
-          const int half = c >> 3, cc = c & 7;
-          *reinterpret_cast<uint4*>(qrow + half * kQHalf + ((cc ^ (r & 7)) << 4)) = v;
-        }
-        tc::fence_proxy_async_smem();
-        mbar_arrive(q_full);
-      }
-
       const int lim = (causal && row_valid) ? si.length - si.qrows + p / G + 1 : si.length;
       // m_used stays -inf until the first unmasked key (its weights are 0)
       float m_used = -INFINITY, l = 0.f;
@@ -499,9 +547,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int valid = min(si.length - tkey,
                               (npieces - kPiecesPerTile * j) * kTileTokens - gi * kHalfN);
         if (valid < kHalfN) {
-          const int st = tg % kTcStages;
-          if (!wait_warp(&v_full[st], (tg / kTcStages) & 1u, flags, aborted)) break;
-          uint8_t* vb = smem + kOffKV + st * kKVStage + kKVTile;
+          const int st = tg % kVStages;
+          if (!wait_warp(&v_full[st], (tg / kVStages) & 1u, flags, aborted)) break;
+          uint8_t* vb = smem + kOffV + st * kKVTile;
           const int r0 = max(valid, 0);
           const int nch = (kHalfN - r0) * 8;  // 16-byte chunks per head-half
           for (int i = r; i < 2 * nch; i += 128) {
@@ -527,11 +575,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       // Row weight sums of both groups (same max) -> divide and store this
       // group's 64 dims.
+      float* xsum = reinterpret_cast<float*>(smem + kOffQ + (unit & 1) * kQBytes);
       xsum[gi * kTcM + r] = l;
       mbar_arrive(l_done);
       if (!wait_warp(l_done, unit & 1, flags, aborted)) break;
       tc::fence_after_sync();
       const float inv = 1.f / (l + xsum[(gi ^ 1) * kTcM + r]);
+      // the Q buffer (and these sums) may now take the item two ahead
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_empty[unit & 1]);
       T* dst = row_valid ? a.out + (static_cast<int64_t>(si.q_row0 + p / G) * a.hq + w.kvh * G +
                                     p % G) * kHeadDim + gi * 64
                          : nullptr;
@@ -568,8 +620,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 template <typename T>
-int launch_t(const CUtensorMap& kmap, const CUtensorMap& vmap, const AttnArgs<T>& args, int grid,
-             cudaStream_t stream) {
+int launch_t(const CUtensorMap& kmap, const CUtensorMap& vmap, const CUtensorMap& qmap,
+             const AttnArgs<T>& args, int grid, cudaStream_t stream) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
@@ -578,7 +630,7 @@ int launch_t(const CUtensorMap& kmap, const CUtensorMap& vmap, const AttnArgs<T>
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "paged_prefill_tc_kernel attribute");
   FE_CUDA_TRY(launch_pdl(paged_prefill_tc_kernel<T>, dim3(grid), dim3(kTcThreads), kTcSmem, stream,
-                         kmap, vmap, args));
+                         kmap, vmap, qmap, args));
   return FE_OK;
 }
 
@@ -587,11 +639,12 @@ int launch_t(const CUtensorMap& kmap, const CUtensorMap& vmap, const AttnArgs<T>
 int prefill_tc_smem_bytes() { return kTcSmem; }
 
 int prefill_tc_launch(int dtype, const CUtensorMap& kmap, const CUtensorMap& vmap,
-                      const void* args, int grid, cudaStream_t stream) {
+                      const CUtensorMap& qmap, const void* args, int grid, cudaStream_t stream) {
   if (dtype == FE_DTYPE_BF16)
-    return launch_t<__nv_bfloat16>(kmap, vmap,
+    return launch_t<__nv_bfloat16>(kmap, vmap, qmap,
                                    *static_cast<const AttnArgs<__nv_bfloat16>*>(args), grid, stream);
-  return launch_t<__half>(kmap, vmap, *static_cast<const AttnArgs<__half>*>(args), grid, stream);
+  return launch_t<__half>(kmap, vmap, qmap, *static_cast<const AttnArgs<__half>*>(args), grid,
+                          stream);
 }
 
 }  // namespace fe
