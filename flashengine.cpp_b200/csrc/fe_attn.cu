@@ -20,6 +20,7 @@
 #include <string>
 
 #include "fe_attn_common.cuh"
+#include "fe_plan_device.h"
 
 namespace fe {
 
@@ -135,6 +136,7 @@ struct fe_attn_plan {
   size_t meta_cap = 0;
   float* d_partials = nullptr;
   int32_t* d_counters = nullptr;
+  void* d_plan_scratch = nullptr;  // device-side planner (fe_plan_device.cu)
   // pinned staging, double-buffered
   uint8_t* h_meta[2] = {nullptr, nullptr};
   cudaEvent_t h_ev[2] = {nullptr, nullptr};
@@ -142,6 +144,7 @@ struct fe_attn_plan {
   int h_idx = 0;
   // last prepare
   bool prepared = false, fixed_grid = false;
+  bool device_planned = false;  // the last prepare built the lists on the device
   bool graph_shape_set = false;
   int graph_batch = 0, graph_rows = 0;
   PlanResult last;
@@ -224,6 +227,7 @@ void destroy(fe_attn_plan* p) {
     if (p->d_meta) cudaFree(p->d_meta);
     if (p->d_partials) cudaFree(p->d_partials);
     if (p->d_counters) cudaFree(p->d_counters);
+    if (p->d_plan_scratch) cudaFree(p->d_plan_scratch);
   }
   delete p;
 }
@@ -256,6 +260,7 @@ int fe_attn_plan_create(int hq, int hkv, int dim, int page, int max_batch, int m
   if (e == cudaSuccess) e = cudaMalloc(&p->d_counters, sizeof(int32_t) * p->cfg.max_groups);
   if (e == cudaSuccess) e = cudaMemset(p->d_counters, 0, sizeof(int32_t) * p->cfg.max_groups);
   if (e == cudaSuccess) e = cudaMemset(p->d_meta, 0, sizeof(MetaHeader));
+  if (e == cudaSuccess) e = cudaMalloc(&p->d_plan_scratch, plan_device_scratch_bytes(max_batch));
   for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
     e = cudaMallocHost(&p->h_meta[i], p->meta_cap);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->h_ev[i], cudaEventDisableTiming);
@@ -322,12 +327,126 @@ int fe_attn_plan_prepare(fe_attn_plan* p, const int32_t* qo, const int32_t* kv,
   for (int c = 0; c < 3; ++c) p->grid_view[c] = res.grid[c];
   p->last = std::move(res);
   p->prepared = true;
+  p->device_planned = false;
   p->fixed_grid = graph != 0;
   if (graph) {
     p->graph_shape_set = true;
     p->graph_batch = batch;
     p->graph_rows = rows;
   }
+  return FE_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Shared tail of the two device-side prepares: launch the planner, then
+// record on the host only what the launches need (graph-mode grids, the
+// step's batch and rows; the item counts stay on the device).
+int prepare_on_device(fe_attn_plan* p, DevPlanArgs& a, int batch, int rows, void* stream,
+                      const char* what) {
+  if (!p) return fail(FE_ERR_INVALID_ARGUMENT, std::string(what) + ": plan is null");
+  if (p->host_only) return fail(FE_ERR_INVALID_ARGUMENT, std::string(what) + ": host-only plan");
+  if (batch < 0 || rows < 0)
+    return fail(FE_ERR_INVALID_ARGUMENT,
+                std::string(what) + ": batch and rows must be non-negative");
+  if (batch > p->cfg.max_batch)
+    return fail(FE_ERR_CAPACITY, std::string(what) + ": batch exceeds the plan's max_batch");
+  if (p->graph_shape_set && (p->graph_batch != batch || p->graph_rows != rows))
+    return fail(FE_ERR_INVALID_ARGUMENT,
+                std::string(what) + ": graph plan batch/rows changed since capture");
+  const PlanConfig& c = p->cfg;
+  a.batch = batch;
+  a.rows = rows;
+  a.hq = c.hq;
+  a.hkv = c.hkv;
+  a.page = c.page;
+  a.max_batch = c.max_batch;
+  a.max_pages = c.max_pages;
+  a.num_blocks = c.num_blocks;
+  a.dec_heads = c.dec_heads;
+  a.grid_cap = c.grid_cap;
+  a.dec_grid_cap = c.dec_grid_cap;
+  a.max_items = c.max_items;
+  a.max_groups = c.max_groups;
+  a.partial_capacity = c.partial_capacity;
+  a.meta_cap = static_cast<int64_t>(p->meta_cap);
+  a.meta = p->d_meta;
+  a.counters = p->d_counters;
+  a.err = device_error_word();
+  plan_device_bind_scratch(a, p->d_plan_scratch);
+  int rc = plan_device_launch(a, static_cast<cudaStream_t>(stream));
+  if (rc != FE_OK) return rc;
+  PlanResult res;
+  res.meta.assign(sizeof(MetaHeader), 0);
+  MetaHeader h{};
+  h.batch = batch;
+  h.rows = rows;
+  std::memcpy(res.meta.data(), &h, sizeof(h));
+  res.n_items = res.decode_items = res.prefill_items = res.split_units = -1;
+  res.chunk_tiles = -1;
+  res.kv_tokens = -1;
+  p->last = std::move(res);
+  p->grid_view[0] = p->grid_view[1] = c.grid_cap;
+  p->grid_view[2] = c.dec_grid_cap;
+  p->prepared = true;
+  p->device_planned = true;
+  p->fixed_grid = true;
+  p->graph_shape_set = true;
+  p->graph_batch = batch;
+  p->graph_rows = rows;
+  return FE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fe_attn_plan_prepare_device(fe_attn_plan* p, const int32_t* qo, const int32_t* kv,
+                                const int32_t* pages, const int32_t* last, int batch, int rows,
+                                void* stream) {
+  if (batch > 0 && (!qo || !kv || !pages || !last))
+    return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_plan_prepare_device: null metadata pointer");
+  DevPlanArgs a{};
+  a.mode = 0;
+  a.qo = qo;
+  a.kv = kv;
+  a.pages = pages;
+  a.last = last;
+  return prepare_on_device(p, a, batch, rows, stream, "fe_attn_plan_prepare_device");
+}
+
+int fe_step_prepare_device(fe_attn_plan* p, const int32_t* block_tables, int table_stride,
+                           const int32_t* starts, int batch, int rows_per_seq, int64_t* slots,
+                           int64_t* positions, void* stream) {
+  if (rows_per_seq < 1 || table_stride < 1)
+    return fail(FE_ERR_INVALID_ARGUMENT,
+                "fe_step_prepare_device: rows_per_seq and table_stride must be positive");
+  if (batch > 0 && (!block_tables || !starts || !slots || !positions))
+    return fail(FE_ERR_INVALID_ARGUMENT, "fe_step_prepare_device: null pointer");
+  if (int64_t(batch) * rows_per_seq > INT32_MAX / 2)
+    return fail(FE_ERR_CAPACITY, "fe_step_prepare_device: batch * rows_per_seq too large");
+  DevPlanArgs a{};
+  a.mode = 1;
+  a.tables = block_tables;
+  a.stride = table_stride;
+  a.starts = starts;
+  a.rows_per_seq = rows_per_seq;
+  a.slots = slots;
+  a.positions = positions;
+  return prepare_on_device(p, a, batch, batch * rows_per_seq, stream, "fe_step_prepare_device");
+}
+
+// Test hook: copy the plan's device metadata (the lists the kernels read)
+// into host memory `dst`, at most `cap` bytes; synchronises `stream`.
+int fe_attn_plan_debug_device_meta(const fe_attn_plan* p, void* dst, int64_t cap, void* stream) {
+  if (!p || !dst) return fail(FE_ERR_INVALID_ARGUMENT, "null pointer");
+  if (p->host_only) return fail(FE_ERR_INVALID_ARGUMENT, "host-only plan");
+  const size_t n = static_cast<size_t>(std::min<int64_t>(cap, static_cast<int64_t>(p->meta_cap)));
+  auto s = static_cast<cudaStream_t>(stream);
+  FE_CUDA_TRY(cudaMemcpyAsync(dst, p->d_meta, n, cudaMemcpyDeviceToHost, s));
+  FE_CUDA_TRY(cudaStreamSynchronize(s));
   return FE_OK;
 }
 
@@ -432,6 +551,7 @@ int fe_attn_plan_get_info(const fe_attn_plan* p, fe_attn_plan_info* info) {
   if (!p->prepared) return FE_OK;
   MetaHeader h;
   std::memcpy(&h, p->last.meta.data(), sizeof(h));
+  // after a device-side prepare the counts stay on the device: they read -1
   info->batch = h.batch;
   info->rows = h.rows;
   info->decode_items = p->last.decode_items;

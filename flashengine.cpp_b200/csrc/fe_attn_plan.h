@@ -95,6 +95,12 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
                const int32_t* last, int batch, int rows, bool fixed_grid, PlanResult& out,
                std::string& err);
 
-inline int partial_rec_floats(int rows) { return ((rows * (kHeadDim + 2)) + 3) & ~3; }
+#ifdef __CUDACC__
+#define FE_HOST_DEVICE __host__ __device__
+#else
+#define FE_HOST_DEVICE
+#endif
+
+FE_HOST_DEVICE inline int partial_rec_floats(int rows) { return ((rows * (kHeadDim + 2)) + 3) & ~3; }
 
 }  // namespace fe

@@ -31,6 +31,7 @@ FE_DEVERR_NTOK_RANGE = 0x4
 FE_DEVERR_TIMEOUT = 0x8
 FE_DEVERR_SMEM_ALIGN = 0x10
 FE_DEVERR_POS_RANGE = 0x20
+FE_DEVERR_PLAN = 0x40
 
 FE_MAX_LAYERS = 128
 
@@ -59,6 +60,9 @@ SIGNATURES = {
     "fe_attn_plan_get_info": (_I, [_P, _P]),
     "fe_attn_plan_create_host": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
     "fe_attn_plan_debug_meta": (_I, [_P, _P, _I64, ctypes.POINTER(_I64)]),
+    "fe_attn_plan_prepare_device": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
+    "fe_step_prepare_device": (_I, [_P, _P, _I, _P, _I, _I, _P, _P, _P]),
+    "fe_attn_plan_debug_device_meta": (_I, [_P, _P, _I64, _P]),
     "fe_paged_decode_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
     "fe_rope": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
     "fe_rope_append": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I64,

@@ -53,6 +53,13 @@ def _host_i32(a) -> np.ndarray:
     return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
 
 
+def _require_device_i32(t):
+    torch = _torch()
+    if not (isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.int32 and
+            t.is_contiguous()):
+        raise ValueError("expected a contiguous int32 CUDA tensor")
+
+
 # ---------------------------------------------------------------------------
 # fe::cuda::store  (include/fe/native_cuda.hpp:14)
 # ---------------------------------------------------------------------------
@@ -201,6 +208,49 @@ class AttentionPlan:
                                             last.ctypes.data_as(_P), batch, rows, int(bool(graph)),
                                             _stream(stream)), "prepare_plan")
 
+    def prepare_device(self, qo, kv, pages, last, batch, rows, stream=None):
+        """fe_attn_plan_prepare_device: the same metadata as `prepare`, as
+        int32 DEVICE tensors; the work lists are built on the GPU (graph mode,
+        nothing read back, capturable in a CUDA graph)."""
+        for t in (qo, kv, pages, last):
+            _require_device_i32(t)
+        check(self.lib.fe_attn_plan_prepare_device(self.handle, _ptr(qo), _ptr(kv), _ptr(pages),
+                                                   _ptr(last), int(batch), int(rows),
+                                                   _stream(stream)), "prepare_plan_device")
+
+    def step_prepare_device(self, block_tables, starts, rows_per_seq, slots, positions,
+                            stream=None):
+        """fe_step_prepare_device: slot mapping and work lists on the GPU from
+        int32 block tables [batch, stride] and start positions [batch] (< 0:
+        graph padding entry); writes int64 slots / positions [batch *
+        rows_per_seq]."""
+        _require_device_i32(block_tables)
+        _require_device_i32(starts)
+        batch, stride = int(block_tables.shape[0]), int(block_tables.shape[1])
+        if int(starts.shape[0]) != batch:
+            raise ValueError("starts must have one entry per block-table row")
+        torch = _torch()
+        for t in (slots, positions):
+            if t.dtype != torch.int64 or not t.is_cuda or t.numel() < batch * rows_per_seq:
+                raise ValueError("slots / positions: int64 CUDA tensors of batch*rows_per_seq")
+        check(self.lib.fe_step_prepare_device(self.handle, _ptr(block_tables), stride, _ptr(starts),
+                                              batch, int(rows_per_seq), _ptr(slots),
+                                              _ptr(positions), _stream(stream)),
+              "step_prepare_device")
+
+    def device_meta(self, total_pages=None, nbytes=1 << 22, stream=None) -> dict:
+        """The plan's device metadata (what the kernels read), copied back and
+        unpacked (parse_meta)."""
+        buf = np.zeros(int(nbytes), np.uint8)
+        check(self.lib.fe_attn_plan_debug_device_meta(self.handle, buf.ctypes.data_as(_P),
+                                                      int(nbytes), _stream(stream)),
+              "debug_device_meta")
+        return parse_meta(buf, total_pages)
+
+    def host_meta(self) -> dict:
+        """The host copy of the last host-side prepare's metadata."""
+        return _host_meta(self.lib, self.handle)
+
     def attention(self, q, k, v, out, causal=True, stream=None, lists=None):
         """fe_attn_run; `lists` (FE_ATTN_LISTS_DECODE / _ROWS) runs only part
         of the prepared work (fe_attn_run_lists)."""
@@ -259,6 +309,45 @@ SEQ_DTYPE = np.dtype([("q_row0", "<i4"), ("qrows", "<i4"), ("length", "<i4"),
                       ("page_off", "<i4")])
 
 
+def _host_meta(lib, handle) -> dict:
+    """The host copy of the last host-side prepare's metadata, unpacked."""
+    n = ctypes.c_int64(0)
+    check(lib.fe_attn_plan_debug_meta(handle, None, 0, ctypes.byref(n)), "meta")
+    buf = np.zeros(n.value, dtype=np.uint8)
+    check(lib.fe_attn_plan_debug_meta(handle, buf.ctypes.data_as(_P), n.value, ctypes.byref(n)),
+          "meta")
+    return parse_meta(buf)
+
+
+def parse_meta(buf: np.ndarray, total_pages: int | None = None) -> dict:
+    """Unpack a plan's metadata blob (fe_attn_plan.h layout; section order
+    from the header's offsets). `total_pages` defaults to everything between
+    the pages offset and the end (the host planner puts the pages last)."""
+    h = buf[:128].view(np.int32)
+    out = {"batch": int(h[18]), "rows": int(h[19]), "chunk_tiles": int(h[23]),
+           "dec_heads": int(h[24]), "views": []}
+    seqs_off, pages_off = int(h[20]), int(h[21])
+    batch = out["batch"]
+    out["seqs"] = buf[seqs_off:seqs_off + SEQ_DTYPE.itemsize * batch].view(SEQ_DTYPE)
+    # lists: 0 = row work (non-causal), 1 = row work (causal), 2 = decode work
+    for c in range(3):
+        n_items, n_groups, grid = int(h[0 + c]), int(h[3 + c]), int(h[6 + c])
+        co, io, go = int(h[9 + c]), int(h[12 + c]), int(h[15 + c])
+        view = {
+            "grid": grid,
+            "n_items": n_items,
+            "cta_off": (buf[co:co + 4 * (grid + 1)].view(np.int32) if grid
+                        else np.zeros(1, np.int32)),
+            "items": buf[io:io + ITEM_DTYPE.itemsize * n_items].view(ITEM_DTYPE),
+            "groups": buf[go:go + GROUP_DTYPE.itemsize * n_groups].view(GROUP_DTYPE),
+        }
+        out["views"].append(view)
+    end = int(h[22]) if total_pages is None else pages_off + 4 * int(total_pages)
+    out["pages"] = buf[pages_off:end].view(np.int32)
+    out["buf"] = buf
+    return out
+
+
 class HostPlan:
     """fe_attn_plan_create_host: validates metadata and builds the work list
     on the host for `grid_cap` CTAs, without touching a GPU."""
@@ -284,33 +373,7 @@ class HostPlan:
         return self.meta()
 
     def meta(self) -> dict:
-        n = ctypes.c_int64(0)
-        check(self.lib.fe_attn_plan_debug_meta(self.handle, None, 0, ctypes.byref(n)), "meta")
-        buf = np.zeros(n.value, dtype=np.uint8)
-        check(self.lib.fe_attn_plan_debug_meta(self.handle, buf.ctypes.data_as(_P), n.value,
-                                               ctypes.byref(n)), "meta")
-        h = buf[:128].view(np.int32)
-        out = {"batch": int(h[18]), "rows": int(h[19]), "chunk_tiles": int(h[23]),
-               "dec_heads": int(h[24]), "views": []}
-        seqs_off, pages_off = int(h[20]), int(h[21])
-        batch = out["batch"]
-        out["seqs"] = buf[seqs_off:seqs_off + SEQ_DTYPE.itemsize * batch].view(SEQ_DTYPE)
-        # lists: 0 = row work (non-causal), 1 = row work (causal), 2 = decode work
-        for c in range(3):
-            n_items, n_groups, grid = int(h[0 + c]), int(h[3 + c]), int(h[6 + c])
-            co, io, go = int(h[9 + c]), int(h[12 + c]), int(h[15 + c])
-            view = {
-                "grid": grid,
-                "cta_off": (buf[co:co + 4 * (grid + 1)].view(np.int32) if grid
-                            else np.zeros(1, np.int32)),
-                "items": buf[io:io + ITEM_DTYPE.itemsize * n_items].view(ITEM_DTYPE),
-                "groups": buf[go:go + GROUP_DTYPE.itemsize * n_groups].view(GROUP_DTYPE),
-            }
-            out["views"].append(view)
-        total = int(h[22])
-        out["pages"] = buf[pages_off:total].view(np.int32)
-        out["buf"] = buf
-        return out
+        return _host_meta(self.lib, self.handle)
 
     def close(self):
         if getattr(self, "handle", None):
@@ -326,4 +389,4 @@ class HostPlan:
 
 __all__ = ["store", "copy_blocks", "paged_decode_noalloc", "clear_pages", "gather", "device_errors", "AttentionPlan",
            "create_plan", "destroy_plan", "prepare_plan", "attention", "HostPlan", "FeError",
-           "dtype_code", "ITEM_DTYPE", "GROUP_DTYPE", "SEQ_DTYPE"]
+           "dtype_code", "ITEM_DTYPE", "GROUP_DTYPE", "SEQ_DTYPE", "parse_meta"]

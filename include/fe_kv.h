@@ -54,6 +54,7 @@ typedef enum fe_dtype { FE_DTYPE_F16 = 0, FE_DTYPE_BF16 = 1 } fe_dtype;
 #define FE_DEVERR_TIMEOUT 0x8u     /* attention: a pipeline wait exceeded its bound */
 #define FE_DEVERR_SMEM_ALIGN 0x10u /* attention: dynamic shared memory not 1 KiB aligned (launch skipped) */
 #define FE_DEVERR_POS_RANGE 0x20u  /* rope: position outside [0, max_positions) (row skipped) */
+#define FE_DEVERR_PLAN 0x40u       /* device-side prepare: invalid step or capacity (plan emptied) */
 
 const char* fe_status_string(int status);
 const char* fe_last_error(void);
@@ -223,7 +224,45 @@ int fe_paged_decode_noalloc(const void* q, const void* k_pool, const void* v_poo
                             int batch, int hq, int hkv, int page, int num_blocks, int max_pages,
                             int dtype, void* stream);
 
-/* Introspection of the last prepare (host-side numbers, no sync). */
+/* ------------------------------------------------------------------------
+ * Device-side step preparation (no reference counterpart: replaces the host
+ * loops of CudaModel::prepare, src/cuda_model.cpp:131-142, and the host
+ * planning plus pageable H2D copies of prepare_plan,
+ * src/flashinfer_attention.cu:29-34). Every array argument is DEVICE memory
+ * and nothing is read back on the host, so both calls can be captured in a
+ * CUDA graph together with the append and attention: a decode or verify
+ * step then replays with no host work at all.
+ *
+ * Both leave the plan in graph mode (the attention kernels launch at full
+ * width; batch and rows must stay those of the first graph prepare). The
+ * work lists are built on the device by one kernel on `stream`: the decode
+ * list is the host planner's exact-cut list item for item (identical split
+ * points, bit-identical outputs); prefill/verify units (never split) are
+ * dealt to the CTAs by cost, longest first, in snake order (at most 8192 such
+ * units). Invalid metadata or exceeded capacity does not fail the call (it
+ * is not seen on the host): the plan is emptied, attention writes nothing,
+ * and FE_DEVERR_PLAN is raised (fe_device_errors).
+ * ------------------------------------------------------------------------ */
+/* The caller's device metadata, in the layout of fe_attn_plan_prepare. */
+int fe_attn_plan_prepare_device(fe_attn_plan* plan, const int32_t* qo, const int32_t* kv,
+                                const int32_t* pages, const int32_t* last, int batch, int rows,
+                                void* stream);
+/* The slot mapping too (CudaModel::prepare): sequence b (b < batch) writes
+ * rows_per_seq tokens at positions starts[b] .. starts[b]+rows_per_seq-1
+ * through its block-table row block_tables[b*table_stride ...] (int32 page
+ * ids, at least ceil((starts[b]+rows_per_seq)/page) of them). starts[b] < 0
+ * marks a padding entry of a graph bucket: slot -1 (the append skips it),
+ * position j, the dummy page num_blocks, last = rows_per_seq (as
+ * src/cuda_model.cpp:138). Writes slots[batch*rows_per_seq] and
+ * positions[batch*rows_per_seq] (int64, device) for fe_kv_append / fe_rope*,
+ * and plans attention over qo[b] = b*rows_per_seq, the first
+ * ceil(length/page) pages of each row, last = (length-1) % page + 1. */
+int fe_step_prepare_device(fe_attn_plan* plan, const int32_t* block_tables, int table_stride,
+                           const int32_t* starts, int batch, int rows_per_seq, int64_t* slots,
+                           int64_t* positions, void* stream);
+
+/* Introspection of the last prepare (host-side numbers, no sync; after a
+ * device-side prepare the item counts read -1). */
 typedef struct fe_attn_plan_info {
   int batch, rows;
   int decode_items, prefill_items; /* work items queued for the two kernels */
@@ -245,6 +284,9 @@ int fe_attn_plan_create_host(int hq, int hkv, int dim, int page, int max_batch, 
 /* Copy the packed work-list metadata of the last prepare into `dst` (at most
  * `cap` bytes); *bytes receives its full size. Layout: fe_attn_plan.h. */
 int fe_attn_plan_debug_meta(const fe_attn_plan* plan, void* dst, int64_t cap, int64_t* bytes);
+/* Copy the plan's DEVICE metadata (what the kernels read; at most `cap`
+ * bytes) into host memory `dst`; synchronises `stream`. */
+int fe_attn_plan_debug_device_meta(const fe_attn_plan* plan, void* dst, int64_t cap, void* stream);
 
 #ifdef __cplusplus
 }
