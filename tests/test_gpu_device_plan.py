@@ -74,13 +74,22 @@ def _same_list(a, b):
 
 
 def _same_row_list(dev, host, grid_cap):
-    """Same items (in any CTA), every CTA range inside the list, balanced."""
-    assert dev["n_items"] == host["n_items"]
-    if host["n_items"] == 0:
+    """The same units with the same key ranges (the host may split a unit into
+    pieces, the device never does), every CTA range inside the list, balanced."""
+    units = {}
+    for it in host["items"]:
+        units.setdefault((int(it["seq"]), int(it["kvh"]), int(it["rb0"]), int(it["nrb"])), []).append(
+            (int(it["kt0"]), int(it["kt1"])))
+    assert dev["n_items"] == len(units)
+    if not units:
         return
     assert dev["grid"] == grid_cap and host["grid"] == grid_cap
-    key = lambda it: np.sort(it, order=["seq", "kvh", "rb0"])  # noqa: E731
-    np.testing.assert_array_equal(key(dev["items"].copy()), key(host["items"].copy()))
+    for it in dev["items"]:
+        ranges = sorted(units.pop((int(it["seq"]), int(it["kvh"]), int(it["rb0"]), int(it["nrb"]))))
+        assert ranges[0][0] == 0 and ranges[-1][1] == int(it["kt1"]) and int(it["kt0"]) == 0
+        assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+        assert it["part"] == -1 and it["group"] == -1
+    assert not units
     off = dev["cta_off"]
     assert off[0] == 0 and off[-1] == dev["n_items"] and np.all(np.diff(off) >= 0)
     # dealt by cost, longest first, in snake order: no CTA exceeds the mean
