@@ -27,6 +27,8 @@ namespace fe {
 int decode_launch(int dtype, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
 int decode_merge_launch(int dtype, const void* args, int grid, cudaStream_t stream);
+int wide_launch(int dtype, const void* args, const void* k_pool, const void* v_pool, int hkv,
+                int grid, cudaStream_t stream);
 int prefill_tc_launch(int dtype, const CUtensorMap& kmap, const CUtensorMap& vmap,
                       const CUtensorMap& qmap, const void* args, int grid, cudaStream_t stream);
 
@@ -169,8 +171,8 @@ int check_shape(int hq, int hkv, int dim, int page, int max_batch, int max_pages
                 int num_blocks) {
   if (dtype != FE_DTYPE_F16 && dtype != FE_DTYPE_BF16)
     return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_plan_create: bad dtype");
-  if (dim != kHeadDim)
-    return fail(FE_ERR_UNSUPPORTED, "fe_attn_plan_create: head_dim must be 128");
+  if (dim != kHeadDim && dim != kWideHeadDim)
+    return fail(FE_ERR_UNSUPPORTED, "fe_attn_plan_create: head_dim must be 128 or 256");
   if (hq <= 0 || hkv <= 0 || hq % hkv != 0 || hq / hkv > kRowBlock)
     return fail(FE_ERR_UNSUPPORTED, "fe_attn_plan_create: need hq % hkv == 0 and hq/hkv <= 16");
   if (hkv * 2 > 256 * 1024)
@@ -348,6 +350,8 @@ int prepare_on_device(fe_attn_plan* p, DevPlanArgs& a, int batch, int rows, void
                       const char* what) {
   if (!p) return fail(FE_ERR_INVALID_ARGUMENT, std::string(what) + ": plan is null");
   if (p->host_only) return fail(FE_ERR_INVALID_ARGUMENT, std::string(what) + ": host-only plan");
+  if (p->cfg.dim != kHeadDim)
+    return fail(FE_ERR_UNSUPPORTED, std::string(what) + ": head_dim 128 plans only");
   if (batch < 0 || rows < 0)
     return fail(FE_ERR_INVALID_ARGUMENT,
                 std::string(what) + ": batch and rows must be non-negative");
@@ -473,6 +477,32 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
     return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_run: null pointer");
   if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out))
     return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_run: buffers must be 16-byte aligned");
+  if (p->cfg.dim == kWideHeadDim) {
+    // head_dim 256: every item is on the row lists and served by one kernel
+    if (!(lists & FE_ATTN_LISTS_ROWS)) return FE_OK;
+    MetaHeader hw;
+    std::memcpy(&hw, p->last.meta.data(), sizeof(hw));
+    const int cap = 2 * p->cfg.grid_cap;  // two 96 KiB CTAs per SM
+    const int grid = p->fixed_grid ? cap : std::min(hw.n_items[view], cap);
+    const float sl2 = 1.4426950408889634f / sqrtf(float(p->cfg.dim));
+    const int Gw = p->cfg.hq / p->cfg.hkv;
+    auto sw = static_cast<cudaStream_t>(stream);
+    int rc;
+    if (p->dtype == FE_DTYPE_BF16) {
+      AttnArgs<__nv_bfloat16> a{p->d_meta, static_cast<const __nv_bfloat16*>(q),
+                                static_cast<__nv_bfloat16*>(out), p->d_partials, p->d_counters,
+                                device_error_word(), p->cfg.hq, Gw, p->cfg.page, view, sl2, 0};
+      rc = wide_launch(p->dtype, &a, k_pool, v_pool, p->cfg.hkv, grid, sw);
+    } else {
+      AttnArgs<__half> a{p->d_meta, static_cast<const __half*>(q), static_cast<__half*>(out),
+                         p->d_partials, p->d_counters, device_error_word(), p->cfg.hq, Gw,
+                         p->cfg.page, view, sl2, 0};
+      rc = wide_launch(p->dtype, &a, k_pool, v_pool, p->cfg.hkv, grid, sw);
+    }
+    if (rc != FE_OK) return rc;
+    FE_CUDA_TRY(cudaGetLastError());
+    return FE_OK;
+  }
   const int64_t cache_slots = int64_t(p->cfg.num_blocks + 1) * p->cfg.page;
   const int H = p->cfg.dec_heads;
   if (k_pool != p->kmap_ptr) {

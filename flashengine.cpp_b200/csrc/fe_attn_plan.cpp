@@ -289,6 +289,16 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
     const int P = qrows * G;
     const int RB = ceil_div(P, kRowBlock);
     const int tiles_full = ceil_div(length, kTileTokens);
+    if (cfg.dim == kWideHeadDim) {
+      // 64-row items (four row blocks) per KV head, whatever the row count
+      for (int rb0 = 0; rb0 < RB; rb0 += 4) {
+        const int nrb = std::min(4, RB - rb0);
+        const int rows_valid = std::min(P, (rb0 + nrb) * kRowBlock) - rb0 * kRowBlock;
+        for (int h = 0; h < cfg.hkv; ++h)
+          row_units_full.push_back(Unit{b, h, 2, rb0, nrb, tiles_full, rows_valid});
+      }
+      continue;
+    }
     if (RB == 1) {
       const int H = cfg.dec_heads;
       for (int h = 0; h < cfg.hkv; h += H)
@@ -313,13 +323,50 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
   // List 0: row work, non-causal; 1: row work, causal (identical key ranges
   // when there is no row work); 2: decode work.
   View views[3];
-  const int row_min_chunk = cfg.row_split ? 16 : (1 << 29);
-  int rc = build_view(cfg, row_units_full, cfg.grid_cap, 4, row_min_chunk, fixed_grid, views[0], err);
-  if (rc != FE_OK) return rc;
-  rc = build_view(cfg, row_units_causal, cfg.grid_cap, 4, row_min_chunk, fixed_grid, views[1], err);
-  if (rc != FE_OK) return rc;
-  rc = build_cut_view(cfg, key_units, cfg.dec_grid_cap, 8, fixed_grid, views[2], err);
-  if (rc != FE_OK) return rc;
+  if (cfg.dim == kWideHeadDim) {
+    // one list for both masks, longest items first (the kernel deals them to
+    // its CTAs in a strided loop); no decode list, no splits
+    std::stable_sort(row_units_full.begin(), row_units_full.end(),
+                     [](const Unit& x, const Unit& y) { return x.tiles * x.nrb > y.tiles * y.nrb; });
+    View& v = views[0];
+    for (const Unit& u : row_units_full) {
+      WorkItem it;
+      it.seq = u.seq;
+      it.kvh = static_cast<int16_t>(u.kvh);
+      it.key_mode = static_cast<int16_t>(u.key_mode);
+      it.rb0 = u.rb0;
+      it.nrb = u.nrb;
+      it.kt0 = 0;
+      it.kt1 = u.tiles;
+      it.part = -1;
+      it.group = -1;
+      v.items.push_back(it);
+    }
+    v.prefill_items = static_cast<int>(v.items.size());
+    if (static_cast<int>(v.items.size()) > cfg.max_items) {
+      err = "attention work exceeds the plan's item capacity";
+      return FE_ERR_CAPACITY;
+    }
+    // (the wide kernel deals items by index and does not read cta_off; it
+    // records one item per CTA for introspection)
+    const int n = static_cast<int>(v.items.size());
+    v.grid = n == 0 ? 0 : std::min(n, 2 * std::max(1, cfg.grid_cap));
+    v.cta_off.assign(v.grid + 1, 0);
+    for (int c = 0; c <= v.grid; ++c) v.cta_off[c] = c < v.grid ? c : n;
+    v.chunk = 1 << 29;
+    views[1] = v;
+    views[2].cta_off.clear();
+  } else {
+    const int row_min_chunk = cfg.row_split ? 16 : (1 << 29);
+    int rc = build_view(cfg, row_units_full, cfg.grid_cap, 4, row_min_chunk, fixed_grid, views[0],
+                        err);
+    if (rc != FE_OK) return rc;
+    rc = build_view(cfg, row_units_causal, cfg.grid_cap, 4, row_min_chunk, fixed_grid, views[1],
+                    err);
+    if (rc != FE_OK) return rc;
+    rc = build_cut_view(cfg, key_units, cfg.dec_grid_cap, 8, fixed_grid, views[2], err);
+    if (rc != FE_OK) return rc;
+  }
   // Both kernels of one run share the split workspace and counters: offset
   // the decode list's records and groups past the larger row list's.
   const int64_t row_floats = std::max(views[0].partial_floats, views[1].partial_floats);

@@ -18,6 +18,7 @@
 namespace fe {
 
 constexpr int kHeadDim = 128;
+constexpr int kWideHeadDim = 256;  // served by the separate wide kernel (fe_wide.cu)
 constexpr int kTileTokens = 16;   // key tokens per tile (one TMA box per K/V half)
 constexpr int kRowBlock = 16;     // packed query rows per mma row block
 
@@ -33,8 +34,11 @@ struct SeqInfo {  // 16 bytes
 //   key_mode = 1: a single row block; the consumer warps split the key tiles
 //                 (decode and short verify) and their results are merged in
 //                 shared memory.
-//   key_mode = 0: up to four row blocks, one per consumer warp, each over all
-//                 key tiles of the item (prefill / long verify).
+//   key_mode = 0: up to eight row blocks (one 128-row tcgen05 tile), each
+//                 over all key tiles of the item (prefill / long verify).
+//   key_mode = 2: head_dim 256 (wide kernel): up to four row blocks against
+//                 every key of the sequence; the kernel derives the key range
+//                 from the mask.
 // A packed row p is query row p / G of the sequence, query head kvh*G + p % G.
 struct WorkItem {  // 32 bytes
   int32_t seq;

@@ -151,3 +151,32 @@ def test_zero_row_sequences_are_skipped():
     meta = hp.prepare([0, 0, 1, 1], [0, 1, 2, 3], [0, 1, 2], [5, 5, 5])
     seqs = [int(it["seq"]) for v in meta["views"] for it in v["items"]]
     assert set(seqs) == {1}
+
+
+def test_head_dim_256_plan_is_one_row_list():
+    """head_dim 256 plans put every (sequence, KV head, 64-row block) on the
+    row lists for the wide kernel (both masks), longest first, with no decode
+    list and no splits."""
+    # a decode row, a 100-row chunk and a 3-row block
+    from fekv.metadata import build_step_metadata
+    tables = [np.arange(i * 200, i * 200 + 200) for i in range(3)]
+    md = build_step_metadata(tables, [40, 2900, 700], [1, 100, 3], 16)
+    hp = HostPlan(16, 2, 256, 16, 3, 200, True, 600, grid_cap=8)
+    meta = hp.prepare(md.qo, md.kv, md.pages, md.last)
+    G = 8
+    want = sum(-(-int(r) * G // 64) * 2 for r in np.diff(md.qo))
+    v0, v1, v2 = meta["views"]
+    assert len(v0["items"]) == want and len(v1["items"]) == want
+    np.testing.assert_array_equal(v0["items"], v1["items"])
+    assert len(v2["items"]) == 0 and len(v0["groups"]) == 0
+    assert (v0["items"]["key_mode"] == 2).all() and (v0["items"]["part"] == -1).all()
+    cost = (v0["items"]["kt1"] - v0["items"]["kt0"]) * v0["items"]["nrb"]
+    assert (np.diff(cost) <= 0).all()
+    # rows covered exactly once per KV head
+    for b, q in enumerate(np.diff(md.qo)):
+        for h in range(2):
+            its = v0["items"][(v0["items"]["seq"] == b) & (v0["items"]["kvh"] == h)]
+            rows = sorted(r for it in its for r in range(int(it["rb0"]) * 16,
+                                                         min(int(q) * G, (int(it["rb0"]) + int(it["nrb"])) * 16)))
+            assert rows == list(range(int(q) * G))
+    hp.close()

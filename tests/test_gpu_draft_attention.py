@@ -10,8 +10,8 @@ formulations on the GPU:
 * Qwen3.5-style full attention (src/hybrid_model.cpp:41-50): partial rotary
   (leading rotary dims only), store, attention of one row over its context.
 
-head_dim is 128 (the dimension this repository's attention kernels, like the
-reference's CUDA build, support)."""
+head_dim 128 runs on the decode / tcgen05 kernels; head_dim 256 (Qwen3.5's
+full-attention layers) on the separate wide kernel."""
 import math
 
 import numpy as np
@@ -46,20 +46,20 @@ def _rotate(x, cos, sin, pos, rot):
                      dim=-1)
 
 
-def _dense_attention(q, kc, vc, read, valid, hq, hkv):
+def _dense_attention(q, kc, vc, read, valid, hq, hkv, dim=DIM):
     """src/block_draft.cpp:28-29 / src/hybrid_model.cpp:48-49: gather the read
     slots, mask timeline >= valid, fp32 softmax attention."""
     import torch
     G = hq // hkv
-    keys = kc.view(-1, hkv, DIM).index_select(0, read).repeat_interleave(G, 1).permute(1, 2, 0)
-    values = vc.view(-1, hkv, DIM).index_select(0, read).repeat_interleave(G, 1).permute(1, 0, 2)
-    scores = torch.bmm(q.permute(1, 0, 2).float(), keys.float()) / math.sqrt(DIM)
+    keys = kc.view(-1, hkv, dim).index_select(0, read).repeat_interleave(G, 1).permute(1, 2, 0)
+    values = vc.view(-1, hkv, dim).index_select(0, read).repeat_interleave(G, 1).permute(1, 0, 2)
+    scores = torch.bmm(q.permute(1, 0, 2).float(), keys.float()) / math.sqrt(dim)
     timeline = torch.arange(read.shape[0], device=q.device)
     scores = scores.masked_fill((timeline >= valid)[None, None, :], float("-inf"))
     return torch.bmm(torch.softmax(scores, -1), values.float()).permute(1, 0, 2).to(q.dtype)
 
 
-def _run_case(hq, hkv, start, rows, rot, max_model_len, seed):
+def _run_case(hq, hkv, start, rows, rot, max_model_len, seed, dim=DIM):
     import torch
 
     import fekv
@@ -69,14 +69,14 @@ def _run_case(hq, hkv, start, rows, rot, max_model_len, seed):
     g.manual_seed(seed)
     num_blocks = 400
     cache_slots = (num_blocks + 1) * PAGE
-    width = hkv * DIM
+    width = hkv * dim
     end = start + rows
     blocks = rng.permutation(num_blocks)[: -(-max_model_len // PAGE)].astype(np.int64)
     kc0 = torch.randn(cache_slots, width, generator=g, device="cuda").to(torch.bfloat16)
     vc0 = torch.randn(cache_slots, width, generator=g, device="cuda").to(torch.bfloat16)
-    q = torch.randn(rows, hq, DIM, generator=g, device="cuda").to(torch.bfloat16)
-    k = torch.randn(rows, hkv, DIM, generator=g, device="cuda").to(torch.bfloat16)
-    v = torch.randn(rows, hkv, DIM, generator=g, device="cuda").to(torch.bfloat16)
+    q = torch.randn(rows, hq, dim, generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn(rows, hkv, dim, generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn(rows, hkv, dim, generator=g, device="cuda").to(torch.bfloat16)
     cos, sin = _cos_sin(max_model_len, rot)
     pos = torch.arange(start, end, device="cuda")
     slots = torch.from_numpy(blocks[np.arange(start, end) // PAGE] * PAGE +
@@ -89,12 +89,13 @@ def _run_case(hq, hkv, start, rows, rot, max_model_len, seed):
     read = np.full(max_model_len, num_blocks * PAGE, np.int64)  # the padding page's first slot
     t = np.arange(end)
     read[:end] = blocks[t // PAGE] * PAGE + t % PAGE
-    out_ref = _dense_attention(q_ref, kc_ref, vc_ref, torch.from_numpy(read).cuda(), end, hq, hkv)
+    out_ref = _dense_attention(q_ref, kc_ref, vc_ref, torch.from_numpy(read).cuda(), end, hq, hkv,
+                               dim)
     # ours: fused RoPE + append, then the plan with the full mask
     qd, kc, vc = q.clone(), kc0.clone(), vc0.clone()
     cache = torch.cat([cos, sin], dim=1).contiguous()
     fekv.rope_append(qd, k, v, kc, vc, slots, pos, cache)
-    plan = fekv.AttentionPlan(hq, hkv, DIM, PAGE, 1, -(-max_model_len // PAGE) + 1, True,
+    plan = fekv.AttentionPlan(hq, hkv, dim, PAGE, 1, -(-max_model_len // PAGE) + 1, True,
                               num_blocks)
     md = draft_block_metadata(blocks, start, rows, PAGE)
     plan.prepare(md.qo, md.kv, md.pages, md.last)
@@ -120,3 +121,14 @@ def test_dflash_draft_block_matches_dense_reference(hq, hkv, start, rows):
 @pytest.mark.parametrize("rot,start", [(64, 777), (32, 5), (128, 1500)])
 def test_partial_rotary_full_attention_row_matches_dense_reference(rot, start):
     _run_case(16, 2, start, 1, rot, max_model_len=2048, seed=rot + start)
+
+
+@pytest.mark.parametrize("hq,hkv,start,rows", [(16, 2, 700, 17), (8, 1, 0, 16), (24, 4, 2000, 9)])
+def test_dflash_draft_block_head_dim_256(hq, hkv, start, rows):
+    _run_case(hq, hkv, start, rows, 256, max_model_len=3072, seed=start + rows, dim=256)
+
+
+@pytest.mark.parametrize("rot,start", [(64, 1234), (256, 77)])
+def test_qwen35_full_attention_row_head_dim_256(rot, start):
+    """Qwen3.5's full-attention layers: head_dim 256 with a partial rotary."""
+    _run_case(16, 2, start, 1, rot, max_model_len=2048, seed=rot + start, dim=256)

@@ -1,0 +1,91 @@
+"""head_dim 256 (fe_wide.cu) through the same plan / attention calls, against
+the fp32 torch restatement of the reference's ATen attention
+(src/portable_gpu_ops.cpp:39-44, which takes any head_dim). Tolerance as for
+head_dim 128: fe_testutil.ATOL widened by one output ulp."""
+import numpy as np
+import pytest
+
+from fe_testutil import compare_attention, to_host_bits, torch_reference_attention
+
+pytestmark = pytest.mark.gpu
+
+DIM = 256
+PAGE = 16
+
+
+@pytest.fixture(scope="module")
+def fk():
+    import torch
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    import fekv
+    fekv.load()
+    return fekv
+
+
+def _case(fk, hq, hkv, cached, rows, bf16, causal, seed, graph=False):
+    import torch
+    import fekv.workloads as wl
+    from fekv.metadata import build_step_metadata
+    rng = np.random.default_rng(seed)
+    npg = [-(-int(c + r) // PAGE) for c, r in zip(cached, rows)]
+    tables = wl._tables_from_permutation(rng.permutation(sum(npg) + 5), npg)
+    nblocks = sum(npg) + 5
+    md = build_step_metadata(tables, cached, rows, PAGE)
+    dt = torch.bfloat16 if bf16 else torch.float16
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    slots_total = (nblocks + 1) * PAGE
+    kc = torch.randn(slots_total, hkv * DIM, generator=g, device="cuda").to(dt)
+    vc = torch.randn(slots_total, hkv * DIM, generator=g, device="cuda").to(dt)
+    q = torch.randn(md.rows, hq, DIM, generator=g, device="cuda").to(dt)
+    plan = fk.AttentionPlan(hq, hkv, DIM, PAGE, md.batch, int(np.diff(md.kv).max()) + 1, bf16,
+                            nblocks)
+    plan.prepare(md.qo, md.kv, md.pages, md.last, graph=graph)
+    out = torch.full_like(q, float("nan"))
+    plan.attention(q, kc, vc, out, causal)
+    ref = torch_reference_attention(q, kc, vc, md.qo, md.kv, md.pages, md.last, hq, hkv, PAGE,
+                                    causal)
+    torch.cuda.synchronize()
+    assert fk.device_errors() == 0
+    res = compare_attention(to_host_bits(out), to_host_bits(ref.to(dt)), bf16,
+                            ref_f32=ref.cpu().numpy())
+    plan.close()
+    return res
+
+
+@pytest.mark.parametrize("bf16", [True, False])
+@pytest.mark.parametrize("hq,hkv", [(16, 2), (24, 4), (8, 8), (32, 2)])
+def test_decode_rows(fk, bf16, hq, hkv):
+    rng = np.random.default_rng(hq + hkv)
+    cached = rng.integers(1, 3000, 12)
+    res = _case(fk, hq, hkv, cached, np.ones(12, int), bf16, True, hq * 7 + hkv)
+    assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, res
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("seed", range(4))
+def test_mixed_rows_random(fk, causal, seed):
+    """Decode rows, draft / verify blocks and prefill chunks in one step."""
+    rng = np.random.default_rng(50 + seed)
+    hkv = int(rng.choice([1, 2, 4]))
+    G = int(rng.choice([1, 2, 3, 4, 6, 8]))
+    batch = int(rng.integers(1, 7))
+    cached = rng.integers(0, 1500, batch)
+    rows = np.where(rng.random(batch) < 0.4, 1, rng.integers(1, 160, batch))
+    res = _case(fk, hkv * G, hkv, cached, rows, bool(seed % 2), causal, 900 + seed)
+    assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, res
+
+
+def test_graph_mode_plan(fk):
+    res = _case(fk, 16, 2, [100, 2000, 7], [33, 1, 5], True, True, 3, graph=True)
+    assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, res
+
+
+def test_device_prepare_is_refused_for_head_dim_256(fk):
+    import torch
+    plan = fk.AttentionPlan(16, 2, DIM, PAGE, 2, 8, True, 32)
+    z = torch.zeros(3, dtype=torch.int32, device="cuda")
+    with pytest.raises(fk.FeError) as e:
+        plan.prepare_device(z, z, z, z[:2], 2, 2)
+    assert e.value.status == fk._lib.FE_ERR_UNSUPPORTED
+    plan.close()
