@@ -48,6 +48,37 @@ def measured_peak_tflops():
         return 1400.0, "fallback (sustained)"
 
 
+# DRAM bytes (read + write) per launch of each roofline kernel, from one
+# `ncu --set full --clock-control none` capture of the same layer shape; the
+# profile named beside each holds the command. Keyed by (workload, kernel) and
+# checked against the algorithmic units (bytes or FLOPs) of the captured launch,
+# so a changed workload reports null rather than a stale figure.
+# The decode kernel streams every page once, so its traffic scales with the
+# bytes a launch reads (the bench's contexts grow by one token per step); the
+# tcgen05 kernel's DRAM bytes depend on L2 reuse of shared prefixes and are
+# only reported for the captured launch itself.
+NCU_TRAFFIC = {
+    ("C2", "paged_decode_kernel"): (611757056, 603463680.0, True,
+                                    "profiles/paged_decode_kernel_c2.md"),
+    ("C4", "paged_prefill_tc_kernel"): (63075840, 75586338816.0, False,
+                                        "profiles/paged_prefill_tc_kernel_c4.md"),
+}
+
+
+def ncu_traffic(workload: str, kernel: str, units_per_launch: float):
+    """(traffic bytes per launch, source) for the bench's launch, or (None, None)."""
+    ent = NCU_TRAFFIC.get((workload, kernel))
+    if ent is None:
+        return None, None
+    dram, units, proportional, src = ent
+    ratio = units_per_launch / units
+    if proportional and 0.9 < ratio < 1.1:
+        return round(dram * ratio), f"ncu capture scaled by algorithmic bytes, {src}"
+    if abs(ratio - 1.0) <= 1e-3:
+        return dram, f"ncu capture, {src}"
+    return None, None
+
+
 def measured_peak_gbs():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -457,6 +488,7 @@ def run_ours(args, rank, world, local):
             "algorithmic_bytes_per_launch": float(per_launch_bytes),
             "avg_launch_ms": round(float(stats[0, 2]), 5),
             "traffic": None,
+            "traffic_source": None,
         },
         "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": int(d2h_bytes),
@@ -483,6 +515,7 @@ def run_ours(args, rank, world, local):
             "kernel": "paged_prefill_tc_kernel",
             "algorithmic_flops_per_launch": per_launch_flops,
             "avg_launch_ms": round(float(stats[0, 2]), 5), "traffic": None,
+            "traffic_source": None,
         }
         if mixed:
             # the step's multi-row sequences on the tcgen05 kernel, and its
@@ -503,6 +536,9 @@ def run_ours(args, rank, world, local):
             line["attention_call_tflops"] = round(float(achieved_tflops), 2)
         line["gpu_launches"] = launches_per_layer * w.layers * args.steps + (
             args.steps if w.cow is not None else 0)
+    rl = line["roofline"]
+    units = rl.get("algorithmic_bytes_per_launch", rl.get("algorithmic_flops_per_launch"))
+    rl["traffic"], rl["traffic_source"] = ncu_traffic(w.name, rl["kernel"], float(units))
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w, args)
     return line
