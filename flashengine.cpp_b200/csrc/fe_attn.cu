@@ -24,9 +24,9 @@
 
 namespace fe {
 
-int decode_launch(int dtype, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
+int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
-int decode_merge_launch(int dtype, const void* args, int grid, cudaStream_t stream);
+int decode_merge_launch(int dtype, int dim, const void* args, int grid, cudaStream_t stream);
 int wide_launch(int dtype, const void* args, const void* k_pool, const void* v_pool, int hkv,
                 int grid, cudaStream_t stream);
 int prefill_tc_launch(int dtype, const CUtensorMap& kmap, const CUtensorMap& vmap,
@@ -102,24 +102,26 @@ int encode_q_map(CUtensorMap* map, const void* q, int dtype, int hq, int rows, i
   return encode_nd(map, q, dtype, 3, dims, strides, box);
 }
 
-// Row kernel: pool viewed as [cache_slots][hkv*2][64] (64-element head-half
-// rows of 128 B); box = 16 slots x 1 head-half x 64 elements.
-int encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int hkv, int64_t cache_slots) {
-  const cuuint64_t dims[3] = {64, cuuint64_t(hkv) * 2, cuuint64_t(cache_slots)};
-  const cuuint64_t strides[2] = {128, cuuint64_t(hkv) * 256};
+// Per-box fallback of the decode kernel: pool viewed as
+// [cache_slots][hkv*dim/64][64] (64-element rows of 128 B: head-halves for
+// head_dim 128); box = 16 slots x 1 row x 64 elements.
+int encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int hkv, int dim,
+                    int64_t cache_slots) {
+  const cuuint64_t dims[3] = {64, cuuint64_t(hkv) * (dim / 64), cuuint64_t(cache_slots)};
+  const cuuint64_t strides[2] = {128, cuuint64_t(hkv) * dim * 2};
   const cuuint32_t box[3] = {64, 1, kTileTokens};
   return encode_3d(map, pool, dtype, dims, strides, box);
 }
 
-// Decode kernel: the same memory walked slots-first, [hkv*2][cache_slots][64];
-// box = 2H head-halves x 16 slots x 64 elements, so one TMA copies a 16-token
-// tile of H heads (a contiguous 16 x H x 256 B block of the page) and lays it
-// out head-half by head-half, 16 swizzled rows each.
-int encode_decode_map(CUtensorMap* map, const void* pool, int dtype, int hkv, int heads,
+// Decode kernel: the same memory walked slots-first, [hkv*dim/64][cache_slots]
+// [64]; box = H*dim/64 rows x 16 slots x 64 elements, so one TMA copies a
+// 16-token tile of H heads (a contiguous 16 x H x 2*dim-byte block of the
+// page) and lays it out 64 dims at a time, 16 swizzled rows each.
+int encode_decode_map(CUtensorMap* map, const void* pool, int dtype, int hkv, int dim, int heads,
                       int64_t cache_slots) {
-  const cuuint64_t dims[3] = {64, cuuint64_t(cache_slots), cuuint64_t(hkv) * 2};
-  const cuuint64_t strides[2] = {cuuint64_t(hkv) * 256, 128};
-  const cuuint32_t box[3] = {64, kTileTokens, cuuint32_t(2 * heads)};
+  const cuuint64_t dims[3] = {64, cuuint64_t(cache_slots), cuuint64_t(hkv) * (dim / 64)};
+  const cuuint64_t strides[2] = {cuuint64_t(hkv) * dim * 2, 128};
+  const cuuint32_t box[3] = {64, kTileTokens, cuuint32_t(heads * (dim / 64))};
   return encode_3d(map, pool, dtype, dims, strides, box);
 }
 
@@ -206,7 +208,9 @@ PlanConfig make_config(int hq, int hkv, int dim, int page, int max_batch, int ma
   c.num_blocks = num_blocks;
   c.grid_cap = grid_cap;
   c.dec_grid_cap = dec_grid_cap;
-  c.dec_heads = gcd8(hkv);
+  // KV heads per decode item: one 16-token tile of them is one TMA box; for
+  // head_dim 256 (8 KiB per head and tile) at most two
+  c.dec_heads = dim == kWideHeadDim ? (hkv % 2 == 0 ? 2 : 1) : gcd8(hkv);
   c.row_group_blocks = 8;  // 128 packed rows per tcgen05 work item
   c.row_split = false;      // the tcgen05 kernel walks an item's whole key range
   int64_t items = int64_t(max_batch) * hkv * 64;
@@ -477,50 +481,32 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
     return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_run: null pointer");
   if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out))
     return fail(FE_ERR_INVALID_ARGUMENT, "fe_attn_run: buffers must be 16-byte aligned");
-  if (p->cfg.dim == kWideHeadDim) {
-    // head_dim 256: every item is on the row lists and served by one kernel
-    if (!(lists & FE_ATTN_LISTS_ROWS)) return FE_OK;
-    MetaHeader hw;
-    std::memcpy(&hw, p->last.meta.data(), sizeof(hw));
-    const int cap = 2 * p->cfg.grid_cap;  // two 96 KiB CTAs per SM
-    const int grid = p->fixed_grid ? cap : std::min(hw.n_items[view], cap);
-    const float sl2 = 1.4426950408889634f / sqrtf(float(p->cfg.dim));
-    const int Gw = p->cfg.hq / p->cfg.hkv;
-    auto sw = static_cast<cudaStream_t>(stream);
-    int rc;
-    if (p->dtype == FE_DTYPE_BF16) {
-      AttnArgs<__nv_bfloat16> a{p->d_meta, static_cast<const __nv_bfloat16*>(q),
-                                static_cast<__nv_bfloat16*>(out), p->d_partials, p->d_counters,
-                                device_error_word(), p->cfg.hq, Gw, p->cfg.page, view, sl2, 0};
-      rc = wide_launch(p->dtype, &a, k_pool, v_pool, p->cfg.hkv, grid, sw);
-    } else {
-      AttnArgs<__half> a{p->d_meta, static_cast<const __half*>(q), static_cast<__half*>(out),
-                         p->d_partials, p->d_counters, device_error_word(), p->cfg.hq, Gw,
-                         p->cfg.page, view, sl2, 0};
-      rc = wide_launch(p->dtype, &a, k_pool, v_pool, p->cfg.hkv, grid, sw);
-    }
-    if (rc != FE_OK) return rc;
-    FE_CUDA_TRY(cudaGetLastError());
-    return FE_OK;
-  }
   const int64_t cache_slots = int64_t(p->cfg.num_blocks + 1) * p->cfg.page;
   const int H = p->cfg.dec_heads;
+  const int dim = p->cfg.dim;
+  const bool wide = dim == kWideHeadDim;
   if (k_pool != p->kmap_ptr) {
-    int rc = encode_pool_map(&p->kmap, k_pool, p->dtype, p->cfg.hkv, cache_slots);
+    int rc = encode_pool_map(&p->kmap, k_pool, p->dtype, p->cfg.hkv, dim, cache_slots);
     if (rc != FE_OK) return rc;
-    if (encode_decode_map(&p->kmap_dec, k_pool, p->dtype, p->cfg.hkv, H, cache_slots) != FE_OK)
+    if (encode_decode_map(&p->kmap_dec, k_pool, p->dtype, p->cfg.hkv, dim, H, cache_slots) !=
+        FE_OK)
       p->per_head_tma = true;
-    rc = encode_tc_map(&p->kmap_tc, k_pool, p->dtype, p->cfg.hkv, cache_slots);
-    if (rc != FE_OK) return rc;
+    if (!wide) {
+      rc = encode_tc_map(&p->kmap_tc, k_pool, p->dtype, p->cfg.hkv, cache_slots);
+      if (rc != FE_OK) return rc;
+    }
     p->kmap_ptr = k_pool;
   }
   if (v_pool != p->vmap_ptr) {
-    int rc = encode_pool_map(&p->vmap, v_pool, p->dtype, p->cfg.hkv, cache_slots);
+    int rc = encode_pool_map(&p->vmap, v_pool, p->dtype, p->cfg.hkv, dim, cache_slots);
     if (rc != FE_OK) return rc;
-    if (encode_decode_map(&p->vmap_dec, v_pool, p->dtype, p->cfg.hkv, H, cache_slots) != FE_OK)
+    if (encode_decode_map(&p->vmap_dec, v_pool, p->dtype, p->cfg.hkv, dim, H, cache_slots) !=
+        FE_OK)
       p->per_head_tma = true;
-    rc = encode_tc_map(&p->vmap_tc, v_pool, p->dtype, p->cfg.hkv, cache_slots);
-    if (rc != FE_OK) return rc;
+    if (!wide) {
+      rc = encode_tc_map(&p->vmap_tc, v_pool, p->dtype, p->cfg.hkv, cache_slots);
+      if (rc != FE_OK) return rc;
+    }
     p->vmap_ptr = v_pool;
   }
   MetaHeader h;
@@ -533,44 +519,46 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
   CUtensorMap qmap;
   std::memset(&qmap, 0, sizeof(qmap));  // unused when G does not divide 128
   int q_map_rows = 0;
-  if (grid_rows > 0 && 128 % (p->cfg.hq / p->cfg.hkv) == 0 && h.rows > 0) {
+  if (!wide && grid_rows > 0 && 128 % (p->cfg.hq / p->cfg.hkv) == 0 && h.rows > 0) {
     int rc = encode_q_map(&qmap, q, p->dtype, p->cfg.hq, h.rows, p->cfg.hq / p->cfg.hkv);
     if (rc != FE_OK) return rc;
     q_map_rows = h.rows;
   }
-  const float scale_log2 = 1.4426950408889634f / sqrtf(float(p->cfg.dim));
+  // head_dim 256 row work runs on the wide kernel, two 96 KiB CTAs per SM
+  const int grid_wide =
+      !wide || grid_rows == 0
+          ? 0
+          : (p->fixed_grid ? 2 * p->cfg.grid_cap : std::min(h.n_items[view], 2 * p->cfg.grid_cap));
+  const float scale_log2 = 1.4426950408889634f / sqrtf(float(dim));
   auto s = static_cast<cudaStream_t>(stream);
   const int G = p->cfg.hq / p->cfg.hkv;
   const CUtensorMap& kd = p->per_head_tma ? p->kmap : p->kmap_dec;
   const CUtensorMap& vd = p->per_head_tma ? p->vmap : p->vmap_dec;
+  auto launch_all = [&](const auto& a) -> int {
+    if (grid_dec > 0) {
+      int rc = decode_launch(p->dtype, dim, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
+      if (rc == FE_OK) rc = decode_merge_launch(p->dtype, dim, &a, grid_merge, s);
+      if (rc != FE_OK) return rc;
+    }
+    if (wide) return wide_launch(p->dtype, &a, k_pool, v_pool, p->cfg.hkv, grid_wide, s);
+    if (grid_rows > 0)
+      return prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, qmap, &a, grid_rows, s);
+    return FE_OK;
+  };
+  int rc;
   if (p->dtype == FE_DTYPE_BF16) {
     AttnArgs<__nv_bfloat16> a{p->d_meta, static_cast<const __nv_bfloat16*>(q),
                               static_cast<__nv_bfloat16*>(out), p->d_partials, p->d_counters,
                               device_error_word(), p->cfg.hq, G, p->cfg.page, view, scale_log2,
                               q_map_rows};
-    if (grid_dec > 0) {
-      int rc = decode_launch(p->dtype, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
-      if (rc == FE_OK) rc = decode_merge_launch(p->dtype, &a, grid_merge, s);
-      if (rc != FE_OK) return rc;
-    }
-    if (grid_rows > 0) {
-      int rc = prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, qmap, &a, grid_rows, s);
-      if (rc != FE_OK) return rc;
-    }
+    rc = launch_all(a);
   } else {
     AttnArgs<__half> a{p->d_meta, static_cast<const __half*>(q), static_cast<__half*>(out),
                        p->d_partials, p->d_counters, device_error_word(), p->cfg.hq, G,
                        p->cfg.page, view, scale_log2, q_map_rows};
-    if (grid_dec > 0) {
-      int rc = decode_launch(p->dtype, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
-      if (rc == FE_OK) rc = decode_merge_launch(p->dtype, &a, grid_merge, s);
-      if (rc != FE_OK) return rc;
-    }
-    if (grid_rows > 0) {
-      int rc = prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, qmap, &a, grid_rows, s);
-      if (rc != FE_OK) return rc;
-    }
+    rc = launch_all(a);
   }
+  if (rc != FE_OK) return rc;
   FE_CUDA_TRY(cudaGetLastError());
   return FE_OK;
 }

@@ -3,9 +3,10 @@
 // launch arguments, the bounded mbarrier wait, and the key-mode tile math.
 //
 // Shared-memory tile layout (both kernels): a key tile is 16 consecutive
-// tokens of one page. For one KV head it is stored as two "head-half" boxes
-// of 16 rows x 128 bytes (dims 0-63 and 64-127), written by TMA with the
-// 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r & 7).
+// tokens of one page. For one KV head it is stored as D/64 boxes of 16 rows x
+// 128 bytes (dims 0-63, 64-127, ...; "head-halves" for head_dim 128), written
+// by TMA with the 128-byte swizzle: 16-byte chunk c of row r sits at chunk
+// c ^ (r & 7).
 #pragma once
 
 #include "fe_attn_plan.h"
@@ -13,7 +14,7 @@
 
 namespace fe {
 
-constexpr int kHalfBytes = kTileTokens * 128;  // one head-half box: 16 rows x 128 B
+constexpr int kHalfBytes = kTileTokens * 128;  // one 64-dim box: 16 rows x 128 B
 constexpr int kCombStride = kHeadDim + 4;      // merge rows: O[128], m, l, pad
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
@@ -91,39 +92,41 @@ __device__ __forceinline__ uint32_t ldg32(const void* p) {
   return __ldg(reinterpret_cast<const uint32_t*>(p));
 }
 
-// Shared-memory addresses of one KV head's slice of a staged tile.
+// Shared-memory addresses of one KV head's slice of a staged tile: the
+// head's 64-dim boxes of K (and of V) follow one another, kHalfBytes apart.
 struct TileAddr {
-  uint32_t k0, k1, v0, v1;  // K dims 0-63 / 64-127, V dims 0-63 / 64-127
+  uint32_t k, v;
 };
 
 // ---------------------------------------------------------------------------
 // Key mode: one row block of P <= 16 packed rows (packed row p = query row
-// p / G, head p % G of the GQA group) against a KV head. The key tile sits on
-// the mma M side: S^T = K Q^T (16 tokens x 8*NT columns), so a GQA group of 8
-// fills the N dimension; O^T = V^T P^T accumulates 128 dims x 8*NT columns.
+// p / G, head p % G of the GQA group) against a KV head of D dims. The key
+// tile sits on the mma M side: S^T = K Q^T (16 tokens x 8*NT columns), so a
+// GQA group of 8 fills the N dimension; O^T = V^T P^T accumulates D dims x
+// 8*NT columns. The state covers packed rows col0 .. col0 + 8*NT - 1.
 // P^T is split into a 16-bit high part and its residual (two mma), keeping
 // ~16 significant bits of the fp32 softmax weights.
 // ---------------------------------------------------------------------------
-template <typename T, int NT>
+template <typename T, int NT, int D = kHeadDim>
 struct KeyState {
-  uint32_t qb[NT][8][2];  // Q^T as B fragments: column lane/4 (+8 nt)
-  int lim[NT][2];         // visible-key limit of this lane's columns
+  static constexpr int kMT = D / 16;  // k-steps of S^T, m-tiles of O^T
+  uint32_t qb[NT][kMT][2];  // Q^T as B fragments: column lane/4 (+8 nt)
+  int lim[NT][2];           // visible-key limit of this lane's columns
   int lim_min;
   float m[NT][2], l[NT][2];
-  float o[NT][8][4];
+  float o[NT][kMT][4];
 
   __device__ __forceinline__ void init(const T* q, int hq, int q_row0, int qrows, int length,
-                                       int head0, int G, bool causal, int lane) {
+                                       int head0, int G, bool causal, int lane, int col0 = 0) {
     const int r8 = lane >> 2, cq = lane & 3;
     const int P = qrows * G;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const int p = nt * 8 + r8;
-      const T* qp =
-          p < P ? q + (static_cast<int64_t>(q_row0 + p / G) * hq + head0 + p % G) * kHeadDim
-                : nullptr;
+      const int p = col0 + nt * 8 + r8;
+      const T* qp = p < P ? q + (static_cast<int64_t>(q_row0 + p / G) * hq + head0 + p % G) * D
+                          : nullptr;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
+      for (int kk = 0; kk < kMT; ++kk) {
         qb[nt][kk][0] = qp ? ldg32(qp + kk * 16 + 2 * cq) : 0u;
         qb[nt][kk][1] = qp ? ldg32(qp + kk * 16 + 8 + 2 * cq) : 0u;
       }
@@ -133,7 +136,7 @@ struct KeyState {
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int p = nt * 8 + 2 * cq + e;
+        const int p = col0 + nt * 8 + 2 * cq + e;
         lim[nt][e] = (causal && p < P) ? length - qrows + p / G + 1 : length;
         lim_min = min(lim_min, lim[nt][e]);
       }
@@ -142,7 +145,7 @@ struct KeyState {
       m[nt][0] = m[nt][1] = -INFINITY;
       l[nt][0] = l[nt][1] = 0.f;
 #pragma unroll
-      for (int mt = 0; mt < 8; ++mt)
+      for (int mt = 0; mt < kMT; ++mt)
         o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
     }
   }
@@ -156,10 +159,10 @@ struct KeyState {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
+    for (int kk = 0; kk < kMT; ++kk) {
       const int tok = li + ((mi & 1) << 3);
-      const int c = 2 * kk + (mi >> 1);
-      const uint32_t addr = ((c >> 3) ? t.k1 : t.k0) + tok * 128 + (((c & 7) ^ li) << 4);
+      const int c = 2 * kk + (mi >> 1);  // 16-byte chunk of the row (8 per 64-dim box)
+      const uint32_t addr = t.k + (c >> 3) * kHalfBytes + tok * 128 + (((c & 7) ^ li) << 4);
       uint32_t af[4];
       ldmatrix_x4(addr, af[0], af[1], af[2], af[3]);
 #pragma unroll
@@ -199,7 +202,7 @@ struct KeyState {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
+      for (int mt = 0; mt < kMT; ++mt) {
         o[nt][mt][0] *= al[nt][0];
         o[nt][mt][1] *= al[nt][1];
         o[nt][mt][2] *= al[nt][0];
@@ -227,10 +230,10 @@ struct KeyState {
     }
     // ---- O^T += V^T P^T (16 dims per m-tile)
 #pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
+    for (int mt = 0; mt < kMT; ++mt) {
       const int tok = li + ((mi >> 1) << 3);
       const int c = 2 * mt + (mi & 1);
-      const uint32_t addr = ((c >> 3) ? t.v1 : t.v0) + tok * 128 + (((c & 7) ^ li) << 4);
+      const uint32_t addr = t.v + (c >> 3) * kHalfBytes + tok * 128 + (((c & 7) ^ li) << 4);
       uint32_t va[4];
       ldmatrix_x4_trans(addr, va[0], va[1], va[2], va[3]);
       va[0] &= vm0;
@@ -257,7 +260,7 @@ struct KeyState {
       }
   }
 
-  // Stash (O, m, l) of every column into merge rows `rows` (kCombStride floats
+  // Stash (O, m, l) of every column into merge rows `rows` (D + 4 floats
   // apart; row = column index).
   __device__ __forceinline__ void stash(float* rows, int lane) const {
     const int r8 = lane >> 2, cq = lane & 3;
@@ -265,15 +268,38 @@ struct KeyState {
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        float* row = rows + (nt * 8 + 2 * cq + e) * kCombStride;
+        float* row = rows + (nt * 8 + 2 * cq + e) * (D + 4);
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
+        for (int mt = 0; mt < kMT; ++mt) {
           row[16 * mt + r8] = o[nt][mt][e];
           row[16 * mt + r8 + 8] = o[nt][mt][2 + e];
         }
         if (r8 == 0) {
-          row[kHeadDim] = m[nt][e];
-          row[kHeadDim + 1] = l[nt][e];
+          row[D] = m[nt][e];
+          row[D + 1] = l[nt][e];
+        }
+      }
+  }
+
+  // Fold a state stashed by another warp over a disjoint key range (same
+  // columns, same lane layout) into this one: O, m and l of the union.
+  __device__ __forceinline__ void absorb(const float* rows, int lane) {
+    const int r8 = lane >> 2, cq = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float* row = rows + (nt * 8 + 2 * cq + e) * (D + 4);
+        const float mo = row[D], lo = row[D + 1];
+        const float mn = fmaxf(m[nt][e], mo);
+        const float base = mn == -INFINITY ? 0.f : mn;
+        const float as = fast_exp2(m[nt][e] - base), ao = fast_exp2(mo - base);
+        m[nt][e] = mn;
+        l[nt][e] = l[nt][e] * as + lo * ao;
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt) {
+          o[nt][mt][e] = o[nt][mt][e] * as + row[16 * mt + r8] * ao;
+          o[nt][mt][2 + e] = o[nt][mt][2 + e] * as + row[16 * mt + r8 + 8] * ao;
         }
       }
   }

@@ -46,7 +46,7 @@ int build_view(const PlanConfig& cfg, const std::vector<Unit>& units, int grid_c
       const int nsplit = std::max(1, ceil_div(u.tiles, chunk));
       const int base = u.tiles / nsplit, extra = u.tiles % nsplit;
       int group = -1, part0 = -1;
-      const int rec = partial_rec_floats(u.rows);
+      const int rec = partial_rec_floats(u.rows, cfg.dim);
       if (nsplit > 1) {
         group = static_cast<int>(v.groups.size());
         part0 = static_cast<int>(v.partial_floats);
@@ -159,7 +159,7 @@ int build_cut_view(const PlanConfig& cfg, const std::vector<Unit>& units, int gr
   std::vector<int> group_of(units.size(), -1), part0_of(units.size(), -1), next_split(units.size(), 0);
   for (size_t i = 0; i < units.size(); ++i) {
     if (pieces[i] > 1) {
-      const int rec = partial_rec_floats(units[i].rows);
+      const int rec = partial_rec_floats(units[i].rows, cfg.dim);
       group_of[i] = static_cast<int>(v.groups.size());
       part0_of[i] = static_cast<int>(v.partial_floats);
       v.groups.push_back(SplitGroup{pieces[i], part0_of[i], rec, units[i].rows, units[i].seq,
@@ -187,7 +187,7 @@ int build_cut_view(const PlanConfig& cfg, const std::vector<Unit>& units, int gr
       it.kt1 = kt + take;
       const int s = next_split[i]++;
       it.group = group_of[i];
-      it.part = group_of[i] >= 0 ? part0_of[i] + s * partial_rec_floats(u.rows) : -1;
+      it.part = group_of[i] >= 0 ? part0_of[i] + s * partial_rec_floats(u.rows, cfg.dim) : -1;
       v.items.push_back(it);
       (u.key_mode ? v.decode_items : v.prefill_items)++;
       kt += take;
@@ -289,8 +289,8 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
     const int P = qrows * G;
     const int RB = ceil_div(P, kRowBlock);
     const int tiles_full = ceil_div(length, kTileTokens);
-    if (cfg.dim == kWideHeadDim) {
-      // 64-row items (four row blocks) per KV head, whatever the row count
+    if (cfg.dim == kWideHeadDim && RB > 1) {
+      // 64-row items (four row blocks) per KV head on the wide kernel
       for (int rb0 = 0; rb0 < RB; rb0 += 4) {
         const int nrb = std::min(4, RB - rb0);
         const int rows_valid = std::min(P, (rb0 + nrb) * kRowBlock) - rb0 * kRowBlock;
@@ -324,8 +324,9 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
   // when there is no row work); 2: decode work.
   View views[3];
   if (cfg.dim == kWideHeadDim) {
-    // one list for both masks, longest items first (the kernel deals them to
-    // its CTAs in a strided loop); no decode list, no splits
+    // multi-block rows: one list for both masks, longest items first (the
+    // wide kernel deals them to its CTAs in a strided loop, no splits);
+    // single-block rows: the decode list, cut exactly like head_dim 128
     std::stable_sort(row_units_full.begin(), row_units_full.end(),
                      [](const Unit& x, const Unit& y) { return x.tiles * x.nrb > y.tiles * y.nrb; });
     View& v = views[0];
@@ -355,7 +356,8 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
     for (int c = 0; c <= v.grid; ++c) v.cta_off[c] = c < v.grid ? c : n;
     v.chunk = 1 << 29;
     views[1] = v;
-    views[2].cta_off.clear();
+    const int rc = build_cut_view(cfg, key_units, cfg.dec_grid_cap, 8, fixed_grid, views[2], err);
+    if (rc != FE_OK) return rc;
   } else {
     const int row_min_chunk = cfg.row_split ? 16 : (1 << 29);
     int rc = build_view(cfg, row_units_full, cfg.grid_cap, 4, row_min_chunk, fixed_grid, views[0],

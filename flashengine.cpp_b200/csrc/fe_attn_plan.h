@@ -38,7 +38,8 @@ struct SeqInfo {  // 16 bytes
 //                 over all key tiles of the item (prefill / long verify).
 //   key_mode = 2: head_dim 256 (wide kernel): up to four row blocks against
 //                 every key of the sequence; the kernel derives the key range
-//                 from the mask.
+//                 from the mask. head_dim 256 sequences with a single row
+//                 block are key-mode (1) work of the decode kernel.
 // A packed row p is query row p / G of the sequence, query head kvh*G + p % G.
 struct WorkItem {  // 32 bytes
   int32_t seq;
@@ -54,7 +55,7 @@ struct WorkItem {  // 32 bytes
 struct SplitGroup {  // 32 bytes
   int32_t nsplit;      // 0 for the placeholder entries that keep row and decode ids apart
   int32_t part0;       // float offset of split 0's record; split s at part0 + s*rec_floats
-  int32_t rec_floats;  // rows*130 rounded up to a multiple of 4
+  int32_t rec_floats;  // rows*(dim+2) rounded up to a multiple of 4
   int32_t rows;        // valid packed rows in each record
   int32_t seq, kvh;    // the unit's sequence and first KV head (where merged rows go)
   int32_t pad[2];
@@ -105,6 +106,10 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
 #define FE_HOST_DEVICE
 #endif
 
-FE_HOST_DEVICE inline int partial_rec_floats(int rows) { return ((rows * (kHeadDim + 2)) + 3) & ~3; }
+// Floats of one split record of `rows` rows: O[rows][dim], m[rows], l[rows],
+// padded to a multiple of 4 (16-byte aligned records).
+FE_HOST_DEVICE inline int partial_rec_floats(int rows, int dim = kHeadDim) {
+  return ((rows * (dim + 2)) + 3) & ~3;
+}
 
 }  // namespace fe

@@ -31,9 +31,9 @@
 
 namespace fe {
 
-int decode_launch(int dtype, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
+int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
-int decode_merge_launch(int dtype, const void* args, int grid, cudaStream_t stream);
+int decode_merge_launch(int dtype, int dim, const void* args, int grid, cudaStream_t stream);
 int decode_smem_bytes(int heads);
 
 namespace {
@@ -41,13 +41,29 @@ namespace {
 constexpr int kDecWarps = 8;
 constexpr int kDecThreads = (kDecWarps + 1) * 32;
 
-template <int H>
+// H KV heads of D dims per item. head_dim 128: the 8/H warps of a head merge
+// through kDecWarps 16-row slots. head_dim 256 (H <= 2): a tile is 8 KiB per
+// head for K and for V, so stages hold 1-2 heads; warps are grouped per (head,
+// 8-column half) and merge pairwise in log2 rounds through kDecWarps/2 slots
+// of 8 rows.
+//
+// The warps sharing a head take tiles j, j + w, j + 2w, ... (w warps); the
+// stage count is a multiple of w, so the tile that last used a warp's stage is
+// that warp's own earlier tile: a warp never waits on a stage's full barrier
+// while the phase before the one it wants is still pending (the parity test
+// would pass a phase early). Items end with a merge barrier of all consumer
+// warps, so this holds across items too.
+template <int H, int D = kHeadDim>
 struct DecCfg {
-  static constexpr int kWh = kDecWarps / H;  // warps per head
-  static constexpr int kKBytes = 2 * H * kHalfBytes;
+  static constexpr int kQ = D / 64;          // 64-dim boxes per head
+  static constexpr int kWh = kDecWarps / H;  // warps per head (most per group)
+  static constexpr int kKBytes = kQ * H * kHalfBytes;
   static constexpr int kStageBytes = 2 * kKBytes;
-  static constexpr int kStages = H == 8 ? 3 : (H == 4 ? 4 : 8);
-  static constexpr int kCombBytes = kWh > 1 ? kDecWarps * kRowBlock * kCombStride * 4 : 0;
+  static constexpr int kStages = D == kHeadDim ? (H == 8 ? 3 : (H == 4 ? 4 : 8)) : (H == 2 ? 4 : 8);
+  static_assert(kStages % kWh == 0 || kWh == 1, "stage count must be a multiple of the warps per head");
+  static constexpr int kCombBytes =
+      D == kHeadDim ? (kWh > 1 ? kDecWarps * kRowBlock * kCombStride * 4 : 0)
+                    : (kDecWarps / 2) * 8 * (D + 4) * 4;
   static constexpr int kBarOff = kStages * kStageBytes + kCombBytes;
   static constexpr int kSmem = 1024 + kBarOff + 2 * kStages * 8 + 16;
 };
@@ -88,10 +104,8 @@ __device__ __forceinline__ void decode_item(const AttnArgs<T>& a, const WorkItem
     }
     const uint32_t base = smem_u32(stages + s * C::kStageBytes);
     TileAddr t;
-    t.k0 = base + (2 * hh) * kHalfBytes;
-    t.k1 = t.k0 + kHalfBytes;
-    t.v0 = t.k0 + C::kKBytes;
-    t.v1 = t.v0 + kHalfBytes;
+    t.k = base + (2 * hh) * kHalfBytes;
+    t.v = t.k + C::kKBytes;
     ks.tile(t, (wi.kt0 + jt) * kTileTokens, si.length, a.scale_log2, lane);
     __syncwarp();
     if (lane == 0) mbar_arrive_cnt(&empty[s], C::kWh);
@@ -206,12 +220,95 @@ __device__ __forceinline__ void decode_item(const AttnArgs<T>& a, const WorkItem
   }
 }
 
+// head_dim 256: warp w serves group w % (H*C) = (head hh, column half ch),
+// C = 2 when the item has more than 8 packed rows; the kWh = 8/(H*C) warps of
+// a group take alternate tiles, then fold their states pairwise (round `step`:
+// warps step..2*step-1 of the group stash, warps 0..step-1 absorb), so the
+// group's first warp ends with the item's whole key range.
 template <typename T, int H>
+__device__ __forceinline__ void decode_item_d256(const AttnArgs<T>& a, const WorkItem& wi,
+                                                 const SeqInfo& si, uint8_t* stages,
+                                                 uint64_t* full, uint64_t* empty,
+                                                 volatile int* flags, float* comb, int w, int lane,
+                                                 uint32_t& g, bool& aborted) {
+  constexpr int D = kWideHeadDim;
+  using C = DecCfg<H, D>;
+  const int G = a.G;
+  const int P = si.qrows * G;
+  const int halves = P > 8 ? 2 : 1;
+  const int groups = H * halves;
+  const int kwh = kDecWarps / groups;
+  const int grp = w % groups, sub = w / groups;
+  const int hh = grp % H, ch = grp / H;
+  const int head0 = (wi.kvh + hh) * G;
+  const bool causal = a.view == 1;
+  KeyState<T, 1, D> ks;
+  ks.init(a.q, a.hq, si.q_row0, si.qrows, si.length, head0, G, causal, lane, ch * 8);
+
+  const int ntiles = wi.kt1 - wi.kt0;
+  for (int jt = sub; jt < ntiles; jt += kwh) {
+    const uint32_t gg = g + jt;
+    const int s = gg % C::kStages;
+    if (aborted || flags[0] || !wait_bounded(&full[s], (gg / C::kStages) & 1u, flags)) {
+      aborted = true;
+      break;
+    }
+    const uint32_t base = smem_u32(stages + s * C::kStageBytes);
+    TileAddr t;
+    t.k = base + (C::kQ * hh) * kHalfBytes;
+    t.v = t.k + C::kKBytes;
+    ks.tile(t, (wi.kt0 + jt) * kTileTokens, si.length, a.scale_log2, lane);
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cnt(&empty[s], kwh);
+  }
+  g += ntiles;
+  ks.reduce_l();
+
+  constexpr int kSlot = 8 * (D + 4);  // floats per stash slot (8 columns)
+  for (int step = kwh >> 1; step >= 1; step >>= 1) {
+    if (sub >= step && sub < 2 * step) ks.stash(comb + ((sub - step) * groups + grp) * kSlot, lane);
+    named_barrier_sync(1, kDecWarps * 32);
+    if (sub < step) ks.absorb(comb + (sub * groups + grp) * kSlot, lane);
+    named_barrier_sync(1, kDecWarps * 32);
+  }
+  if (sub != 0 || aborted) return;
+
+  const int r8 = lane >> 2, cq = lane & 3;
+  const int R = H * P;  // rows of the item's record: head-major, then packed row
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int p = ch * 8 + 2 * cq + e;
+    if (p >= P) continue;
+    if (wi.group < 0) {
+      const float inv = 1.f / ks.l[0][e];
+      T* dst = a.out + (static_cast<int64_t>(si.q_row0 + p / G) * a.hq + head0 + p % G) * D;
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt) {
+        dst[16 * mt + r8] = to_elem<T>(ks.o[0][mt][e] * inv);
+        dst[16 * mt + r8 + 8] = to_elem<T>(ks.o[0][mt][2 + e] * inv);
+      }
+    } else {
+      float* rec = a.partials + wi.part;
+      float* row = rec + (hh * P + p) * D;
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt) {
+        row[16 * mt + r8] = ks.o[0][mt][e];
+        row[16 * mt + r8 + 8] = ks.o[0][mt][2 + e];
+      }
+      if (r8 == 0) {
+        rec[R * D + hh * P + p] = ks.m[0][e];
+        rec[R * (D + 1) + hh * P + p] = ks.l[0][e];
+      }
+    }
+  }
+}
+
+template <typename T, int H, int D>
 __global__ void __launch_bounds__(kDecThreads, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const AttnArgs<T> a,
                         int per_head_tma) {
-  using C = DecCfg<H>;
+  using C = DecCfg<H, D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -260,7 +357,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     for (int it = it0; it < it1 && ok; ++it) {
       const WorkItem w = items[it];
       const SeqInfo si = seqs[w.seq];
-      const int hh0 = w.kvh * 2;
+      const int hh0 = w.kvh * C::kQ;  // first 64-dim box of the item's heads
       // Slots of 32 tiles are fetched per batch (one per lane); the next
       // batch is requested before the current one is consumed.
       auto tile_slot = [&](int j) -> int {
@@ -288,7 +385,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                 tma_load_3d(st, &kmap, &full[s], 0, s0, hh0);
                 tma_load_3d(st + C::kKBytes, &vmap, &full[s], 0, s0, hh0);
               } else {
-                for (int x = 0; x < 2 * H; ++x) {
+                for (int x = 0; x < C::kQ * H; ++x) {
                   tma_load_3d(st + x * kHalfBytes, &kmap, &full[s], 0, hh0 + x, s0);
                   tma_load_3d(st + C::kKBytes + x * kHalfBytes, &vmap, &full[s], 0, hh0 + x, s0);
                 }
@@ -323,7 +420,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   for (int it = it0; it < it1; ++it) {
     const WorkItem wi = items[it];
     const SeqInfo si = seqs[wi.seq];
-    if (si.qrows * a.G <= 8)
+    if constexpr (D != kHeadDim)
+      decode_item_d256<T, H>(a, wi, si, stages, full, empty, flags, comb, warp, lane, g, aborted);
+    else if (si.qrows * a.G <= 8)
       decode_item<T, H, 1, false>(a, wi, si, groups, stages, full, empty, flags, comb, warp, lane,
                                   g, aborted);
     else
@@ -333,18 +432,18 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   if (aborted && lane == 0) raise_device_error(a.err, FE_DEVERR_TIMEOUT);
 }
 
-template <typename T, int H>
+template <typename T, int H, int D = kHeadDim>
 int launch_t(const CUtensorMap& kmap, const CUtensorMap& vmap, bool per_head_tma,
              const AttnArgs<T>& args, int grid, cudaStream_t stream) {
-  using C = DecCfg<H>;
+  using C = DecCfg<H, D>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(paged_decode_kernel<T, H>,
+    attr_err = cudaFuncSetAttribute(paged_decode_kernel<T, H, D>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "paged_decode_kernel attribute");
-  FE_CUDA_TRY(launch_pdl(paged_decode_kernel<T, H>, dim3(grid), dim3(kDecThreads), C::kSmem,
+  FE_CUDA_TRY(launch_pdl(paged_decode_kernel<T, H, D>, dim3(grid), dim3(kDecThreads), C::kSmem,
                          stream, kmap, vmap, args, per_head_tma ? 1 : 0));
   return FE_OK;
 }
@@ -372,12 +471,15 @@ namespace {
 // early finishers free and start when that grid has completed.
 constexpr int kMergeThreads = 1024;
 
-template <typename T>
+// Records of a D-dim split unit: O[rows][D] unnormalised, then m[rows], l[rows].
+template <typename T, int D>
 __device__ __forceinline__ void merge_row_warp(const float* partials, const SplitGroup& gi, int r,
                                                int lane, T* out_row) {
+  constexpr int kV = D / 128;  // float4 vectors per lane
   const int ns = gi.nsplit;
-  const int d4 = lane * 4;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 acc[kV];
+#pragma unroll
+  for (int v = 0; v < kV; ++v) acc[v] = make_float4(0.f, 0.f, 0.f, 0.f);
   float M = -INFINITY, L = 0.f;
   for (int s0 = 0; s0 < ns; s0 += 32) {
     // this chunk's maxima and sums: split s0 + lane per lane
@@ -385,8 +487,8 @@ __device__ __forceinline__ void merge_row_warp(const float* partials, const Spli
     float m = -INFINITY, l = 0.f;
     if (sl < ns) {
       const float* rec = partials + gi.part0 + static_cast<int64_t>(sl) * gi.rec_floats;
-      m = __ldcg(rec + gi.rows * kHeadDim + r);
-      l = __ldcg(rec + gi.rows * (kHeadDim + 1) + r);
+      m = __ldcg(rec + gi.rows * D + r);
+      l = __ldcg(rec + gi.rows * (D + 1) + r);
     }
     float mc = m;
 #pragma unroll
@@ -395,10 +497,13 @@ __device__ __forceinline__ void merge_row_warp(const float* partials, const Spli
     const float base = M_new == -INFINITY ? 0.f : M_new;
     // rescale what the earlier chunks accumulated
     const float resc = M == -INFINITY ? 0.f : fast_exp2(M - base);
-    acc.x *= resc;
-    acc.y *= resc;
-    acc.z *= resc;
-    acc.w *= resc;
+#pragma unroll
+    for (int v = 0; v < kV; ++v) {
+      acc[v].x *= resc;
+      acc[v].y *= resc;
+      acc[v].z *= resc;
+      acc[v].w *= resc;
+    }
     L *= resc;
     M = M_new;
     const float sc = sl < ns ? fast_exp2(m - base) : 0.f;
@@ -410,19 +515,25 @@ __device__ __forceinline__ void merge_row_warp(const float* partials, const Spli
 #pragma unroll 4
     for (int j = 0; j < n; ++j) {
       const float* rec = partials + gi.part0 + static_cast<int64_t>(s0 + j) * gi.rec_floats;
-      const float4 x = __ldcg(reinterpret_cast<const float4*>(rec + r * kHeadDim + d4));
       const float w = __shfl_sync(0xffffffffu, sc, j);
-      acc.x = fmaf(x.x, w, acc.x);
-      acc.y = fmaf(x.y, w, acc.y);
-      acc.z = fmaf(x.z, w, acc.z);
-      acc.w = fmaf(x.w, w, acc.w);
+#pragma unroll
+      for (int v = 0; v < kV; ++v) {
+        const float4 x = __ldcg(reinterpret_cast<const float4*>(rec + r * D + v * 128 + lane * 4));
+        acc[v].x = fmaf(x.x, w, acc[v].x);
+        acc[v].y = fmaf(x.y, w, acc[v].y);
+        acc[v].z = fmaf(x.z, w, acc[v].z);
+        acc[v].w = fmaf(x.w, w, acc[v].w);
+      }
     }
   }
   const float inv = 1.f / L;
-  store4<T>(out_row + d4, acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+#pragma unroll
+  for (int v = 0; v < kV; ++v)
+    store4<T>(out_row + v * 128 + lane * 4, acc[v].x * inv, acc[v].y * inv, acc[v].z * inv,
+              acc[v].w * inv);
 }
 
-template <typename T>
+template <typename T, int D>
 __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const AttnArgs<T> a) {
   pdl_trigger();
   pdl_wait();
@@ -440,31 +551,40 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const AttnA
     for (int r = warp; r < gi.rows; r += kMergeThreads / 32) {
       const int rh = r / P, p = r % P;
       T* dst = a.out + (static_cast<int64_t>(si.q_row0 + p / G) * a.hq + (gi.kvh + rh) * G +
-                        p % G) * kHeadDim;
-      merge_row_warp<T>(a.partials, gi, r, lane, dst);
+                        p % G) * D;
+      merge_row_warp<T, D>(a.partials, gi, r, lane, dst);
     }
   }
 }
 
 template <typename T>
-int launch_merge_t(const AttnArgs<T>& args, int grid, cudaStream_t stream) {
-  FE_CUDA_TRY(launch_pdl(decode_merge_kernel<T>, dim3(grid), dim3(kMergeThreads), 0, stream, args));
+int launch_merge_t(const AttnArgs<T>& args, int dim, int grid, cudaStream_t stream) {
+  if (dim == kWideHeadDim)
+    FE_CUDA_TRY(launch_pdl(decode_merge_kernel<T, kWideHeadDim>, dim3(grid), dim3(kMergeThreads), 0,
+                           stream, args));
+  else
+    FE_CUDA_TRY(launch_pdl(decode_merge_kernel<T, kHeadDim>, dim3(grid), dim3(kMergeThreads), 0,
+                           stream, args));
   return FE_OK;
 }
 
 }  // namespace
 
-int decode_merge_launch(int dtype, const void* args, int grid, cudaStream_t stream) {
+int decode_merge_launch(int dtype, int dim, const void* args, int grid, cudaStream_t stream) {
   if (grid <= 0) return FE_OK;
   if (dtype == FE_DTYPE_BF16)
-    return launch_merge_t(*static_cast<const AttnArgs<__nv_bfloat16>*>(args), grid, stream);
-  return launch_merge_t(*static_cast<const AttnArgs<__half>*>(args), grid, stream);
+    return launch_merge_t(*static_cast<const AttnArgs<__nv_bfloat16>*>(args), dim, grid, stream);
+  return launch_merge_t(*static_cast<const AttnArgs<__half>*>(args), dim, grid, stream);
 }
 
-int decode_launch(int dtype, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
+int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream) {
   if (dtype == FE_DTYPE_BF16) {
     const auto& a = *static_cast<const AttnArgs<__nv_bfloat16>*>(args);
+    if (dim == kWideHeadDim)
+      return heads == 2
+                 ? launch_t<__nv_bfloat16, 2, kWideHeadDim>(kmap, vmap, per_head_tma, a, grid, stream)
+                 : launch_t<__nv_bfloat16, 1, kWideHeadDim>(kmap, vmap, per_head_tma, a, grid, stream);
     switch (heads) {
       case 8: return launch_t<__nv_bfloat16, 8>(kmap, vmap, per_head_tma, a, grid, stream);
       case 4: return launch_t<__nv_bfloat16, 4>(kmap, vmap, per_head_tma, a, grid, stream);
@@ -473,6 +593,9 @@ int decode_launch(int dtype, int heads, const CUtensorMap& kmap, const CUtensorM
     }
   }
   const auto& a = *static_cast<const AttnArgs<__half>*>(args);
+  if (dim == kWideHeadDim)
+    return heads == 2 ? launch_t<__half, 2, kWideHeadDim>(kmap, vmap, per_head_tma, a, grid, stream)
+                      : launch_t<__half, 1, kWideHeadDim>(kmap, vmap, per_head_tma, a, grid, stream);
   switch (heads) {
     case 8: return launch_t<__half, 8>(kmap, vmap, per_head_tma, a, grid, stream);
     case 4: return launch_t<__half, 4>(kmap, vmap, per_head_tma, a, grid, stream);

@@ -159,8 +159,11 @@ int fe_accept(const int64_t* draft, const int64_t* verify, int64_t* out, int bat
  * ------------------------------------------------------------------------ */
 typedef struct fe_attn_plan fe_attn_plan;
 
-/* head_dim must be 128 (as src/flashinfer_attention.cu:23 requires); page a
- * multiple of 16; hq a multiple of hkv with hq/hkv <= 16.
+/* head_dim 128 (as src/flashinfer_attention.cu:23 requires) or 256 (the
+ * full-attention layers of hybrid and DFlash draft models, which the reference
+ * serves through ATen with any head_dim: src/hybrid_model.cpp:98,
+ * src/block_draft.cpp:38); page a multiple of 16; hq a multiple of hkv with
+ * hq/hkv <= 16.
  * max_pages = per-sequence page capacity (the reference passes
  * ceil(max_model_len/page)+1, src/cuda_model.cpp:118). Allocates the plan's
  * fixed device workspaces on the current device. */

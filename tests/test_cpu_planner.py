@@ -153,30 +153,47 @@ def test_zero_row_sequences_are_skipped():
     assert set(seqs) == {1}
 
 
-def test_head_dim_256_plan_is_one_row_list():
-    """head_dim 256 plans put every (sequence, KV head, 64-row block) on the
-    row lists for the wide kernel (both masks), longest first, with no decode
-    list and no splits."""
-    # a decode row, a 100-row chunk and a 3-row block
+def test_head_dim_256_plan_lists():
+    """head_dim 256 plans put every (sequence, KV head, 64-row block) of the
+    multi-block sequences on the row lists for the wide kernel (both masks),
+    longest first, unsplit; sequences whose packed rows fit one 16-row block
+    go to the decode list (two KV heads per item), cut exactly like head_dim
+    128, with split records of rows x (256 + 2) floats."""
+    # a decode row, a 100-row chunk, a 3-row block and a long decode row
     from fekv.metadata import build_step_metadata
-    tables = [np.arange(i * 200, i * 200 + 200) for i in range(3)]
-    md = build_step_metadata(tables, [40, 2900, 700], [1, 100, 3], 16)
-    hp = HostPlan(16, 2, 256, 16, 3, 200, True, 600, grid_cap=8)
+    tables = [np.arange(i * 400, i * 400 + 400) for i in range(4)]
+    md = build_step_metadata(tables, [40, 2900, 700, 6000], [1, 100, 3, 1], 16)
+    hp = HostPlan(16, 2, 256, 16, 4, 400, True, 1600, grid_cap=8)
     meta = hp.prepare(md.qo, md.kv, md.pages, md.last)
     G = 8
-    want = sum(-(-int(r) * G // 64) * 2 for r in np.diff(md.qo))
+    q = np.diff(md.qo)
+    multi = [b for b in range(4) if q[b] * G > 16]
+    want = sum(-(-int(q[b]) * G // 64) * 2 for b in multi)
     v0, v1, v2 = meta["views"]
     assert len(v0["items"]) == want and len(v1["items"]) == want
     np.testing.assert_array_equal(v0["items"], v1["items"])
-    assert len(v2["items"]) == 0 and len(v0["groups"]) == 0
+    assert len(v0["groups"]) == 0
     assert (v0["items"]["key_mode"] == 2).all() and (v0["items"]["part"] == -1).all()
+    assert set(v0["items"]["seq"]) == set(multi)
     cost = (v0["items"]["kt1"] - v0["items"]["kt0"]) * v0["items"]["nrb"]
     assert (np.diff(cost) <= 0).all()
     # rows covered exactly once per KV head
-    for b, q in enumerate(np.diff(md.qo)):
+    for b in multi:
         for h in range(2):
             its = v0["items"][(v0["items"]["seq"] == b) & (v0["items"]["kvh"] == h)]
             rows = sorted(r for it in its for r in range(int(it["rb0"]) * 16,
-                                                         min(int(q) * G, (int(it["rb0"]) + int(it["nrb"])) * 16)))
-            assert rows == list(range(int(q) * G))
+                                                         min(int(q[b]) * G, (int(it["rb0"]) + int(it["nrb"])) * 16)))
+            assert rows == list(range(int(q[b]) * G))
+    # decode list: both KV heads in one unit, key tiles covered exactly once
+    it2 = v2["items"]
+    assert set(it2["seq"]) == {0, 3} and (it2["kvh"] == 0).all() and (it2["key_mode"] == 1).all()
+    for b in (0, 3):
+        its = np.sort(it2[it2["seq"] == b], order="kt0")
+        tiles = -(-((int(md.kv[b + 1] - md.kv[b]) - 1) * 16 + int(md.last[b])) // 16)
+        assert its["kt0"][0] == 0 and its["kt1"][-1] == tiles
+        assert (its["kt0"][1:] == its["kt1"][:-1]).all()
+    split = v2["groups"][v2["groups"]["nsplit"] > 1]
+    assert len(split) >= 1
+    for gi in split:
+        assert gi["rows"] == 2 * G and gi["rec_floats"] == (2 * G * 258 + 3) // 4 * 4
     hp.close()
