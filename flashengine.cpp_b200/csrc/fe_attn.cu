@@ -26,7 +26,8 @@ namespace fe {
 
 int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
-int decode_merge_launch(int dtype, int dim, const void* args, int grid, cudaStream_t stream);
+int decode_merge_launch(int dtype, int dim, int list, const void* args, int grid,
+                        cudaStream_t stream);
 int wide_launch(int dtype, const void* args, const void* k_pool, const void* v_pool, int hkv,
                 int grid, cudaStream_t stream);
 int prefill_tc_launch(int dtype, const CUtensorMap& kmap, const CUtensorMap& vmap,
@@ -163,7 +164,9 @@ struct fe_attn_plan {
 namespace {
 
 size_t meta_capacity(const PlanConfig& c) {
-  size_t per_view = sizeof(int32_t) * (std::max(c.grid_cap, c.dec_grid_cap) + 1) +
+  // the wide kernel (head_dim 256) runs two CTAs per SM on the row lists
+  const int row_grid = c.dim == kWideHeadDim ? 2 * c.grid_cap : c.grid_cap;
+  size_t per_view = sizeof(int32_t) * (std::max(row_grid, c.dec_grid_cap) + 1) +
                     sizeof(WorkItem) * c.max_items + sizeof(SplitGroup) * c.max_groups + 64;
   return sizeof(MetaHeader) + 3 * per_view + sizeof(SeqInfo) * c.max_batch +
          sizeof(int32_t) * size_t(c.max_batch) * c.max_pages + 256;
@@ -524,11 +527,11 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
     if (rc != FE_OK) return rc;
     q_map_rows = h.rows;
   }
-  // head_dim 256 row work runs on the wide kernel, two 96 KiB CTAs per SM
-  const int grid_wide =
-      !wide || grid_rows == 0
-          ? 0
-          : (p->fixed_grid ? 2 * p->cfg.grid_cap : std::min(h.n_items[view], 2 * p->cfg.grid_cap));
+  // head_dim 256 row work runs on the wide kernel, two 96 KiB CTAs per SM,
+  // and its split pieces are merged by the merge kernel over the row list
+  const int grid_wide = !wide || grid_rows == 0 ? 0 : (p->fixed_grid ? 2 * p->cfg.grid_cap : h.grid[view]);
+  const int grid_wide_merge =
+      grid_wide == 0 ? 0 : (p->fixed_grid ? p->cfg.grid_cap : h.n_groups[view]);
   const float scale_log2 = 1.4426950408889634f / sqrtf(float(dim));
   auto s = static_cast<cudaStream_t>(stream);
   const int G = p->cfg.hq / p->cfg.hkv;
@@ -537,10 +540,14 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
   auto launch_all = [&](const auto& a) -> int {
     if (grid_dec > 0) {
       int rc = decode_launch(p->dtype, dim, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
-      if (rc == FE_OK) rc = decode_merge_launch(p->dtype, dim, &a, grid_merge, s);
+      if (rc == FE_OK) rc = decode_merge_launch(p->dtype, dim, 2, &a, grid_merge, s);
       if (rc != FE_OK) return rc;
     }
-    if (wide) return wide_launch(p->dtype, &a, k_pool, v_pool, p->cfg.hkv, grid_wide, s);
+    if (wide) {
+      int rc = wide_launch(p->dtype, &a, k_pool, v_pool, p->cfg.hkv, grid_wide, s);
+      if (rc == FE_OK) rc = decode_merge_launch(p->dtype, dim, view, &a, grid_wide_merge, s);
+      return rc;
+    }
     if (grid_rows > 0)
       return prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, qmap, &a, grid_rows, s);
     return FE_OK;

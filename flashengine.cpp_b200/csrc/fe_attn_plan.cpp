@@ -50,7 +50,11 @@ int build_view(const PlanConfig& cfg, const std::vector<Unit>& units, int grid_c
       if (nsplit > 1) {
         group = static_cast<int>(v.groups.size());
         part0 = static_cast<int>(v.partial_floats);
-        v.groups.push_back(SplitGroup{nsplit, part0, rec, u.rows, u.seq, u.kvh, {0, 0}});
+        // key-mode records hold all of the sequence's rows; row-mode ones
+        // hold the unit's rows of one KV head from packed row rb0*16
+        const bool rows_rec = u.key_mode != 1;
+        v.groups.push_back(SplitGroup{nsplit, part0, rec, u.rows, u.seq, u.kvh,
+                                      rows_rec ? u.rb0 * kRowBlock : 0, rows_rec ? u.rows : 0});
         v.partial_floats += int64_t(rec) * nsplit;
         ++v.split_units;
       }
@@ -69,7 +73,7 @@ int build_view(const PlanConfig& cfg, const std::vector<Unit>& units, int grid_c
         it.group = group;
         kt += n;
         v.items.push_back(it);
-        (u.key_mode ? v.decode_items : v.prefill_items)++;
+        (u.key_mode == 1 ? v.decode_items : v.prefill_items)++;
       }
     }
     if (static_cast<int>(v.items.size()) > cfg.max_items || v.partial_floats > cfg.partial_capacity ||
@@ -94,7 +98,7 @@ int build_view(const PlanConfig& cfg, const std::vector<Unit>& units, int grid_c
   for (int i = 0; i < n; ++i) {
     const auto& it = v.items[i];
     const int64_t tiles = it.kt1 - it.kt0;
-    const int64_t cost = (it.key_mode ? tiles : tiles * it.nrb) + 4;
+    const int64_t cost = (it.key_mode == 1 ? tiles : tiles * it.nrb) + 4;
     order[i] = {cost, i};
   }
   std::stable_sort(order.begin(), order.end(),
@@ -163,7 +167,7 @@ int build_cut_view(const PlanConfig& cfg, const std::vector<Unit>& units, int gr
       group_of[i] = static_cast<int>(v.groups.size());
       part0_of[i] = static_cast<int>(v.partial_floats);
       v.groups.push_back(SplitGroup{pieces[i], part0_of[i], rec, units[i].rows, units[i].seq,
-                                    units[i].kvh, {0, 0}});
+                                    units[i].kvh, 0, 0});
       v.partial_floats += int64_t(rec) * pieces[i];
       ++v.split_units;
     }
@@ -291,11 +295,16 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
     const int tiles_full = ceil_div(length, kTileTokens);
     if (cfg.dim == kWideHeadDim && RB > 1) {
       // 64-row items (four row blocks) per KV head on the wide kernel
-      for (int rb0 = 0; rb0 < RB; rb0 += 4) {
-        const int nrb = std::min(4, RB - rb0);
-        const int rows_valid = std::min(P, (rb0 + nrb) * kRowBlock) - rb0 * kRowBlock;
-        for (int h = 0; h < cfg.hkv; ++h)
+      for (int rb0 = 0; rb0 < RB; rb0 += kWideRowBlocks) {
+        const int nrb = std::min(kWideRowBlocks, RB - rb0);
+        const int last_row = std::min(P, (rb0 + nrb) * kRowBlock) - 1;
+        const int rows_valid = last_row + 1 - rb0 * kRowBlock;
+        const int64_t limit = length - qrows + last_row / G + 1;  // bottom-right causal
+        const int tiles_causal = ceil_div(limit, kTileTokens);
+        for (int h = 0; h < cfg.hkv; ++h) {
           row_units_full.push_back(Unit{b, h, 2, rb0, nrb, tiles_full, rows_valid});
+          row_units_causal.push_back(Unit{b, h, 2, rb0, nrb, tiles_causal, rows_valid});
+        }
       }
       continue;
     }
@@ -324,39 +333,16 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
   // when there is no row work); 2: decode work.
   View views[3];
   if (cfg.dim == kWideHeadDim) {
-    // multi-block rows: one list for both masks, longest items first (the
-    // wide kernel deals them to its CTAs in a strided loop, no splits);
-    // single-block rows: the decode list, cut exactly like head_dim 128
-    std::stable_sort(row_units_full.begin(), row_units_full.end(),
-                     [](const Unit& x, const Unit& y) { return x.tiles * x.nrb > y.tiles * y.nrb; });
-    View& v = views[0];
-    for (const Unit& u : row_units_full) {
-      WorkItem it;
-      it.seq = u.seq;
-      it.kvh = static_cast<int16_t>(u.kvh);
-      it.key_mode = static_cast<int16_t>(u.key_mode);
-      it.rb0 = u.rb0;
-      it.nrb = u.nrb;
-      it.kt0 = 0;
-      it.kt1 = u.tiles;
-      it.part = -1;
-      it.group = -1;
-      v.items.push_back(it);
-    }
-    v.prefill_items = static_cast<int>(v.items.size());
-    if (static_cast<int>(v.items.size()) > cfg.max_items) {
-      err = "attention work exceeds the plan's item capacity";
-      return FE_ERR_CAPACITY;
-    }
-    // (the wide kernel deals items by index and does not read cta_off; it
-    // records one item per CTA for introspection)
-    const int n = static_cast<int>(v.items.size());
-    v.grid = n == 0 ? 0 : std::min(n, 2 * std::max(1, cfg.grid_cap));
-    v.cta_off.assign(v.grid + 1, 0);
-    for (int c = 0; c <= v.grid; ++c) v.cta_off[c] = c < v.grid ? c : n;
-    v.chunk = 1 << 29;
-    views[1] = v;
-    const int rc = build_cut_view(cfg, key_units, cfg.dec_grid_cap, 8, fixed_grid, views[2], err);
+    // multi-block rows: the wide kernel (two CTAs per SM), key ranges split
+    // into pieces of at least kWideMinChunk tiles when there are fewer
+    // items than CTAs; single-block rows: the decode list, cut exactly like
+    // head_dim 128
+    const int wide_cap = 2 * cfg.grid_cap;
+    int rc = build_view(cfg, row_units_full, wide_cap, 1, kWideMinChunk, fixed_grid, views[0], err);
+    if (rc != FE_OK) return rc;
+    rc = build_view(cfg, row_units_causal, wide_cap, 1, kWideMinChunk, fixed_grid, views[1], err);
+    if (rc != FE_OK) return rc;
+    rc = build_cut_view(cfg, key_units, cfg.dec_grid_cap, 8, fixed_grid, views[2], err);
     if (rc != FE_OK) return rc;
   } else {
     const int row_min_chunk = cfg.row_split ? 16 : (1 << 29);

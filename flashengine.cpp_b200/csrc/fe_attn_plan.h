@@ -18,7 +18,9 @@
 namespace fe {
 
 constexpr int kHeadDim = 128;
-constexpr int kWideHeadDim = 256;  // served by the separate wide kernel (fe_wide.cu)
+constexpr int kWideHeadDim = 256;  // rows: fe_wide.cu; single-block sequences: fe_decode.cu
+constexpr int kWideRowBlocks = 4;  // 16-row blocks per wide-kernel item (64 packed rows)
+constexpr int kWideMinChunk = 16;  // fewest key tiles in a split piece of a wide item
 constexpr int kTileTokens = 16;   // key tokens per tile (one TMA box per K/V half)
 constexpr int kRowBlock = 16;     // packed query rows per mma row block
 
@@ -37,9 +39,9 @@ struct SeqInfo {  // 16 bytes
 //   key_mode = 0: up to eight row blocks (one 128-row tcgen05 tile), each
 //                 over all key tiles of the item (prefill / long verify).
 //   key_mode = 2: head_dim 256 (wide kernel): up to four row blocks against
-//                 every key of the sequence; the kernel derives the key range
-//                 from the mask. head_dim 256 sequences with a single row
-//                 block are key-mode (1) work of the decode kernel.
+//                 key tiles [kt0, kt1) (cut to the mask's range), split
+//                 across CTAs like key mode. head_dim 256 sequences with a
+//                 single row block are key-mode (1) work of the decode kernel.
 // A packed row p is query row p / G of the sequence, query head kvh*G + p % G.
 struct WorkItem {  // 32 bytes
   int32_t seq;
@@ -58,7 +60,9 @@ struct SplitGroup {  // 32 bytes
   int32_t rec_floats;  // rows*(dim+2) rounded up to a multiple of 4
   int32_t rows;        // valid packed rows in each record
   int32_t seq, kvh;    // the unit's sequence and first KV head (where merged rows go)
-  int32_t pad[2];
+  // record row r is packed row row0 + r % rph of KV head kvh + r / rph, with
+  // rph = rows_per_head, or the sequence's packed rows (qrows x G) when 0
+  int32_t row0, rows_per_head;
 };
 
 // Byte offsets are from the start of the metadata buffer. Index [c] of the

@@ -33,7 +33,8 @@ namespace fe {
 
 int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
-int decode_merge_launch(int dtype, int dim, const void* args, int grid, cudaStream_t stream);
+int decode_merge_launch(int dtype, int dim, int list, const void* args, int grid,
+                        cudaStream_t stream);
 int decode_smem_bytes(int heads);
 
 namespace {
@@ -534,12 +535,13 @@ __device__ __forceinline__ void merge_row_warp(const float* partials, const Spli
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const AttnArgs<T> a) {
+__global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const AttnArgs<T> a,
+                                                                     int list) {
   pdl_trigger();
   pdl_wait();
   const MetaHeader* hdr = reinterpret_cast<const MetaHeader*>(a.meta);
-  const int n = hdr->n_groups[2];
-  const SplitGroup* groups = reinterpret_cast<const SplitGroup*>(a.meta + hdr->groups_off[2]);
+  const int n = hdr->n_groups[list];
+  const SplitGroup* groups = reinterpret_cast<const SplitGroup*>(a.meta + hdr->groups_off[list]);
   const SeqInfo* seqs = reinterpret_cast<const SeqInfo*>(a.meta + hdr->seqs_off);
   const int G = a.G;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -547,9 +549,9 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const AttnA
     const SplitGroup gi = groups[gidx];
     if (gi.nsplit < 2) continue;  // placeholder ids of the row lists
     const SeqInfo si = seqs[gi.seq];
-    const int P = si.qrows * G;
+    const int rph = gi.rows_per_head > 0 ? gi.rows_per_head : si.qrows * G;
     for (int r = warp; r < gi.rows; r += kMergeThreads / 32) {
-      const int rh = r / P, p = r % P;
+      const int rh = r / rph, p = gi.row0 + r % rph;
       T* dst = a.out + (static_cast<int64_t>(si.q_row0 + p / G) * a.hq + (gi.kvh + rh) * G +
                         p % G) * D;
       merge_row_warp<T, D>(a.partials, gi, r, lane, dst);
@@ -558,23 +560,25 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const AttnA
 }
 
 template <typename T>
-int launch_merge_t(const AttnArgs<T>& args, int dim, int grid, cudaStream_t stream) {
+int launch_merge_t(const AttnArgs<T>& args, int dim, int list, int grid, cudaStream_t stream) {
   if (dim == kWideHeadDim)
     FE_CUDA_TRY(launch_pdl(decode_merge_kernel<T, kWideHeadDim>, dim3(grid), dim3(kMergeThreads), 0,
-                           stream, args));
+                           stream, args, list));
   else
     FE_CUDA_TRY(launch_pdl(decode_merge_kernel<T, kHeadDim>, dim3(grid), dim3(kMergeThreads), 0,
-                           stream, args));
+                           stream, args, list));
   return FE_OK;
 }
 
 }  // namespace
 
-int decode_merge_launch(int dtype, int dim, const void* args, int grid, cudaStream_t stream) {
+int decode_merge_launch(int dtype, int dim, int list, const void* args, int grid,
+                        cudaStream_t stream) {
   if (grid <= 0) return FE_OK;
   if (dtype == FE_DTYPE_BF16)
-    return launch_merge_t(*static_cast<const AttnArgs<__nv_bfloat16>*>(args), dim, grid, stream);
-  return launch_merge_t(*static_cast<const AttnArgs<__half>*>(args), dim, grid, stream);
+    return launch_merge_t(*static_cast<const AttnArgs<__nv_bfloat16>*>(args), dim, list, grid,
+                          stream);
+  return launch_merge_t(*static_cast<const AttnArgs<__half>*>(args), dim, list, grid, stream);
 }
 
 int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,

@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_device_kernel(const DevP
           }
           if (split) {
             groups[gid] = SplitGroup{static_cast<int32_t>(pc), static_cast<int32_t>(part), rec,
-                                     H * P, b, g * H, {0, 0}};
+                                     H * P, b, g * H, 0, 0};
             ++gid;
             part += rec * pc;
           }

@@ -7,10 +7,12 @@
 // dim = 256, for decode rows, verify / draft blocks and prefill chunks alike,
 // with the bottom-right causal or the full mask.
 //
-// Design (functional path, not tuned like the 128-dim kernels): one CTA of 4
-// warps per work item = 64 packed query rows (row p = query row p / G, head
-// kvh*G + p % G) of one (sequence, KV head) against all of its keys. Q is
-// staged once in shared memory; K and V tiles of 32 keys (16 KiB each) are
+// Design: one CTA of 4 warps per work item = 64 packed query rows (row p =
+// query row p / G, head kvh*G + p % G) of one (sequence, KV head) against the
+// item's key range: all keys the mask shows the item's rows, or, when the
+// planner splits an item whose rows are too few to fill the GPU, one piece of
+// that range (the piece writes an unnormalised (O, m, l) record, merged by
+// decode_merge_kernel). Q is staged once in shared memory; K and V tiles of 32 keys (16 KiB each) are
 // gathered through the page table with 16-byte cp.async (positions past the
 // key limit read as zeros) into a 2-stage ring; rows of 512 bytes are stored
 // with the 16-byte chunk index XOR-swizzled by the row, so ldmatrix reads are
@@ -18,7 +20,8 @@
 // mma.m16n8k16 with fp32 accumulation, an exact online softmax in base 2 (O
 // rescaled every tile), and P entering the PV product as a 16-bit high part
 // plus its 16-bit residual (two MMAs), which keeps ~16 bits of each fp32 weight
-// like the 128-dim kernels. Work items are dealt to the grid in a strided loop.
+// like the 128-dim kernels. Each CTA walks its own item list (cta_off), laid
+// out by the host planner longest first onto the least-loaded CTA.
 #include "fe_attn_common.cuh"
 
 namespace fe {
@@ -69,7 +72,8 @@ __global__ void __launch_bounds__(kWThreads) paged_wide_kernel(const AttnArgs<T>
   pdl_wait();
   const MetaHeader* hdr = reinterpret_cast<const MetaHeader*>(a.meta);
   const int view = a.view;
-  const int n_items = hdr->n_items[view];
+  if (static_cast<int>(blockIdx.x) >= hdr->grid[view]) return;
+  const int32_t* cta_off = reinterpret_cast<const int32_t*>(a.meta + hdr->cta_off_off[view]);
   const WorkItem* items = reinterpret_cast<const WorkItem*>(a.meta + hdr->items_off[view]);
   const SeqInfo* seqs = reinterpret_cast<const SeqInfo*>(a.meta + hdr->seqs_off);
   const int32_t* pages = reinterpret_cast<const int32_t*>(a.meta + hdr->pages_off);
@@ -79,23 +83,27 @@ __global__ void __launch_bounds__(kWThreads) paged_wide_kernel(const AttnArgs<T>
   const uint32_t q_s = smem_u32(wsmem);
   const uint32_t kv_s = q_s + kWQBytes;  // stage s: K at kv_s + s*2*tile, V after it
 
-  for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+  const int it_end = cta_off[blockIdx.x + 1];
+  for (int it = cta_off[blockIdx.x]; it < it_end; ++it) {
     const WorkItem w = items[it];
     const SeqInfo si = seqs[w.seq];
     const int len = si.length, qrows = si.qrows, P = qrows * G;
     const int p0 = w.rb0 * kRowBlock;  // first packed row of the item
     const int p_last = min(P, p0 + kWRows) - 1;
     const int lim_block = causal ? len - qrows + p_last / G + 1 : len;
-    const int ntiles = (lim_block + kWKeys - 1) / kWKeys;
+    // this item's keys: [key0, key_end), the piece of the mask's range
+    const int key0 = w.kt0 * kTileTokens;
+    const int key_end = min(lim_block, w.kt1 * kTileTokens);
+    const int ntiles = key_end > key0 ? (key_end - key0 + kWKeys - 1) / kWKeys : 0;
 
     auto load_tile = [&](int j) {
       const int st = j & 1;
-      const int t0 = j * kWKeys;
+      const int t0 = key0 + j * kWKeys;
       const uint32_t kb = kv_s + st * 2 * kWTileBytes, vb = kb + kWTileBytes;
       for (int i = tid; i < kWKeys * kWChunks; i += kWThreads) {
         const int key = i / kWChunks, c = i % kWChunks;
         const int t = t0 + key;
-        const bool ok = t < lim_block;
+        const bool ok = t < key_end;
         int64_t off = 0;
         if (ok) {
           const int64_t slot = int64_t(__ldg(pages + si.page_off + t / page)) * page + t % page;
@@ -130,7 +138,7 @@ __global__ void __launch_bounds__(kWThreads) paged_wide_kernel(const AttnArgs<T>
     for (int e = 0; e < 2; ++e) {
       const int p = p0 + warp * 16 + g + 8 * e;
       valid[e] = p < P;
-      lim[e] = (causal && valid[e]) ? len - qrows + p / G + 1 : len;
+      lim[e] = min((causal && valid[e]) ? len - qrows + p / G + 1 : len, key_end);
     }
     float o[kWD / 8][4];
 #pragma unroll
@@ -160,7 +168,7 @@ __global__ void __launch_bounds__(kWThreads) paged_wide_kernel(const AttnArgs<T>
         }
       }
       // mask, online softmax (base 2), P
-      const int t0 = j * kWKeys;
+      const int t0 = key0 + j * kWKeys;
       float alpha[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
@@ -231,20 +239,37 @@ __global__ void __launch_bounds__(kWThreads) paged_wide_kernel(const AttnArgs<T>
     }
     cp_async_wait<0>();
 
-    // divide by the row sums (over the quad's columns) and store
+    // divide by the row sums (over the quad's columns) and store, or write
+    // this piece's record: O[r][256] unnormalised, then m[r], l[r] (r = row
+    // within the item; rows = the item's valid rows)
+    const int rows = p_last + 1 - p0;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       float sum = l[e];
       sum += __shfl_xor_sync(0xffffffffu, sum, 1);
       sum += __shfl_xor_sync(0xffffffffu, sum, 2);
       if (!valid[e]) continue;
-      const float inv = 1.f / sum;
-      const int p = p0 + warp * 16 + g + 8 * e;
-      T* dst = a.out + (static_cast<int64_t>(si.q_row0 + p / G) * a.hq + w.kvh * G + p % G) * kWD;
+      const int r = warp * 16 + g + 8 * e;
+      const int p = p0 + r;
+      if (w.part < 0) {
+        const float inv = 1.f / sum;
+        T* dst =
+            a.out + (static_cast<int64_t>(si.q_row0 + p / G) * a.hq + w.kvh * G + p % G) * kWD;
 #pragma unroll
-      for (int d = 0; d < kWD / 8; ++d)
-        *reinterpret_cast<uint32_t*>(dst + d * 8 + 2 * tq) =
-            pack2<T>(o[d][2 * e] * inv, o[d][2 * e + 1] * inv);
+        for (int d = 0; d < kWD / 8; ++d)
+          *reinterpret_cast<uint32_t*>(dst + d * 8 + 2 * tq) =
+              pack2<T>(o[d][2 * e] * inv, o[d][2 * e + 1] * inv);
+      } else {
+        float* rec = a.partials + w.part;
+        float* row = rec + r * kWD;
+#pragma unroll
+        for (int d = 0; d < kWD / 8; ++d)
+          *reinterpret_cast<float2*>(row + d * 8 + 2 * tq) = make_float2(o[d][2 * e], o[d][2 * e + 1]);
+        if (tq == 0) {
+          rec[rows * kWD + r] = m[e];
+          rec[rows * (kWD + 1) + r] = sum;
+        }
+      }
     }
     __syncthreads();  // Q and the ring are reused by the next item
   }

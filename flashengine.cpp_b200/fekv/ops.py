@@ -303,8 +303,8 @@ ITEM_DTYPE = np.dtype([("seq", "<i4"), ("kvh", "<i2"), ("key_mode", "<i2"), ("rb
                        ("nrb", "<i4"), ("kt0", "<i4"), ("kt1", "<i4"), ("part", "<i4"),
                        ("group", "<i4")])
 GROUP_DTYPE = np.dtype([("nsplit", "<i4"), ("part0", "<i4"), ("rec_floats", "<i4"),
-                        ("rows", "<i4"), ("seq", "<i4"), ("kvh", "<i4"), ("pad0", "<i4"),
-                        ("pad1", "<i4")])
+                        ("rows", "<i4"), ("seq", "<i4"), ("kvh", "<i4"), ("row0", "<i4"),
+                        ("rows_per_head", "<i4")])
 SEQ_DTYPE = np.dtype([("q_row0", "<i4"), ("qrows", "<i4"), ("length", "<i4"),
                       ("page_off", "<i4")])
 

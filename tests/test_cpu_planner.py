@@ -153,12 +153,35 @@ def test_zero_row_sequences_are_skipped():
     assert set(seqs) == {1}
 
 
+def _wide_units_covered(view, md, G, causal):
+    """Every (sequence, KV head, 64-row block) of the multi-block sequences is
+    on the list once per key tile of its mask's range, pieces contiguous."""
+    items = view["items"]
+    q = np.diff(md.qo)
+    L = md.lengths(16)
+    for b in range(len(q)):
+        P = int(q[b]) * G
+        if P <= 16:
+            assert not (items["seq"] == b).any()
+            continue
+        for h in range(2):
+            for rb0 in range(0, -(-P // 16), 4):
+                its = items[(items["seq"] == b) & (items["kvh"] == h) & (items["rb0"] == rb0)]
+                its = np.sort(its, order="kt0")
+                last_row = min(P, (rb0 + 4) * 16) - 1
+                keys = int(L[b]) - int(q[b]) + last_row // G + 1 if causal else int(L[b])
+                assert len(its) >= 1 and (its["key_mode"] == 2).all()
+                assert its["kt0"][0] == 0 and its["kt1"][-1] == -(-keys // 16)
+                assert (its["kt0"][1:] == its["kt1"][:-1]).all()
+                assert (its["nrb"] == min(4, -(-P // 16) - rb0)).all()
+
+
 def test_head_dim_256_plan_lists():
     """head_dim 256 plans put every (sequence, KV head, 64-row block) of the
-    multi-block sequences on the row lists for the wide kernel (both masks),
-    longest first, unsplit; sequences whose packed rows fit one 16-row block
-    go to the decode list (two KV heads per item), cut exactly like head_dim
-    128, with split records of rows x (256 + 2) floats."""
+    multi-block sequences on the row lists for the wide kernel, with each
+    mask's key range; sequences whose packed rows fit one 16-row block go to
+    the decode list (two KV heads per item), cut exactly like head_dim 128,
+    with split records of rows x (256 + 2) floats."""
     # a decode row, a 100-row chunk, a 3-row block and a long decode row
     from fekv.metadata import build_step_metadata
     tables = [np.arange(i * 400, i * 400 + 400) for i in range(4)]
@@ -166,24 +189,12 @@ def test_head_dim_256_plan_lists():
     hp = HostPlan(16, 2, 256, 16, 4, 400, True, 1600, grid_cap=8)
     meta = hp.prepare(md.qo, md.kv, md.pages, md.last)
     G = 8
-    q = np.diff(md.qo)
-    multi = [b for b in range(4) if q[b] * G > 16]
-    want = sum(-(-int(q[b]) * G // 64) * 2 for b in multi)
     v0, v1, v2 = meta["views"]
-    assert len(v0["items"]) == want and len(v1["items"]) == want
-    np.testing.assert_array_equal(v0["items"], v1["items"])
-    assert len(v0["groups"]) == 0
-    assert (v0["items"]["key_mode"] == 2).all() and (v0["items"]["part"] == -1).all()
-    assert set(v0["items"]["seq"]) == set(multi)
-    cost = (v0["items"]["kt1"] - v0["items"]["kt0"]) * v0["items"]["nrb"]
-    assert (np.diff(cost) <= 0).all()
-    # rows covered exactly once per KV head
-    for b in multi:
-        for h in range(2):
-            its = v0["items"][(v0["items"]["seq"] == b) & (v0["items"]["kvh"] == h)]
-            rows = sorted(r for it in its for r in range(int(it["rb0"]) * 16,
-                                                         min(int(q[b]) * G, (int(it["rb0"]) + int(it["nrb"])) * 16)))
-            assert rows == list(range(int(q[b]) * G))
+    _wide_units_covered(v0, md, G, causal=False)
+    _wide_units_covered(v1, md, G, causal=True)
+    for v in (v0, v1):
+        assert v["grid"] <= 16 and len(v["cta_off"]) == v["grid"] + 1
+        assert v["cta_off"][-1] == len(v["items"]) and (np.diff(v["cta_off"]) >= 0).all()
     # decode list: both KV heads in one unit, key tiles covered exactly once
     it2 = v2["items"]
     assert set(it2["seq"]) == {0, 3} and (it2["kvh"] == 0).all() and (it2["key_mode"] == 1).all()
@@ -196,4 +207,37 @@ def test_head_dim_256_plan_lists():
     assert len(split) >= 1
     for gi in split:
         assert gi["rows"] == 2 * G and gi["rec_floats"] == (2 * G * 258 + 3) // 4 * 4
+        assert gi["row0"] == 0 and gi["rows_per_head"] == 0
+    hp.close()
+
+
+def test_head_dim_256_draft_blocks_are_split():
+    """DFlash-style draft blocks (16 rows over long contexts) give too few
+    64-row items to fill the GPU: their key ranges are split into pieces of at
+    about 16 tiles or more, whose records (one KV head, the item's rows) the merge
+    kernel maps back with row0 / rows_per_head."""
+    from fekv.metadata import build_step_metadata
+    tables = [np.arange(i * 200, i * 200 + 200) for i in range(2)]
+    md = build_step_metadata(tables, [3000, 2500], [16, 16], 16)
+    hp = HostPlan(16, 2, 256, 16, 2, 200, True, 400, grid_cap=148)
+    meta = hp.prepare(md.qo, md.kv, md.pages, md.last)
+    G = 8
+    for causal, v in ((False, meta["views"][0]), (True, meta["views"][1])):
+        _wide_units_covered(v, md, G, causal)
+        it = v["items"]
+        assert len(it) > 8  # 2 seqs x 2 KV heads x 2 row items, split
+        split = it[it["part"] >= 0]
+        assert len(split) == len(it)
+        # pieces split a unit evenly, each near the 16-tile minimum or longer
+        assert ((it["kt1"] - it["kt0"]) >= 8).all()
+        for gi in v["groups"]:
+            assert gi["nsplit"] >= 2 and gi["rows"] == 64
+            assert gi["row0"] in (0, 64) and gi["rows_per_head"] == 64
+            assert gi["rec_floats"] == 64 * 258
+        # every piece's record lies inside its group's records
+        for x in split:
+            gi = v["groups"][x["group"]]
+            assert gi["part0"] <= x["part"] < gi["part0"] + gi["nsplit"] * gi["rec_floats"]
+            assert (x["part"] - gi["part0"]) % gi["rec_floats"] == 0
+    assert len(meta["views"][2]["items"]) == 0
     hp.close()

@@ -89,3 +89,22 @@ def test_device_prepare_is_refused_for_head_dim_256(fk):
         plan.prepare_device(z, z, z, z[:2], 2, 2)
     assert e.value.status == fk._lib.FE_ERR_UNSUPPORTED
     plan.close()
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("bf16", [True, False])
+def test_draft_blocks_split_across_ctas(fk, causal, bf16):
+    """DFlash-style 16-row blocks over long contexts: too few 64-row items to
+    fill the GPU, so their key ranges are split into pieces whose records the
+    merge kernel combines; checked against the fp32 reference, and the plan
+    is checked to have split them."""
+    from fekv.metadata import build_step_metadata
+    cached, rows = [3000, 2500, 1800], [16, 16, 16]
+    res = _case(fk, 16, 2, cached, rows, bf16, causal, 77 + causal)
+    assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, res
+    tables = [np.arange(i * 200, i * 200 + 200) for i in range(3)]
+    md = build_step_metadata(tables, cached, rows, PAGE)
+    hp = fk.HostPlan(16, 2, DIM, PAGE, 3, 200, True, 600, grid_cap=148)
+    meta = hp.prepare(md.qo, md.kv, md.pages, md.last)
+    assert (meta["views"][1 if causal else 0]["groups"]["nsplit"] >= 2).any()
+    hp.close()
