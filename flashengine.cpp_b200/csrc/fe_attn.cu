@@ -28,9 +28,7 @@ int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const 
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
 int decode_merge_launch(int dtype, int dim, int list, const void* args, int grid,
                         cudaStream_t stream);
-int wide_launch(int dtype, const void* args, const void* k_pool, const void* v_pool, int hkv,
-                int grid, cudaStream_t stream);
-int prefill_tc_launch(int dtype, const CUtensorMap& kmap, const CUtensorMap& vmap,
+int prefill_tc_launch(int dtype, int dim, const CUtensorMap& kmap, const CUtensorMap& vmap,
                       const CUtensorMap& qmap, const void* args, int grid, cudaStream_t stream);
 
 namespace {
@@ -79,26 +77,28 @@ int encode_3d(CUtensorMap* map, const void* pool, int dtype, const cuuint64_t di
   return encode_nd(map, pool, dtype, 3, dims, strides, box);
 }
 
-// tcgen05 row kernel: pool viewed as [cache_slots/8][hkv*2][8][64] (slot
-// groups of 8, head-halves, slots within the group, 64 elements); box =
-// 2 groups x 2 head-halves x 8 slots x 64 elements, so one TMA copies both
-// halves of a 16-token piece of one KV head and lays it out as
-// [group][half][8 rows of 128 B]: 1 KiB swizzle atoms, 8-key groups 2 KiB
-// apart, the two head-halves 1 KiB apart.
-int encode_tc_map(CUtensorMap* map, const void* pool, int dtype, int hkv, int64_t cache_slots) {
-  const cuuint64_t dims[4] = {64, 8, cuuint64_t(hkv) * 2, cuuint64_t(cache_slots / 8)};
-  const cuuint64_t strides[3] = {cuuint64_t(hkv) * 256, 128, cuuint64_t(hkv) * 256 * 8};
-  const cuuint32_t box[4] = {64, 8, 2, 2};
+// tcgen05 row kernel: pool viewed as [cache_slots/8][hkv*dim/64][8][64]
+// (slot groups of 8, 64-dim boxes, slots within the group, 64 elements);
+// box = 2 groups x dim/64 boxes x 8 slots x 64 elements, so one TMA copies a
+// 16-token piece of one KV head and lays it out as [group][box][8 rows of
+// 128 B]: 1 KiB swizzle atoms, the boxes 1 KiB apart, 8-key groups dim*16 B
+// apart.
+int encode_tc_map(CUtensorMap* map, const void* pool, int dtype, int hkv, int dim,
+                  int64_t cache_slots) {
+  const cuuint64_t boxes = cuuint64_t(dim / 64);
+  const cuuint64_t dims[4] = {64, 8, cuuint64_t(hkv) * boxes, cuuint64_t(cache_slots / 8)};
+  const cuuint64_t strides[3] = {cuuint64_t(hkv) * dim * 2, 128, cuuint64_t(hkv) * dim * 2 * 8};
+  const cuuint32_t box[4] = {64, 8, cuuint32_t(boxes), 2};
   return encode_nd(map, pool, dtype, 4, dims, strides, box);
 }
 
-// tcgen05 row kernel, queries: q [rows][hq][128] viewed as [rows][hq][128]
-// with box (128/G rows) x (G heads) x 64 elements: one box is the 64-dim half
-// of a 128-row packed Q tile (packed row p = query row p / G, head p % G of
-// the KV head's group), landing in packed-row order.
-int encode_q_map(CUtensorMap* map, const void* q, int dtype, int hq, int rows, int G) {
-  const cuuint64_t dims[3] = {128, cuuint64_t(hq), cuuint64_t(rows)};
-  const cuuint64_t strides[2] = {256, cuuint64_t(hq) * 256};
+// tcgen05 row kernel, queries: q [rows][hq][dim] with box (128/G rows) x
+// (G heads) x 64 elements: one box is a 64-dim slice of a 128-row packed Q
+// tile (packed row p = query row p / G, head p % G of the KV head's group),
+// landing in packed-row order.
+int encode_q_map(CUtensorMap* map, const void* q, int dtype, int hq, int dim, int rows, int G) {
+  const cuuint64_t dims[3] = {cuuint64_t(dim), cuuint64_t(hq), cuuint64_t(rows)};
+  const cuuint64_t strides[2] = {cuuint64_t(dim) * 2, cuuint64_t(hq) * dim * 2};
   const cuuint32_t box[3] = {64, cuuint32_t(G), cuuint32_t(128 / G)};
   return encode_nd(map, q, dtype, 3, dims, strides, box);
 }
@@ -164,9 +164,7 @@ struct fe_attn_plan {
 namespace {
 
 size_t meta_capacity(const PlanConfig& c) {
-  // the wide kernel (head_dim 256) runs two CTAs per SM on the row lists
-  const int row_grid = c.dim == kWideHeadDim ? 2 * c.grid_cap : c.grid_cap;
-  size_t per_view = sizeof(int32_t) * (std::max(row_grid, c.dec_grid_cap) + 1) +
+  size_t per_view = sizeof(int32_t) * (std::max(c.grid_cap, c.dec_grid_cap) + 1) +
                     sizeof(WorkItem) * c.max_items + sizeof(SplitGroup) * c.max_groups + 64;
   return sizeof(MetaHeader) + 3 * per_view + sizeof(SeqInfo) * c.max_batch +
          sizeof(int32_t) * size_t(c.max_batch) * c.max_pages + 256;
@@ -494,10 +492,8 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
     if (encode_decode_map(&p->kmap_dec, k_pool, p->dtype, p->cfg.hkv, dim, H, cache_slots) !=
         FE_OK)
       p->per_head_tma = true;
-    if (!wide) {
-      rc = encode_tc_map(&p->kmap_tc, k_pool, p->dtype, p->cfg.hkv, cache_slots);
-      if (rc != FE_OK) return rc;
-    }
+    rc = encode_tc_map(&p->kmap_tc, k_pool, p->dtype, p->cfg.hkv, dim, cache_slots);
+    if (rc != FE_OK) return rc;
     p->kmap_ptr = k_pool;
   }
   if (v_pool != p->vmap_ptr) {
@@ -506,10 +502,8 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
     if (encode_decode_map(&p->vmap_dec, v_pool, p->dtype, p->cfg.hkv, dim, H, cache_slots) !=
         FE_OK)
       p->per_head_tma = true;
-    if (!wide) {
-      rc = encode_tc_map(&p->vmap_tc, v_pool, p->dtype, p->cfg.hkv, cache_slots);
-      if (rc != FE_OK) return rc;
-    }
+    rc = encode_tc_map(&p->vmap_tc, v_pool, p->dtype, p->cfg.hkv, dim, cache_slots);
+    if (rc != FE_OK) return rc;
     p->vmap_ptr = v_pool;
   }
   MetaHeader h;
@@ -522,16 +516,15 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
   CUtensorMap qmap;
   std::memset(&qmap, 0, sizeof(qmap));  // unused when G does not divide 128
   int q_map_rows = 0;
-  if (!wide && grid_rows > 0 && 128 % (p->cfg.hq / p->cfg.hkv) == 0 && h.rows > 0) {
-    int rc = encode_q_map(&qmap, q, p->dtype, p->cfg.hq, h.rows, p->cfg.hq / p->cfg.hkv);
+  if (grid_rows > 0 && 128 % (p->cfg.hq / p->cfg.hkv) == 0 && h.rows > 0) {
+    int rc = encode_q_map(&qmap, q, p->dtype, p->cfg.hq, dim, h.rows, p->cfg.hq / p->cfg.hkv);
     if (rc != FE_OK) return rc;
     q_map_rows = h.rows;
   }
-  // head_dim 256 row work runs on the wide kernel, two 96 KiB CTAs per SM,
-  // and its split pieces are merged by the merge kernel over the row list
-  const int grid_wide = !wide || grid_rows == 0 ? 0 : (p->fixed_grid ? 2 * p->cfg.grid_cap : h.grid[view]);
-  const int grid_wide_merge =
-      grid_wide == 0 ? 0 : (p->fixed_grid ? p->cfg.grid_cap : h.n_groups[view]);
+  // split pieces of the row list (head_dim 256 steps with few row items)
+  // are merged by the merge kernel over that list
+  const int grid_row_merge =
+      !wide || grid_rows == 0 ? 0 : (p->fixed_grid ? p->cfg.grid_cap : h.n_groups[view]);
   const float scale_log2 = 1.4426950408889634f / sqrtf(float(dim));
   auto s = static_cast<cudaStream_t>(stream);
   const int G = p->cfg.hq / p->cfg.hkv;
@@ -543,13 +536,11 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
       if (rc == FE_OK) rc = decode_merge_launch(p->dtype, dim, 2, &a, grid_merge, s);
       if (rc != FE_OK) return rc;
     }
-    if (wide) {
-      int rc = wide_launch(p->dtype, &a, k_pool, v_pool, p->cfg.hkv, grid_wide, s);
-      if (rc == FE_OK) rc = decode_merge_launch(p->dtype, dim, view, &a, grid_wide_merge, s);
+    if (grid_rows > 0) {
+      int rc = prefill_tc_launch(p->dtype, dim, p->kmap_tc, p->vmap_tc, qmap, &a, grid_rows, s);
+      if (rc == FE_OK) rc = decode_merge_launch(p->dtype, dim, view, &a, grid_row_merge, s);
       return rc;
     }
-    if (grid_rows > 0)
-      return prefill_tc_launch(p->dtype, p->kmap_tc, p->vmap_tc, qmap, &a, grid_rows, s);
     return FE_OK;
   };
   int rc;

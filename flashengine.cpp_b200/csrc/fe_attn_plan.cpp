@@ -293,21 +293,6 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
     const int P = qrows * G;
     const int RB = ceil_div(P, kRowBlock);
     const int tiles_full = ceil_div(length, kTileTokens);
-    if (cfg.dim == kWideHeadDim && RB > 1) {
-      // 64-row items (four row blocks) per KV head on the wide kernel
-      for (int rb0 = 0; rb0 < RB; rb0 += kWideRowBlocks) {
-        const int nrb = std::min(kWideRowBlocks, RB - rb0);
-        const int last_row = std::min(P, (rb0 + nrb) * kRowBlock) - 1;
-        const int rows_valid = last_row + 1 - rb0 * kRowBlock;
-        const int64_t limit = length - qrows + last_row / G + 1;  // bottom-right causal
-        const int tiles_causal = ceil_div(limit, kTileTokens);
-        for (int h = 0; h < cfg.hkv; ++h) {
-          row_units_full.push_back(Unit{b, h, 2, rb0, nrb, tiles_full, rows_valid});
-          row_units_causal.push_back(Unit{b, h, 2, rb0, nrb, tiles_causal, rows_valid});
-        }
-      }
-      continue;
-    }
     if (RB == 1) {
       const int H = cfg.dec_heads;
       for (int h = 0; h < cfg.hkv; h += H)
@@ -332,25 +317,18 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
   // List 0: row work, non-causal; 1: row work, causal (identical key ranges
   // when there is no row work); 2: decode work.
   View views[3];
-  if (cfg.dim == kWideHeadDim) {
-    // multi-block rows: the wide kernel (two CTAs per SM), key ranges split
-    // into pieces of at least kWideMinChunk tiles when there are fewer
-    // items than CTAs; single-block rows: the decode list, cut exactly like
-    // head_dim 128
-    const int wide_cap = 2 * cfg.grid_cap;
-    int rc = build_view(cfg, row_units_full, wide_cap, 1, kWideMinChunk, fixed_grid, views[0], err);
+  {
+    // head_dim 256 splits the key ranges of row items too (pieces of at
+    // least kWideMinChunk tiles) when there are fewer items than CTAs, as
+    // DFlash draft blocks give; head_dim 128 keeps whole items (cfg.row_split)
+    const int row_min_chunk =
+        cfg.dim == kWideHeadDim ? kWideMinChunk : (cfg.row_split ? 16 : (1 << 29));
+    const int per_cta = cfg.dim == kWideHeadDim ? 1 : 4;
+    int rc = build_view(cfg, row_units_full, cfg.grid_cap, per_cta, row_min_chunk, fixed_grid,
+                        views[0], err);
     if (rc != FE_OK) return rc;
-    rc = build_view(cfg, row_units_causal, wide_cap, 1, kWideMinChunk, fixed_grid, views[1], err);
-    if (rc != FE_OK) return rc;
-    rc = build_cut_view(cfg, key_units, cfg.dec_grid_cap, 8, fixed_grid, views[2], err);
-    if (rc != FE_OK) return rc;
-  } else {
-    const int row_min_chunk = cfg.row_split ? 16 : (1 << 29);
-    int rc = build_view(cfg, row_units_full, cfg.grid_cap, 4, row_min_chunk, fixed_grid, views[0],
-                        err);
-    if (rc != FE_OK) return rc;
-    rc = build_view(cfg, row_units_causal, cfg.grid_cap, 4, row_min_chunk, fixed_grid, views[1],
-                    err);
+    rc = build_view(cfg, row_units_causal, cfg.grid_cap, per_cta, row_min_chunk, fixed_grid,
+                    views[1], err);
     if (rc != FE_OK) return rc;
     rc = build_cut_view(cfg, key_units, cfg.dec_grid_cap, 8, fixed_grid, views[2], err);
     if (rc != FE_OK) return rc;

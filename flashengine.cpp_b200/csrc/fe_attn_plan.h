@@ -18,9 +18,8 @@
 namespace fe {
 
 constexpr int kHeadDim = 128;
-constexpr int kWideHeadDim = 256;  // rows: fe_wide.cu; single-block sequences: fe_decode.cu
-constexpr int kWideRowBlocks = 4;  // 16-row blocks per wide-kernel item (64 packed rows)
-constexpr int kWideMinChunk = 16;  // fewest key tiles in a split piece of a wide item
+constexpr int kWideHeadDim = 256;  // the hybrid / DFlash models' full-attention head dim
+constexpr int kWideMinChunk = 16;  // fewest key tiles in a split piece of a head_dim 256 row item
 constexpr int kTileTokens = 16;   // key tokens per tile (one TMA box per K/V half)
 constexpr int kRowBlock = 16;     // packed query rows per mma row block
 
@@ -37,11 +36,9 @@ struct SeqInfo {  // 16 bytes
 //                 (decode and short verify) and their results are merged in
 //                 shared memory.
 //   key_mode = 0: up to eight row blocks (one 128-row tcgen05 tile), each
-//                 over all key tiles of the item (prefill / long verify).
-//   key_mode = 2: head_dim 256 (wide kernel): up to four row blocks against
-//                 key tiles [kt0, kt1) (cut to the mask's range), split
-//                 across CTAs like key mode. head_dim 256 sequences with a
-//                 single row block are key-mode (1) work of the decode kernel.
+//                 over all key tiles of the item (prefill / long verify);
+//                 for head_dim 256 the key range may be split across CTAs
+//                 (a piece of [kt0, kt1) writes a partial record).
 // A packed row p is query row p / G of the sequence, query head kvh*G + p % G.
 struct WorkItem {  // 32 bytes
   int32_t seq;

@@ -46,48 +46,61 @@
 
 namespace fe {
 
-int prefill_tc_launch(int dtype, const CUtensorMap& kmap, const CUtensorMap& vmap,
+int prefill_tc_launch(int dtype, int dim, const CUtensorMap& kmap, const CUtensorMap& vmap,
                       const CUtensorMap& qmap, const void* args, int grid, cudaStream_t stream);
 int prefill_tc_smem_bytes();
 
 namespace {
 
-constexpr int kTcM = 128;                   // packed rows per work item
-constexpr int kTcN = 128;                   // keys per tile (S MMA N)
-constexpr int kHalfN = kTcN / 2;            // keys per softmax group and tile
-constexpr int kPiecesPerTile = kTcN / kTileTokens;
-constexpr int kKStages = 2;
-constexpr int kVStages = 3;
-constexpr int kTcThreads = 12 * 32;         // 3 warpgroups: softmax 0, softmax 1, producers/MMA
+// Per head dim D (128, or 256 for the hybrid / DFlash models' full-attention
+// layers). Both use the same shared-memory budget: 64 KiB of Q (two 128-dim
+// tiles, or one 256-dim tile), a 2-stage K and a 3-stage V ring of 32 KiB
+// stages (128 keys of 128 dims, or 64 keys of 256 dims).
+constexpr int kKStagesTc = 2;
+constexpr int kVStagesTc = 3;
+constexpr int kSlotsTc = 3;
+constexpr int kTcThreads = 12 * 32;  // 3 warpgroups: softmax 0, softmax 1, producers/MMA
 constexpr int kProducerWarp = 8, kMmaWarp = 9, kPvWarp = 10, kVProducerWarp = 11;
-constexpr int kQHalf = kTcM * 128;          // 16 KiB: 128 rows x 64 dims
-constexpr int kQBytes = 2 * kQHalf;         // one Q tile
-// A K (or V) stage holds one tile as eight 4 KiB pieces laid out
-// [8-key group][head-half][8 rows x 128 B] (swizzled 1 KiB atoms): the 8-key
-// groups of one head-half are 2 KiB apart, the two halves 1 KiB apart.
-constexpr int kPieceBytes = kTileTokens * 256;  // 16 keys x 128 dims x 2 B
-constexpr int kKVTile = kPiecesPerTile * kPieceBytes;  // 32 KiB
-constexpr int kOffQ = 0;                                // two Q tiles
-constexpr int kOffK = 2 * kQBytes;
-constexpr int kOffV = kOffK + kKStages * kKVTile;
-constexpr int kOffX = kOffV + kVStages * kKVTile;       // half-row maxima
-constexpr int kXBytes = 2 * 2 * kTcM * 4;               // [tile parity][group][128 rows]
-constexpr int kOffBar = kOffX + kXBytes;
-constexpr int kSlots = 3;
 // q_full[2], q_empty[2], o_free, l_done, k_full[2], k_empty[2], v_full[3],
 // v_empty[3], s_full[3], s_free[3], p_full[3][2], mma_drain, xmax[2][4]
-constexpr int kNumBars = 4 + 2 + 2 * kKStages + 2 * kVStages + kSlots + kSlots + 2 * kSlots + 1 + 8;
-// The dynamic shared memory base is 1 KiB aligned (no static shared memory;
-// checked at entry), as the 128-byte swizzle atoms require.
-constexpr int kTcSmem = kOffBar + kNumBars * 8 + 32;
-// TMEM columns: slot s at s*128 (S fp32; group g's half [g*64, g*64+64) is
-// later overwritten by its P: high part in the first 32, residual in the last
-// 32 columns); O at 384.
+constexpr int kNumBarsTc =
+    4 + 2 + 2 * kKStagesTc + 2 * kVStagesTc + kSlotsTc + kSlotsTc + 2 * kSlotsTc + 1 + 8;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kOCol = kSlots * kTcN;  // 384
 constexpr float kRescaleThreshold = 8.f;
-static_assert(kTcSmem <= 232448, "shared memory budget");
-static_assert(kPiecesPerTile == 8, "page-id prefetch assumes 4 tiles per 32 pieces");
+
+template <int D>
+struct TcCfg {
+  static constexpr int kM = 128;                        // packed rows per work item
+  static constexpr int kN = D == kHeadDim ? 128 : 64;   // keys per tile (S MMA N)
+  static constexpr int kHalfN = kN / 2;                 // keys per softmax group and tile
+  static constexpr int kPiecesPerTile = kN / kTileTokens;
+  static constexpr int kBoxes = D / 64;                 // 64-dim boxes per row
+  static constexpr int kQBox = kM * 128;                // 16 KiB: 128 rows x 64 dims
+  static constexpr int kQBytes = kBoxes * kQBox;        // one Q tile
+  static constexpr int kQBufs = D == kHeadDim ? 2 : 1;
+  // A K (or V) stage holds one tile as 16-token pieces laid out
+  // [8-key group][64-dim box][8 rows x 128 B] (swizzled 1 KiB atoms): the
+  // 8-key groups of one box are kGroupBytes apart, the boxes 1 KiB apart.
+  static constexpr int kPieceBytes = kTileTokens * D * 2;
+  static constexpr int kGroupBytes = 8 * D * 2;
+  static constexpr int kKVTile = kPiecesPerTile * kPieceBytes;  // 32 KiB
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kQBufs * kQBytes;
+  static constexpr int kOffV = kOffK + kKStagesTc * kKVTile;
+  static constexpr int kOffX = kOffV + kVStagesTc * kKVTile;   // half-row maxima
+  static constexpr int kXBytes = 2 * 2 * kM * 4;               // [tile parity][group][128 rows]
+  static constexpr int kOffBar = kOffX + kXBytes;
+  static constexpr int kSmem = kOffBar + kNumBarsTc * 8 + 32;
+  // TMEM columns: slot s at s*kN (S fp32; group g's half [g*kN/2, (g+1)*kN/2)
+  // is later overwritten by its P: high part in its first kN/4 columns,
+  // residual in the last kN/4); O (D fp32 columns) at kOCol.
+  static constexpr uint32_t kOCol = D == kHeadDim ? kSlotsTc * kN : 256;
+  static constexpr int kGroupDims = D / 2;  // O dims each softmax group rescales / stores
+  static_assert(kSmem <= 232448, "shared memory budget");
+  static_assert(kSlotsTc * kN <= int(kOCol) && kOCol + D <= 512, "TMEM budget");
+  static_assert(32 % kPiecesPerTile == 0, "page-id prefetch assumes whole tiles per 32 pieces");
+  static_assert(kHalfN % 32 == 0, "softmax loads S in 32-column chunks");
+};
 
 template <typename T>
 struct Fmt;
@@ -129,14 +142,20 @@ __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volati
   return !aborted;
 }
 
-template <typename T>
+template <typename T, int D>
 __global__ void __launch_bounds__(kTcThreads, 1)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
                             const __grid_constant__ CUtensorMap vmap,
                             const __grid_constant__ CUtensorMap qmap, const AttnArgs<T> a) {
+  using C = TcCfg<D>;
+  constexpr int kTcM = C::kM, kTcN = C::kN, kHalfN = C::kHalfN;
+  constexpr int kPiecesPerTile = C::kPiecesPerTile;
+  constexpr int kSlots = kSlotsTc, kKStages = kKStagesTc, kVStages = kVStagesTc;
+  constexpr uint32_t kOCol = C::kOCol;
+  constexpr bool kSplits = D != kHeadDim;  // the planner splits head_dim 256 row items only
   // declared 16-byte aligned so that the 1 KiB check below is not folded away
   extern __shared__ __align__(16) uint8_t smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
   uint64_t* q_full = bars + 0;   // [buffer]: Q tile landed
   uint64_t* q_empty = bars + 2;  // [buffer]: both groups done with the item
   uint64_t* o_free = bars + 4;
@@ -152,12 +171,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* p_full = s_free + kSlots;       // [slot*2 + group]: P written
   uint64_t* mma_drain = p_full + 2 * kSlots;  // every MMA issued has completed
   uint64_t* xmax_bar = mma_drain + 1;         // [tile parity*4 + quad]: maxima written
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBarsTc);
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 2);
-  float* xmax = reinterpret_cast<float*>(smem + kOffX);  // [parity][group][row]
+  float* xmax = reinterpret_cast<float*>(smem + C::kOffX);  // [parity][group][row]
   // Row weight sums at the end of an item go to the item's Q buffer (dead by
-  // then, [group][row]); the buffer is released for the item two ahead only
-  // after both groups have read them.
+  // then, [group][row]); the buffer is released for the item kQBufs ahead
+  // only after both groups have read them.
 
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -223,7 +242,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t* full = is_v ? v_full : k_full;
     uint64_t* empty = is_v ? v_empty : k_empty;
     const int stages = is_v ? kVStages : kKStages;
-    uint8_t* region = smem + (is_v ? kOffV : kOffK);
+    uint8_t* region = smem + (is_v ? C::kOffV : C::kOffK);
     // Q tiles by TMA when a tile is whole query rows (G divides 128) inside
     // the rows the Q map covers, else by the warp's lanes
     const bool q_tma = (kTcM % a.G) == 0 && a.q_map_rows > 0;
@@ -236,26 +255,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int it = it0; it < it1 && !aborted; ++it, ++unit) {
       const WorkItem w = items[it];
       const SeqInfo si = seqs[w.seq];
-      const int h2 = w.kvh * 2;
+      const int hbox = w.kvh * C::kBoxes;  // the KV head's first 64-dim box
       if (!is_v) {
         // the item's Q tile: packed row p = query row p / G, head kvh*G + p % G,
         // i.e. 128/G query rows x G heads x 64 dims per box (rows past the
         // sequence are other sequences' q or zero fill; their output is
         // never stored)
-        const int b = unit & 1;
-        uint8_t* dst = smem + kOffQ + b * kQBytes;
+        const int b = unit % C::kQBufs;
+        uint8_t* dst = smem + C::kOffQ + b * C::kQBytes;
         const int G = a.G, P = si.qrows * G;
         const bool tma_item =
             q_tma && si.q_row0 + (min(P, w.rb0 * kRowBlock + kTcM) - 1) / G < a.q_map_rows;
         int good = 1;
         if (lane == 0) {
-          if (!wait_or_abort(&q_empty[b], ((unit >> 1) & 1u) ^ 1u, flags, aborted)) {
+          if (!wait_or_abort(&q_empty[b], ((unit / C::kQBufs) & 1u) ^ 1u, flags, aborted)) {
             good = 0;
           } else if (tma_item) {
-            mbar_arrive_expect_tx(&q_full[b], kQBytes);
+            mbar_arrive_expect_tx(&q_full[b], C::kQBytes);
             const int row0 = si.q_row0 + (w.rb0 * kRowBlock) / a.G;
-            tma_load_3d(dst, &qmap, &q_full[b], 0, w.kvh * a.G, row0);
-            tma_load_3d(dst + kQHalf, &qmap, &q_full[b], 64, w.kvh * a.G, row0);
+#pragma unroll
+            for (int x = 0; x < C::kBoxes; ++x)
+              tma_load_3d(dst + x * C::kQBox, &qmap, &q_full[b], 64 * x, w.kvh * a.G, row0);
           }
         }
         if (!__shfl_sync(0xffffffffu, good, 0)) {
@@ -265,16 +285,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (!tma_item) {
           // copy with the lanes into the swizzled K-major tile (zeros past the
           // sequence), then publish
-          for (int i = lane; i < kTcM * 16; i += 32) {
-            const int r = i >> 4, c = i & 15;
+          constexpr int kChunks = D / 8;  // 16-byte chunks per row
+          for (int i = lane; i < kTcM * kChunks; i += 32) {
+            const int r = i / kChunks, c = i % kChunks;
             const int pr = w.rb0 * kRowBlock + r;
             uint4 val = make_uint4(0, 0, 0, 0);
             if (pr < P)
               val = __ldg(reinterpret_cast<const uint4*>(
                             a.q + (static_cast<int64_t>(si.q_row0 + pr / G) * a.hq + w.kvh * G +
-                                   pr % G) * kHeadDim) + c);
-            const int half = c >> 3, cc = c & 7;
-            *reinterpret_cast<uint4*>(dst + half * kQHalf + r * 128 + ((cc ^ (r & 7)) << 4)) = val;
+                                   pr % G) * D) + c);
+            const int box = c >> 3, cc = c & 7;
+            *reinterpret_cast<uint4*>(dst + box * C::kQBox + r * 128 + ((cc ^ (r & 7)) << 4)) =
+                val;
           }
           tc::fence_proxy_async_smem();
           __syncwarp();
@@ -283,8 +305,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       const int npieces = w.kt1 - w.kt0;
       const int ntiles = (npieces + kPiecesPerTile - 1) / kPiecesPerTile;
-      // Slot of 16-token piece `i` of the item; lanes fetch 32 pieces (4
-      // tiles) at a time and the next 32 are requested before they are needed.
+      // Slot of 16-token piece `i` of the item; lanes fetch 32 pieces at a
+      // time and the next 32 are requested before they are needed.
       auto piece_slot = [&](int i) -> int {
         if (i >= npieces) return 0;
         const int t0 = (w.kt0 + i) * kTileTokens;
@@ -307,14 +329,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (!wait_or_abort(&empty[st], ((g / stages) & 1u) ^ 1u, flags, aborted)) {
             good = 0;
           } else {
-            mbar_arrive_expect_tx(&full[st], pieces * kPieceBytes);
-            uint8_t* dst = region + st * kKVTile;
+            mbar_arrive_expect_tx(&full[st], pieces * C::kPieceBytes);
+            uint8_t* dst = region + st * C::kKVTile;
             // piece start slots are multiples of 16: coordinates (0, 0,
-            // head-half pair, slot / 8)
+            // first box of the head, slot / 8)
 #pragma unroll
             for (int u = 0; u < kPiecesPerTile; ++u)
               if (u < pieces)
-                tma_load_4d(dst + u * kPieceBytes, map, &full[st], 0, 0, h2, sl[u] >> 3);
+                tma_load_4d(dst + u * C::kPieceBytes, map, &full[st], 0, 0, hbox, sl[u] >> 3);
           }
         }
         if (!__shfl_sync(0xffffffffu, good, 0)) {
@@ -330,8 +352,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (uint32_t t = g > uint32_t(stages) ? g - stages : 0; t < g; ++t)
         wait_bounded_short(&full[t % stages], (t / stages) & 1u, flags + 1);
       if (!is_v && unit > 0) {  // and the last Q tiles
-        for (int u = unit > 2 ? unit - 2 : 0; u < unit; ++u)
-          wait_bounded_short(&q_full[u & 1], (u >> 1) & 1u, flags + 1);
+        for (int u = unit > C::kQBufs ? unit - C::kQBufs : 0; u < unit; ++u)
+          wait_bounded_short(&q_full[u % C::kQBufs], (u / C::kQBufs) & 1u, flags + 1);
       }
     }
   } else if (warp == kMmaWarp || warp == kPvWarp) {
@@ -341,16 +363,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // queue is full) and S runs ahead as far as its slots allow.
     if (lane == 0) {
       constexpr uint32_t idesc_s = tc::idesc_f16(Fmt<T>::v, false, false, kTcM, kTcN);
-      constexpr uint32_t idesc_o = tc::idesc_f16(Fmt<T>::v, false, true, kTcM, kHeadDim);
+      constexpr uint32_t idesc_o = tc::idesc_f16(Fmt<T>::v, false, true, kTcM, D);
       // Descriptors of stage 0 / the Q tile; the 14-bit start-address field
       // (address >> 4) is advanced by plain addition (shared addresses stay
       // below 256 KiB, so it never carries out of the field).
-      // K: K-major, 8-key groups 2 KiB apart, dims 64..127 at +1 KiB.
-      // V: MN-major, 64-dim halves 1 KiB apart (leading), 8-key groups 2 KiB
-      // apart (stride), 16 keys per 4 KiB.
-      const uint64_t q_desc0 = tc::smem_desc_sw128(smem_u32(smem + kOffQ), 16, 1024);
-      const uint64_t k_desc0 = tc::smem_desc_sw128(smem_u32(smem + kOffK), 16, 2048);
-      const uint64_t v_desc0 = tc::smem_desc_sw128(smem_u32(smem + kOffV), 1024, 2048);
+      // K: K-major, 8-key groups kGroupBytes apart, each next 64 dims at +1 KiB.
+      // V: MN-major, 64-dim boxes 1 KiB apart (leading), 8-key groups
+      // kGroupBytes apart (stride), 16 keys per piece.
+      const uint64_t q_desc0 = tc::smem_desc_sw128(smem_u32(smem + C::kOffQ), 16, 1024);
+      const uint64_t k_desc0 = tc::smem_desc_sw128(smem_u32(smem + C::kOffK), 16, C::kGroupBytes);
+      const uint64_t v_desc0 =
+          tc::smem_desc_sw128(smem_u32(smem + C::kOffV), 1024, C::kGroupBytes);
       const bool s_stream = warp == kMmaWarp;
       uint32_t tbase = 0;  // global index of the item's first tile
       uint32_t n = 0;      // tiles issued (slot and phase)
@@ -361,8 +384,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (s_stream) {
           // S_t = Q K_t^T into the next slot once both PVs that read the
           // slot's P have completed.
-          if (!wait_or_abort(&q_full[unit & 1], (unit >> 1) & 1u, flags, aborted)) break;
-          const uint64_t q_desc = q_desc0 + uint64_t(((unit & 1) * kQBytes) >> 4);
+          const int qb = unit % C::kQBufs;
+          if (!wait_or_abort(&q_full[qb], (unit / C::kQBufs) & 1u, flags, aborted)) break;
+          const uint64_t q_desc = q_desc0 + uint64_t((qb * C::kQBytes) >> 4);
           for (int t = 0; t < ntiles && !aborted; ++t, ++n) {
             const int slot = n % kSlots;
             const uint32_t tg = tbase + t;
@@ -370,13 +394,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (!wait_or_abort(&s_free[slot], ((n / kSlots) & 1u) ^ 1u, flags, aborted)) break;
             if (!wait_or_abort(&k_full[st], (tg / kKStages) & 1u, flags, aborted)) break;
             tc::fence_after_sync();
-            const uint64_t k_desc = k_desc0 + uint64_t((st * kKVTile) >> 4);
+            const uint64_t k_desc = k_desc0 + uint64_t((st * C::kKVTile) >> 4);
             const uint32_t d = tmem + slot * kTcN;
 #pragma unroll
-            for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-              const int half = kk >> 2, ko = (kk & 3) * 32;
-              tc::mma_f16(d, q_desc + uint64_t((half * kQHalf + ko) >> 4),
-                          k_desc + uint64_t((half * 1024 + ko) >> 4), idesc_s, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const int box = kk >> 2, ko = (kk & 3) * 32;
+              tc::mma_f16(d, q_desc + uint64_t((box * C::kQBox + ko) >> 4),
+                          k_desc + uint64_t((box * 1024 + ko) >> 4), idesc_s, kk > 0 ? 1u : 0u);
             }
             tc::commit(&s_full[slot]);
             tc::commit(&k_empty[st]);  // S (and every earlier S) done -> K stage free
@@ -396,19 +420,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (!wait_or_abort(&p_full[slot * 2], (n / kSlots) & 1u, flags, aborted)) break;
             if (!wait_or_abort(&p_full[slot * 2 + 1], (n / kSlots) & 1u, flags, aborted)) break;
             tc::fence_after_sync();
-            const uint64_t v_desc = v_desc0 + uint64_t((st * kKVTile) >> 4);
+            const uint64_t v_desc = v_desc0 + uint64_t((st * C::kKVTile) >> 4);
             const uint32_t d = tmem + kOCol;
 #pragma unroll
             for (int gi = 0; gi < 2; ++gi) {
               const uint32_t p_col = tmem + slot * kTcN + gi * kHalfN;
-              const uint64_t vg = v_desc + uint64_t((gi * 4 * kPieceBytes) >> 4);
+              const uint64_t vg =
+                  v_desc + uint64_t((gi * (kPiecesPerTile / 2) * C::kPieceBytes) >> 4);
 #pragma unroll
               for (int part = 0; part < 2; ++part) {
 #pragma unroll
                 for (int kk = 0; kk < kHalfN / 16; ++kk) {
                   const bool first = j == 0 && gi == 0 && part == 0 && kk == 0;
-                  tc::mma_f16_ts(d, p_col + part * 32 + kk * 8,
-                                 vg + uint64_t((kk * kPieceBytes) >> 4), idesc_o,
+                  tc::mma_f16_ts(d, p_col + part * (kHalfN / 2) + kk * 8,
+                                 vg + uint64_t((kk * C::kPieceBytes) >> 4), idesc_o,
                                  first ? 0u : 1u);
                 }
               }
@@ -428,11 +453,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else if (warp < 8) {
     // ------------------------------------------------ softmax groups / epilogue
+    constexpr int kGD = C::kGroupDims;
     const int gi = warp >= 4 ? 1 : 0;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // packed row = TMEM lane
     const uint32_t lane_addr = tmem + (uint32_t(quad * 32) << 16);
-    const uint32_t o_dims = lane_addr + kOCol + gi * 64;  // this group's 64 O dims
+    const uint32_t o_dims = lane_addr + kOCol + gi * kGD;  // this group's O dims
     const int G = a.G;
     const bool causal = view == 1;
     uint32_t tbase = 0;
@@ -446,7 +472,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int P = si.qrows * G;
       const int p = w.rb0 * kRowBlock + r;
       const bool row_valid = p < P;
-      const int lim = (causal && row_valid) ? si.length - si.qrows + p / G + 1 : si.length;
+      // keys this row sees in this item: the mask's, cut at the end of the
+      // item's pieces (a split item covers part of the range; head_dim 128
+      // items are never split)
+      int lim = (causal && row_valid) ? si.length - si.qrows + p / G + 1 : si.length;
+      if constexpr (kSplits) lim = min(lim, w.kt1 * kTileTokens);
       // m_used stays -inf until the first unmasked key (its weights are 0)
       float m_used = -INFINITY, l = 0.f;
       bool first = true;
@@ -457,12 +487,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t half_addr = slot_addr + gi * kHalfN;
         if (!wait_warp(&s_full[slot], (nt / kSlots) & 1u, flags, aborted)) break;
         tc::fence_after_sync();
-        // this group's 64 S columns straight into registers
+        // this group's S columns straight into registers
         const int key0 = (w.kt0 + kPiecesPerTile * j) * kTileTokens;
         const int tkey = key0 + gi * kHalfN;
         float s[kHalfN];
-        tc::ld_32x32b_x32(half_addr, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-        tc::ld_32x32b_x32(half_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+#pragma unroll
+        for (int c = 0; c < kHalfN; c += 32)
+          tc::ld_32x32b_x32(half_addr + c, *reinterpret_cast<uint32_t(*)[32]>(&s[c]));
         tc::wait_ld();
         if (tkey + kHalfN > lim) {
 #pragma unroll
@@ -500,12 +531,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (!first) {
             // O holds the item's earlier tiles: wait for the last PV into it
             // (tile nt - 1; every earlier one completed before S of tile
-            // nt - 1 was issued), then rescale this group's 64 dims in TMEM.
+            // nt - 1 was issued), then rescale this group's O dims in TMEM.
             if (!wait_warp(&s_free[(nt - 1) % kSlots], ((nt - 1) / kSlots) & 1u, flags, aborted))
               break;
             tc::fence_after_sync();
 #pragma unroll
-            for (int c2 = 0; c2 < 2; ++c2) {
+            for (int c2 = 0; c2 < kGD / 32; ++c2) {
               float ov[32];
               tc::ld_32x32b_x32(o_dims + c2 * 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
               tc::wait_ld();
@@ -519,14 +550,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         first = false;
         const float m_sub = m_used == -INFINITY ? 0.f : m_used;
-        // P = exp2(S * scale - m): high 16-bit part over the half's columns
-        // [0, 32), residual over [32, 64) (S is already in registers).
+        // P = exp2(S * scale - m): high 16-bit part over the half's first
+        // kHalfN/2 columns, residual over the last kHalfN/2 (S is already in
+        // registers).
         float2 l4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                         make_float2(0.f, 0.f)};
         const float2 sc2 = make_float2(a.scale_log2, a.scale_log2);
         const float2 nm2 = make_float2(-m_sub, -m_sub);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {  // 32 keys -> 16 high + 16 residual columns
+        for (int h = 0; h < kHalfN / 32; ++h) {  // 32 keys -> 16 high + 16 residual columns
           uint32_t hi[16], lo[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
@@ -538,7 +570,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             lo[e] = pack2<T>(res.x, res.y);
           }
           tc::st_32x32b_x16(half_addr + 16 * h, hi);
-          tc::st_32x32b_x16(half_addr + 32 + 16 * h, lo);
+          tc::st_32x32b_x16(half_addr + kHalfN / 2 + 16 * h, lo);
         }
         l += ((l4[0].x + l4[0].y) + (l4[1].x + l4[1].y)) + ((l4[2].x + l4[2].y) + (l4[3].x + l4[3].y));
         // V rows of this half past the sequence end or past the loaded pieces
@@ -549,14 +581,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (valid < kHalfN) {
           const int st = tg % kVStages;
           if (!wait_warp(&v_full[st], (tg / kVStages) & 1u, flags, aborted)) break;
-          uint8_t* vb = smem + kOffV + st * kKVTile;
+          uint8_t* vb = smem + C::kOffV + st * C::kKVTile;
           const int r0 = max(valid, 0);
-          const int nch = (kHalfN - r0) * 8;  // 16-byte chunks per head-half
-          for (int i = r; i < 2 * nch; i += 128) {
-            const int half = i / nch, rem = i % nch;
+          const int nch = (kHalfN - r0) * 8;  // 16-byte chunks per 64-dim box
+          for (int i = r; i < C::kBoxes * nch; i += 128) {
+            const int box = i / nch, rem = i % nch;
             const int row = gi * kHalfN + r0 + rem / 8, ch = rem % 8;
-            *reinterpret_cast<uint4*>(vb + (row >> 3) * 2048 + half * 1024 + (row & 7) * 128 +
-                                      (ch << 4)) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(vb + (row >> 3) * C::kGroupBytes + box * 1024 +
+                                      (row & 7) * 128 + (ch << 4)) = make_uint4(0, 0, 0, 0);
           }
           tc::fence_proxy_async_smem();
         }
@@ -574,21 +606,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           !wait_warp(&s_free[(nt - 1) % kSlots], ((nt - 1) / kSlots) & 1u, flags, aborted))
         break;
       // Row weight sums of both groups (same max) -> divide and store this
-      // group's 64 dims.
-      float* xsum = reinterpret_cast<float*>(smem + kOffQ + (unit & 1) * kQBytes);
+      // group's O dims, or write them unnormalised into the item's split
+      // record with the row's (m, l).
+      const int qb = unit % C::kQBufs;
+      float* xsum = reinterpret_cast<float*>(smem + C::kOffQ + qb * C::kQBytes);
       xsum[gi * kTcM + r] = l;
       mbar_arrive(l_done);
       if (!wait_warp(l_done, unit & 1, flags, aborted)) break;
       tc::fence_after_sync();
-      const float inv = 1.f / (l + xsum[(gi ^ 1) * kTcM + r]);
-      // the Q buffer (and these sums) may now take the item two ahead
+      const float lsum = l + xsum[(gi ^ 1) * kTcM + r];
+      const float inv = 1.f / lsum;
+      // the Q buffer (and these sums) may now take the next item
       __syncwarp();
-      if (lane == 0) mbar_arrive(&q_empty[unit & 1]);
-      T* dst = row_valid ? a.out + (static_cast<int64_t>(si.q_row0 + p / G) * a.hq + w.kvh * G +
-                                    p % G) * kHeadDim + gi * 64
-                         : nullptr;
+      if (lane == 0) mbar_arrive(&q_empty[qb]);
+      const bool split = kSplits && w.part >= 0;
+      const int rows_rec = min(P, w.rb0 * kRowBlock + kTcM) - w.rb0 * kRowBlock;
+      float* rec = split ? a.partials + w.part : nullptr;
+      T* dst = row_valid && !split
+                   ? a.out + (static_cast<int64_t>(si.q_row0 + p / G) * a.hq + w.kvh * G + p % G) *
+                                 D + gi * kGD
+                   : nullptr;
+      if (split && row_valid && gi == 0) {
+        rec[rows_rec * D + r] = m_used;
+        rec[rows_rec * (D + 1) + r] = lsum;
+      }
 #pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {
+      for (int c2 = 0; c2 < kGD / 32; ++c2) {
         float o[32];
         tc::ld_32x32b_x32(o_dims + c2 * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
         tc::wait_ld();
@@ -602,6 +645,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             pk.w = pack2<T>(o[8 * v + 6] * inv, o[8 * v + 7] * inv);
             *reinterpret_cast<uint4*>(dst + c2 * 32 + 8 * v) = pk;
           }
+        } else if (split && row_valid) {
+          float* row = rec + r * D + gi * kGD + c2 * 32;
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            *reinterpret_cast<float4*>(row + 4 * v) =
+                make_float4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
         }
       }
       // O and this item's sums have been read: the next item may reuse them
@@ -619,32 +668,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
-template <typename T>
+template <typename T, int D>
 int launch_t(const CUtensorMap& kmap, const CUtensorMap& vmap, const CUtensorMap& qmap,
              const AttnArgs<T>& args, int grid, cudaStream_t stream) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(paged_prefill_tc_kernel<T>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+    attr_err = cudaFuncSetAttribute(paged_prefill_tc_kernel<T, D>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<D>::kSmem);
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "paged_prefill_tc_kernel attribute");
-  FE_CUDA_TRY(launch_pdl(paged_prefill_tc_kernel<T>, dim3(grid), dim3(kTcThreads), kTcSmem, stream,
-                         kmap, vmap, qmap, args));
+  FE_CUDA_TRY(launch_pdl(paged_prefill_tc_kernel<T, D>, dim3(grid), dim3(kTcThreads),
+                         TcCfg<D>::kSmem, stream, kmap, vmap, qmap, args));
   return FE_OK;
+}
+
+template <typename T>
+int launch_dim(int dim, const CUtensorMap& kmap, const CUtensorMap& vmap, const CUtensorMap& qmap,
+               const void* args, int grid, cudaStream_t stream) {
+  const auto& a = *static_cast<const AttnArgs<T>*>(args);
+  if (dim == kWideHeadDim) return launch_t<T, kWideHeadDim>(kmap, vmap, qmap, a, grid, stream);
+  return launch_t<T, kHeadDim>(kmap, vmap, qmap, a, grid, stream);
 }
 
 }  // namespace
 
-int prefill_tc_smem_bytes() { return kTcSmem; }
+int prefill_tc_smem_bytes() { return TcCfg<kHeadDim>::kSmem; }
 
-int prefill_tc_launch(int dtype, const CUtensorMap& kmap, const CUtensorMap& vmap,
+int prefill_tc_launch(int dtype, int dim, const CUtensorMap& kmap, const CUtensorMap& vmap,
                       const CUtensorMap& qmap, const void* args, int grid, cudaStream_t stream) {
   if (dtype == FE_DTYPE_BF16)
-    return launch_t<__nv_bfloat16>(kmap, vmap, qmap,
-                                   *static_cast<const AttnArgs<__nv_bfloat16>*>(args), grid, stream);
-  return launch_t<__half>(kmap, vmap, qmap, *static_cast<const AttnArgs<__half>*>(args), grid,
-                          stream);
+    return launch_dim<__nv_bfloat16>(dim, kmap, vmap, qmap, args, grid, stream);
+  return launch_dim<__half>(dim, kmap, vmap, qmap, args, grid, stream);
 }
 
 }  // namespace fe

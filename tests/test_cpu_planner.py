@@ -154,8 +154,8 @@ def test_zero_row_sequences_are_skipped():
 
 
 def _wide_units_covered(view, md, G, causal):
-    """Every (sequence, KV head, 64-row block) of the multi-block sequences is
-    on the list once per key tile of its mask's range, pieces contiguous."""
+    """Every (sequence, KV head, 128-row block) of the multi-block sequences
+    is on the list once per key tile of its mask's range, pieces contiguous."""
     items = view["items"]
     q = np.diff(md.qo)
     L = md.lengths(16)
@@ -165,20 +165,20 @@ def _wide_units_covered(view, md, G, causal):
             assert not (items["seq"] == b).any()
             continue
         for h in range(2):
-            for rb0 in range(0, -(-P // 16), 4):
+            for rb0 in range(0, -(-P // 16), 8):
                 its = items[(items["seq"] == b) & (items["kvh"] == h) & (items["rb0"] == rb0)]
                 its = np.sort(its, order="kt0")
-                last_row = min(P, (rb0 + 4) * 16) - 1
+                last_row = min(P, (rb0 + 8) * 16) - 1
                 keys = int(L[b]) - int(q[b]) + last_row // G + 1 if causal else int(L[b])
-                assert len(its) >= 1 and (its["key_mode"] == 2).all()
+                assert len(its) >= 1 and (its["key_mode"] == 0).all()
                 assert its["kt0"][0] == 0 and its["kt1"][-1] == -(-keys // 16)
                 assert (its["kt0"][1:] == its["kt1"][:-1]).all()
-                assert (its["nrb"] == min(4, -(-P // 16) - rb0)).all()
+                assert (its["nrb"] == min(8, -(-P // 16) - rb0)).all()
 
 
 def test_head_dim_256_plan_lists():
-    """head_dim 256 plans put every (sequence, KV head, 64-row block) of the
-    multi-block sequences on the row lists for the wide kernel, with each
+    """head_dim 256 plans put every (sequence, KV head, 128-row block) of the
+    multi-block sequences on the row lists for the tcgen05 kernel, with each
     mask's key range; sequences whose packed rows fit one 16-row block go to
     the decode list (two KV heads per item), cut exactly like head_dim 128,
     with split records of rows x (256 + 2) floats."""
@@ -193,7 +193,7 @@ def test_head_dim_256_plan_lists():
     _wide_units_covered(v0, md, G, causal=False)
     _wide_units_covered(v1, md, G, causal=True)
     for v in (v0, v1):
-        assert v["grid"] <= 16 and len(v["cta_off"]) == v["grid"] + 1
+        assert v["grid"] <= 8 and len(v["cta_off"]) == v["grid"] + 1
         assert v["cta_off"][-1] == len(v["items"]) and (np.diff(v["cta_off"]) >= 0).all()
     # decode list: both KV heads in one unit, key tiles covered exactly once
     it2 = v2["items"]
@@ -213,9 +213,9 @@ def test_head_dim_256_plan_lists():
 
 def test_head_dim_256_draft_blocks_are_split():
     """DFlash-style draft blocks (16 rows over long contexts) give too few
-    64-row items to fill the GPU: their key ranges are split into pieces of at
-    about 16 tiles or more, whose records (one KV head, the item's rows) the merge
-    kernel maps back with row0 / rows_per_head."""
+    128-row items to fill the GPU: their key ranges are split into pieces of
+    about 16 tiles or more, whose records (one KV head, the item's rows) the
+    merge kernel maps back with row0 / rows_per_head."""
     from fekv.metadata import build_step_metadata
     tables = [np.arange(i * 200, i * 200 + 200) for i in range(2)]
     md = build_step_metadata(tables, [3000, 2500], [16, 16], 16)
@@ -225,15 +225,15 @@ def test_head_dim_256_draft_blocks_are_split():
     for causal, v in ((False, meta["views"][0]), (True, meta["views"][1])):
         _wide_units_covered(v, md, G, causal)
         it = v["items"]
-        assert len(it) > 8  # 2 seqs x 2 KV heads x 2 row items, split
+        assert len(it) > 4  # 2 seqs x 2 KV heads x 1 row item, split
         split = it[it["part"] >= 0]
         assert len(split) == len(it)
         # pieces split a unit evenly, each near the 16-tile minimum or longer
         assert ((it["kt1"] - it["kt0"]) >= 8).all()
         for gi in v["groups"]:
-            assert gi["nsplit"] >= 2 and gi["rows"] == 64
-            assert gi["row0"] in (0, 64) and gi["rows_per_head"] == 64
-            assert gi["rec_floats"] == 64 * 258
+            assert gi["nsplit"] >= 2 and gi["rows"] == 128
+            assert gi["row0"] == 0 and gi["rows_per_head"] == 128
+            assert gi["rec_floats"] == 128 * 258
         # every piece's record lies inside its group's records
         for x in split:
             gi = v["groups"][x["group"]]

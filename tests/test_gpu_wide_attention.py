@@ -1,4 +1,4 @@
-"""head_dim 256 (fe_wide.cu) through the same plan / attention calls, against
+"""head_dim 256 (tcgen05 rows in fe_prefill_tc.cu, decode rows in fe_decode.cu) through the same plan / attention calls, against
 the fp32 torch restatement of the reference's ATen attention
 (src/portable_gpu_ops.cpp:39-44, which takes any head_dim). Tolerance as for
 head_dim 128: fe_testutil.ATOL widened by one output ulp."""
