@@ -39,6 +39,15 @@
 //             consumption of P. At the end each group divides its 64 dims by
 //             the summed row weights and stores them in 16 bits.
 // All hand-offs are mbarriers; every wait is bounded.
+//
+// head_dim 256 (hybrid and DFlash draft models, which the reference serves
+// through ATen with any head_dim) instantiates the same kernel with 64-key
+// tiles, one 64 KiB Q buffer, S slots of 64 TMEM columns and O (256 fp32
+// columns) at column 256; each softmax group then owns 32 keys of a tile and
+// 128 of O's dims. Its items may be pieces of a key range split across CTAs
+// (few 128-row items, as DFlash draft blocks give): a piece stores its
+// unnormalised O with the row's (m, l) into a partial record, and
+// decode_merge_kernel combines them.
 #include <mutex>
 
 #include "fe_attn_common.cuh"
