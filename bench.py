@@ -11,7 +11,11 @@ layers, 64 sequences, contexts U[512,4096], page 16). Under torchrun every
 rank runs its own 64 sequences (weak scaling); NCCL is used only after the
 timed loop to gather per-rank results (no collective on the hot path).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c5]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3|c4|c5|q35|draft]
+
+c3 / c4 time the chunked-prefill and verify steps (rows/s, tensor-core
+roofline); q35 and draft are head_dim 256 steps (hybrid-model full-attention
+decode, and 16-row draft blocks under the full mask).
   python bench.py --impl reference ...   # the reference's own CPU/ATen path
 
 Prints one JSON line (rank 0).
@@ -193,11 +197,15 @@ def make_workload(config, rank, world, total_steps):
         return workloads.c3(seed=1000 + rank)
     if config == "c4":
         return workloads.c4(seed=1000 + rank)
+    if config == "q35":
+        return workloads.q35(seed=1000 + rank, steps=total_steps)
+    if config == "draft":
+        return workloads.draft(seed=1000 + rank)
     raise ValueError(config)
 
 
 def is_decode(config):
-    return config in ("c2", "c5")
+    return config in ("c2", "c5", "q35")
 
 
 def attention_flops(w, md, select=None):
@@ -657,7 +665,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c2", "c3", "c4", "c5"], default="c2")
+    ap.add_argument("--config", choices=["c2", "c3", "c4", "c5", "q35", "draft"], default="c2")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--pool-gb", type=float, default=150.0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

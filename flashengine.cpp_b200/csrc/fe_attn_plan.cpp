@@ -125,7 +125,7 @@ int build_view(const PlanConfig& cfg, const std::vector<Unit>& units, int grid_c
   return FE_OK;
 }
 
-// Decode lists are bandwidth-bound and their cost is proportional to key
+// Decode lists (and head_dim 256 row lists) cost in proportion to key
 // tiles, so they are balanced exactly: the units' tile ranges are laid end to
 // end and cut into `grid` equal contiguous pieces, one per CTA. A unit cut
 // into several pieces becomes a split unit (its pieces write partial records,
@@ -163,11 +163,15 @@ int build_cut_view(const PlanConfig& cfg, const std::vector<Unit>& units, int gr
   std::vector<int> group_of(units.size(), -1), part0_of(units.size(), -1), next_split(units.size(), 0);
   for (size_t i = 0; i < units.size(); ++i) {
     if (pieces[i] > 1) {
-      const int rec = partial_rec_floats(units[i].rows, cfg.dim);
+      const Unit& u = units[i];
+      const int rec = partial_rec_floats(u.rows, cfg.dim);
       group_of[i] = static_cast<int>(v.groups.size());
       part0_of[i] = static_cast<int>(v.partial_floats);
-      v.groups.push_back(SplitGroup{pieces[i], part0_of[i], rec, units[i].rows, units[i].seq,
-                                    units[i].kvh, 0, 0});
+      // key-mode records hold all of the sequence's rows; row-mode ones the
+      // unit's rows of one KV head from packed row rb0*16
+      const bool rows_rec = u.key_mode != 1;
+      v.groups.push_back(SplitGroup{pieces[i], part0_of[i], rec, u.rows, u.seq, u.kvh,
+                                    rows_rec ? u.rb0 * kRowBlock : 0, rows_rec ? u.rows : 0});
       v.partial_floats += int64_t(rec) * pieces[i];
       ++v.split_units;
     }
@@ -211,7 +215,7 @@ int build_cut_view(const PlanConfig& cfg, const std::vector<Unit>& units, int gr
   v.chunk = static_cast<int>(per);
   if (static_cast<int>(v.items.size()) > cfg.max_items || v.partial_floats > cfg.partial_capacity ||
       static_cast<int>(v.groups.size()) > cfg.max_groups) {
-    err = "decode work exceeds the plan's item / split-workspace capacity";
+    err = "attention work exceeds the plan's item / split-workspace capacity";
     return FE_ERR_CAPACITY;
   }
   if (fixed_grid && v.grid < grid_cap) {
@@ -318,17 +322,28 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
   // when there is no row work); 2: decode work.
   View views[3];
   {
-    // head_dim 256 splits the key ranges of row items too (pieces of at
-    // least kWideMinChunk tiles) when there are fewer items than CTAs, as
-    // DFlash draft blocks give; head_dim 128 keeps whole items (cfg.row_split)
-    const int row_min_chunk =
-        cfg.dim == kWideHeadDim ? kWideMinChunk : (cfg.row_split ? 16 : (1 << 29));
-    const int per_cta = cfg.dim == kWideHeadDim ? 1 : 4;
-    int rc = build_view(cfg, row_units_full, cfg.grid_cap, per_cta, row_min_chunk, fixed_grid,
-                        views[0], err);
-    if (rc != FE_OK) return rc;
-    rc = build_view(cfg, row_units_causal, cfg.grid_cap, per_cta, row_min_chunk, fixed_grid,
-                    views[1], err);
+    int rc;
+    if (cfg.dim == kWideHeadDim) {
+      // head_dim 256 row lists are cut exactly like the decode list: the
+      // tcgen05 kernel's time per key tile hardly depends on how many of an
+      // item's 128 rows are valid, so equal tile counts per CTA balance it,
+      // at the price of up to one split unit per CTA boundary (pieces of at
+      // least kWideMinChunk tiles per CTA)
+      rc = build_cut_view(cfg, row_units_full, cfg.grid_cap, kWideMinChunk, fixed_grid, views[0],
+                          err);
+      if (rc != FE_OK) return rc;
+      rc = build_cut_view(cfg, row_units_causal, cfg.grid_cap, kWideMinChunk, fixed_grid,
+                          views[1], err);
+    } else {
+      // head_dim 128 keeps whole items (cfg.row_split), longest first onto
+      // the least-loaded CTA
+      const int row_min_chunk = cfg.row_split ? 16 : (1 << 29);
+      rc = build_view(cfg, row_units_full, cfg.grid_cap, 4, row_min_chunk, fixed_grid, views[0],
+                      err);
+      if (rc != FE_OK) return rc;
+      rc = build_view(cfg, row_units_causal, cfg.grid_cap, 4, row_min_chunk, fixed_grid, views[1],
+                      err);
+    }
     if (rc != FE_OK) return rc;
     rc = build_cut_view(cfg, key_units, cfg.dec_grid_cap, 8, fixed_grid, views[2], err);
     if (rc != FE_OK) return rc;

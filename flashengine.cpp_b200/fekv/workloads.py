@@ -18,6 +18,16 @@ C4 ``c4``: hq32/hkv4 bf16, 48 layers; 128 sequences over one shared
     a 16-row verify block per sequence, non-causal.
 C5 ``c5``: hq64/hkv8 bf16, 64 layers; 1024 sequences, 128 per GPU, contexts
     LogNormal(ln 8192, 0.5) clipped to [2048, 32768]; split-K decode.
+
+Two head_dim 256 workloads cover the hybrid and draft models' full-attention
+layers (the reference serves them through ATen with any head_dim):
+Q35 ``q35``: hq16/hkv2/d256 bf16 (the full-attention layer shape of the
+    public Qwen3-Next hybrid configuration), 12 layers (one full-attention
+    layer in four of a 48-layer stack); 64 sequences, contexts U[512,4096];
+    x0.5; 1 appended token + decode per step.
+DFL ``draft``: hq16/hkv2/d256 bf16, 4 layers; 32 sequences, contexts
+    U[512,4096], each appending a 16-row block attended with the full
+    (non-causal) mask, as a block draft model's step does.
 """
 from __future__ import annotations
 
@@ -103,7 +113,7 @@ def c1(seed: int = 0) -> PagedWorkload:
 
 
 def decode_workload(name, hq, hkv, ctx, bf16, seed, steps=1, scale=1.0, layers=1, page=16,
-                    spare_pages=0) -> PagedWorkload:
+                    spare_pages=0, dim=128) -> PagedWorkload:
     """Batched decode: 1 appended token per sequence per step, with block
     tables drawn as a seeded random permutation of a pool sized to the sum of
     contexts (+ steps) plus `spare_pages`."""
@@ -112,7 +122,7 @@ def decode_workload(name, hq, hkv, ctx, bf16, seed, steps=1, scale=1.0, layers=1
     npages = [-(-(int(c) + steps) // page) for c in ctx]
     blocks = int(sum(npages)) + int(spare_pages)
     perm = rng.permutation(blocks)
-    return PagedWorkload(name, hq, hkv, 128, page, bf16, blocks,
+    return PagedWorkload(name, hq, hkv, dim, page, bf16, blocks,
                          _tables_from_permutation(perm, npages), ctx,
                          np.ones(ctx.shape[0], dtype=np.int64), True, scale, layers, seed)
 
@@ -207,6 +217,25 @@ def c5(rank: int = 0, world: int = 1, seed: int = 0, steps: int = 32, per_gpu: i
                         layers=64)
     w.notes["sigma"] = 0.5
     return w
+
+
+def q35(seed: int = 0, steps: int = 1, batch: int = 64) -> PagedWorkload:
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(512, 4097, size=batch)
+    return decode_workload("Q35", 16, 2, ctx, True, seed + 1, steps=steps, scale=0.5, layers=12,
+                           dim=256)
+
+
+def draft(seed: int = 0, batch: int = 32, block: int = 16) -> PagedWorkload:
+    rng = np.random.default_rng(seed)
+    page = 16
+    cached = rng.integers(512, 4097, size=batch).astype(np.int64)
+    rows = np.full(batch, block, dtype=np.int64)
+    npages = [-(-int(c + r) // page) for c, r in zip(cached, rows)]
+    blocks = int(sum(npages))
+    perm = rng.permutation(blocks)
+    return PagedWorkload("DFL", 16, 2, 256, page, True, blocks,
+                         _tables_from_permutation(perm, npages), cached, rows, False, 0.5, 4, seed)
 
 
 def random_bits(rng, shape, bf16: bool, scale: float = 1.0) -> np.ndarray:

@@ -213,9 +213,9 @@ def test_head_dim_256_plan_lists():
 
 def test_head_dim_256_draft_blocks_are_split():
     """DFlash-style draft blocks (16 rows over long contexts) give too few
-    128-row items to fill the GPU: their key ranges are split into pieces of
-    about 16 tiles or more, whose records (one KV head, the item's rows) the
-    merge kernel maps back with row0 / rows_per_head."""
+    128-row items to fill the GPU: the row lists are cut into equal tile
+    ranges per CTA, and units cut in pieces write records (one KV head, the
+    unit's rows) that the merge kernel maps back with row0 / rows_per_head."""
     from fekv.metadata import build_step_metadata
     tables = [np.arange(i * 200, i * 200 + 200) for i in range(2)]
     md = build_step_metadata(tables, [3000, 2500], [16, 16], 16)
@@ -227,9 +227,12 @@ def test_head_dim_256_draft_blocks_are_split():
         it = v["items"]
         assert len(it) > 4  # 2 seqs x 2 KV heads x 1 row item, split
         split = it[it["part"] >= 0]
-        assert len(split) == len(it)
-        # pieces split a unit evenly, each near the 16-tile minimum or longer
-        assert ((it["kt1"] - it["kt0"]) >= 8).all()
+        assert len(split) >= 1
+        # exact cut: every CTA but the last streams the same number of tiles
+        co = v["cta_off"]
+        loads = [int((it[co[c]:co[c + 1]]["kt1"] - it[co[c]:co[c + 1]]["kt0"]).sum())
+                 for c in range(v["grid"])]
+        assert v["grid"] <= 148 and max(loads[:-1]) == min(loads[:-1]) >= 16
         for gi in v["groups"]:
             assert gi["nsplit"] >= 2 and gi["rows"] == 128
             assert gi["row0"] == 0 and gi["rows_per_head"] == 128
