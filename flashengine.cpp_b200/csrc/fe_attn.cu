@@ -26,7 +26,7 @@ namespace fe {
 
 int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
-int decode_merge_launch(int dtype, int dim, int list, const void* args, int grid,
+int decode_merge_launch(int dtype, int dim, int list, const void* args, int grid, int grid_rows,
                         cudaStream_t stream);
 int prefill_tc_launch(int dtype, int dim, const CUtensorMap& kmap, const CUtensorMap& vmap,
                       const CUtensorMap& qmap, const void* args, int grid, cudaStream_t stream);
@@ -511,6 +511,15 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
   // split units of the decode list are merged by a second, dependent kernel
   int grid_merge = 0;
   if (grid_dec > 0) grid_merge = p->fixed_grid ? p->cfg.dec_grid_cap : h.n_groups[2];
+  // Merge CTAs per split unit: one warp per record row, 32 rows per CTA. The
+  // host plan knows its units' rows; a graph plan (fixed launch geometry) or
+  // a device-built plan takes the bound: H heads x 16 packed rows for the
+  // decode list, 128 rows for a row list.
+  auto merge_y = [&](int list) {
+    const int bound = list == 2 ? p->cfg.dec_heads * kRowBlock : 128;
+    const int rows = (p->fixed_grid || p->device_planned) ? bound : p->last.split_rows[list];
+    return std::max(1, (rows + 31) / 32);
+  };
   // the row kernel's Q tiles come from a tensor map over this call's q
   // (the prepared step's query rows, which a graph plan keeps fixed)
   CUtensorMap qmap;
@@ -533,12 +542,13 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
   auto launch_all = [&](const auto& a) -> int {
     if (grid_dec > 0) {
       int rc = decode_launch(p->dtype, dim, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
-      if (rc == FE_OK) rc = decode_merge_launch(p->dtype, dim, 2, &a, grid_merge, s);
+      if (rc == FE_OK) rc = decode_merge_launch(p->dtype, dim, 2, &a, grid_merge, merge_y(2), s);
       if (rc != FE_OK) return rc;
     }
     if (grid_rows > 0) {
       int rc = prefill_tc_launch(p->dtype, dim, p->kmap_tc, p->vmap_tc, qmap, &a, grid_rows, s);
-      if (rc == FE_OK) rc = decode_merge_launch(p->dtype, dim, view, &a, grid_row_merge, s);
+      if (rc == FE_OK)
+        rc = decode_merge_launch(p->dtype, dim, view, &a, grid_row_merge, merge_y(view), s);
       return rc;
     }
     return FE_OK;

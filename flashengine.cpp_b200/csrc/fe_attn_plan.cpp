@@ -435,6 +435,9 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
   for (int c = 0; c < 3; ++c) out.grid[c] = views[c].grid;
   out.kv_tokens = kv_tokens;
   out.partial_floats = row_floats + views[2].partial_floats;
+  for (int c = 0; c < 3; ++c)
+    for (const auto& gi : views[c].groups)
+      if (gi.nsplit > 1) out.split_rows[c] = std::max(out.split_rows[c], gi.rows);
   return FE_OK;
 }
 

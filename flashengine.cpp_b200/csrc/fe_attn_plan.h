@@ -91,6 +91,7 @@ struct PlanResult {
   int n_items = 0, n_groups = 0, decode_items = 0, prefill_items = 0, split_units = 0;
   int chunk_tiles = 0;
   int grid[3] = {0, 0, 0};    // CTAs per work list (0 = nothing to launch)
+  int split_rows[3] = {0, 0, 0};  // most rows in one split unit's records, per list
   int64_t kv_tokens = 0, partial_floats = 0;
 };
 

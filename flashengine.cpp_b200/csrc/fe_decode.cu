@@ -33,7 +33,7 @@ namespace fe {
 
 int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
-int decode_merge_launch(int dtype, int dim, int list, const void* args, int grid,
+int decode_merge_launch(int dtype, int dim, int list, const void* args, int grid, int grid_rows,
                         cudaStream_t stream);
 int decode_smem_bytes(int heads);
 
@@ -462,14 +462,16 @@ int decode_smem_bytes(int heads) {
 
 namespace {
 
-// Merge the partial records of every split unit of the decode list: one CTA
-// per unit (striding when the grid is smaller, as under graph replay, where
-// the grid is fixed and the unit count comes from the metadata), one warp per
-// merged row. A row's loads are issued together (the split records' O vectors
-// four at a time, m and l one split per lane), so a row costs about one L2
-// round trip. Launched with programmatic stream serialization after
-// paged_decode_kernel: its CTAs become resident on the SMs the decode grid's
-// early finishers free and start when that grid has completed.
+// Merge the partial records of every split unit of a work list (the decode
+// list, or a head_dim 256 row list): gridDim.x CTAs stride over the units
+// (fewer than units under graph replay, where the grid is fixed and the unit
+// count comes from the metadata), gridDim.y CTAs share a unit's rows, one
+// warp per merged row, so all rows of a unit are in flight at once. A row's
+// loads are issued together (the split records' O vectors four at a time, m
+// and l one split per lane), so a row costs about one L2 round trip.
+// Launched with programmatic stream serialization after the kernel that
+// wrote the records: its CTAs become resident on the SMs that grid's early
+// finishers free and start when that grid has completed.
 constexpr int kMergeThreads = 1024;
 
 // Records of a D-dim split unit: O[rows][D] unnormalised, then m[rows], l[rows].
@@ -550,7 +552,8 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const AttnA
     if (gi.nsplit < 2) continue;  // placeholder ids of the row lists
     const SeqInfo si = seqs[gi.seq];
     const int rph = gi.rows_per_head > 0 ? gi.rows_per_head : si.qrows * G;
-    for (int r = warp; r < gi.rows; r += kMergeThreads / 32) {
+    for (int r = warp + blockIdx.y * (kMergeThreads / 32); r < gi.rows;
+         r += gridDim.y * (kMergeThreads / 32)) {
       const int rh = r / rph, p = gi.row0 + r % rph;
       T* dst = a.out + (static_cast<int64_t>(si.q_row0 + p / G) * a.hq + (gi.kvh + rh) * G +
                         p % G) * D;
@@ -560,25 +563,28 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const AttnA
 }
 
 template <typename T>
-int launch_merge_t(const AttnArgs<T>& args, int dim, int list, int grid, cudaStream_t stream) {
+int launch_merge_t(const AttnArgs<T>& args, int dim, int list, dim3 grid, cudaStream_t stream) {
   if (dim == kWideHeadDim)
-    FE_CUDA_TRY(launch_pdl(decode_merge_kernel<T, kWideHeadDim>, dim3(grid), dim3(kMergeThreads), 0,
+    FE_CUDA_TRY(launch_pdl(decode_merge_kernel<T, kWideHeadDim>, grid, dim3(kMergeThreads), 0,
                            stream, args, list));
   else
-    FE_CUDA_TRY(launch_pdl(decode_merge_kernel<T, kHeadDim>, dim3(grid), dim3(kMergeThreads), 0,
-                           stream, args, list));
+    FE_CUDA_TRY(launch_pdl(decode_merge_kernel<T, kHeadDim>, grid, dim3(kMergeThreads), 0, stream,
+                           args, list));
   return FE_OK;
 }
 
 }  // namespace
 
-int decode_merge_launch(int dtype, int dim, int list, const void* args, int grid,
+// grid: CTAs over the list's split units (strided); grid_rows: CTAs per
+// unit, each taking 32 of its record rows (one per warp), strided.
+int decode_merge_launch(int dtype, int dim, int list, const void* args, int grid, int grid_rows,
                         cudaStream_t stream) {
   if (grid <= 0) return FE_OK;
+  const dim3 g(grid, grid_rows > 0 ? grid_rows : 1);
   if (dtype == FE_DTYPE_BF16)
-    return launch_merge_t(*static_cast<const AttnArgs<__nv_bfloat16>*>(args), dim, list, grid,
+    return launch_merge_t(*static_cast<const AttnArgs<__nv_bfloat16>*>(args), dim, list, g,
                           stream);
-  return launch_merge_t(*static_cast<const AttnArgs<__half>*>(args), dim, list, grid, stream);
+  return launch_merge_t(*static_cast<const AttnArgs<__half>*>(args), dim, list, g, stream);
 }
 
 int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
