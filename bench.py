@@ -66,6 +66,8 @@ NCU_TRAFFIC = {
                                     "profiles/paged_decode_kernel_c2.md"),
     ("C4", "paged_prefill_tc_kernel"): (63075840, 75586338816.0, False,
                                         "profiles/paged_prefill_tc_kernel_c4.md"),
+    ("DFL", "paged_prefill_tc_kernel"): (159589120, 155019264.0, True,
+                                         "profiles/paged_prefill_tc_kernel_d256_draft.md"),
 }
 
 
@@ -525,6 +527,25 @@ def run_ours(args, rank, world, local):
             "avg_launch_ms": round(float(stats[0, 2]), 5), "traffic": None,
             "traffic_source": None,
         }
+        # With no page shared between sequences every K/V byte comes from HBM
+        # once per launch; below the ridge (FLOPs per byte < peak FLOP/s /
+        # peak B/s, e.g. 16-row draft blocks x a GQA group of 8 = 128 FLOP/B)
+        # the launch is bound by HBM, not by the tensor pipe.
+        all_pages = np.concatenate([np.asarray(t) for t in w.block_tables])
+        shared = len(np.unique(all_pages)) < len(all_pages)
+        ridge = tpeak * 1e12 / (peak * 1e9)
+        if not mixed and not shared and per_launch_flops / per_launch_bytes < ridge:
+            line["roofline"] = {
+                "bound": "hbm", "achieved": round(float(stats[0, 3]), 1), "peak": peak,
+                "unit": "GB/s", "frac": round(float(stats[0, 3]) / peak, 4),
+                "peak_kind": peak_kind, "kernel": "paged_prefill_tc_kernel",
+                "algorithmic_bytes_per_launch": float(per_launch_bytes),
+                "flops_per_byte": round(per_launch_flops / per_launch_bytes, 1),
+                "ridge_flops_per_byte": round(ridge, 1),
+                "avg_launch_ms": round(float(stats[0, 2]), 5), "traffic": None,
+                "traffic_source": None,
+            }
+            line["tensor_tflops"] = round(float(stats[0, 5]), 2)
         if mixed:
             # the step's multi-row sequences on the tcgen05 kernel, and its
             # decode rows on the decode kernel, each against its own roof
