@@ -51,8 +51,9 @@ constexpr int kThreads = 256;
 constexpr int kUnroll = 4;  // 16-byte chunks in flight per thread
 
 // ---------------------------------------------------------------------------
-// append: one 16-byte chunk per (row, K|V, chunk) unit. A thread handles up to
-// kUnroll units strided by the grid, issuing all loads before any store.
+// append: one warp per (row, K|V) unit, units strided over the grid's warps.
+// The row's slot is read once; the lanes move the row's 16-byte chunks,
+// kUnroll per lane in flight, all loads before any store.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads) append_kernel(const uint4* __restrict__ k,
                                                           const uint4* __restrict__ v,
@@ -63,36 +64,32 @@ __global__ void __launch_bounds__(kThreads) append_kernel(const uint4* __restric
                                                           int64_t cache_slots) {
   pdl_trigger();
   pdl_wait();  // k, v come from, and the pools are read by, earlier kernels
-  const int64_t per_tensor = static_cast<int64_t>(rows) * chunks_per_row;
-  const int64_t total = per_tensor * 2;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  for (; base < total; base += stride * kUnroll) {
-    uint4 val[kUnroll];
-    uint4* dst[kUnroll];
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x / 32);
+  for (int w = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); w < 2 * rows; w += warps) {
+    const int row = w >> 1;
+    const bool is_v = w & 1;
+    const int64_t slot = __ldg(slots + row);
+    if (slot < 0) continue;  // graph padding rows, as the reference store skips them
+    if (slot >= cache_slots) {
+      if (lane == 0 && !is_v) raise_device_error(&g_device_errors, FE_DEVERR_SLOT_RANGE);
+      continue;
+    }
+    const uint4* src = (is_v ? v : k) + static_cast<int64_t>(row) * chunks_per_row;
+    uint4* dst = (is_v ? vc : kc) + slot * chunks_per_row;
+    for (int c0 = 0; c0 < chunks_per_row; c0 += 32 * kUnroll) {
+      uint4 val[kUnroll];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t i = base + u * stride;
-      dst[u] = nullptr;
-      if (i < total) {
-        const bool is_v = i >= per_tensor;
-        const int64_t j = is_v ? i - per_tensor : i;
-        const int64_t row = j / chunks_per_row;
-        const int64_t col = j - row * chunks_per_row;
-        const int64_t slot = __ldg(slots + row);
-        if (slot >= 0) {
-          if (slot < cache_slots) {
-            val[u] = __ldg((is_v ? v : k) + j);
-            dst[u] = (is_v ? vc : kc) + slot * chunks_per_row + col;
-          } else if (col == 0) {
-            raise_device_error(&g_device_errors, FE_DEVERR_SLOT_RANGE);
-          }
-        }
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < chunks_per_row) val[u] = __ldg(src + c);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < chunks_per_row) dst[c] = val[u];
       }
     }
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u)
-      if (dst[u]) *dst[u] = val[u];
   }
 }
 
@@ -250,8 +247,9 @@ int fe_kv_append(const void* k, const void* v, void* k_pool, void* v_pool, const
   if (!aligned16(k) || !aligned16(v) || !aligned16(k_pool) || !aligned16(v_pool))
     return fail(FE_ERR_INVALID_ARGUMENT, "fe_kv_append: buffers must be 16-byte aligned");
   const int chunks = width / 8;
-  const int64_t units = static_cast<int64_t>(rows) * chunks * 2;
-  int64_t blocks = (units + kThreads * kUnroll - 1) / (kThreads * kUnroll);
+  if (rows > INT32_MAX / 2) return fail(FE_ERR_CAPACITY, "fe_kv_append: too many rows");
+  // one warp per (row, K|V)
+  int64_t blocks = (static_cast<int64_t>(rows) * 2 + kThreads / 32 - 1) / (kThreads / 32);
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;

@@ -14,8 +14,9 @@
 // (C2: 64 rows x 48 heads x 256 B). The fused kernel reads q, k and v once and
 // writes q', the pool rows of k' and v (and optionally k') in one launch, where
 // the reference runs rope (read/write q and k) and then store (read k and v).
-// One thread owns two adjacent pairs (4-byte loads and stores), so a warp
-// covers one 128-dimension head with fully coalesced 128-byte accesses.
+// The usual shapes run rope_vec_kernel (16-byte accesses, eight rotation
+// pairs per thread); others run rope_kernel, where one thread owns two
+// adjacent pairs (4-byte loads and stores).
 #include "fe_common.cuh"
 
 namespace fe {
@@ -131,6 +132,99 @@ __global__ void __launch_bounds__(kRopeThreads)
   vd[i1] = vb[i1];
 }
 
+// 16-byte form of rope_kernel, for rotary_dim a multiple of 16, dim a
+// multiple of 8 and 16-byte aligned buffers (every model shape the path
+// serves): block (x, y) covers units of rows y, y + gridDim.y, ...; a unit is
+// (head, u) with u < rot/16 owning the eight rotation pairs 8u..8u+7 <->
+// r+8u..r+8u+7 (r = rot/2), two 16-byte chunks of the head, or u >= rot/16
+// owning the unrotated 8-element chunk rot + 8(u - rot/16). Same roundings as
+// rope_kernel (the rotate() above), so the same bits; 32-bit indexing.
+template <typename T>
+__global__ void __launch_bounds__(kRopeThreads)
+    rope_vec_kernel(T* __restrict__ q, const T* k, const T* __restrict__ v, T* k_out,
+                    T* __restrict__ kc, T* __restrict__ vc, const int64_t* __restrict__ slots,
+                    const int64_t* __restrict__ pos, const float* __restrict__ cache, int rows,
+                    int hq, int hkv, int dim, int rot, int max_positions, int64_t cache_slots,
+                    unsigned int* err) {
+  using V = typename Pair2<T>::V;
+  union Chunk {
+    uint4 u;
+    V v[4];
+  };
+  pdl_trigger();
+  pdl_wait();  // q, k, v come from, and the pools are read by, earlier kernels
+  const int rot_units = rot / 16;
+  const int per_head = rot_units + (dim - rot) / 8;
+  const int heads = hq + hkv;
+  const int unit = blockIdx.x * blockDim.x + threadIdx.x;
+  if (unit >= heads * per_head) return;
+  const int head = unit / per_head, u = unit - head * per_head;
+  const bool rotating = u < rot_units;
+  const int r = rot / 2;
+  const int e0 = rotating ? 8 * u : rot + 8 * (u - rot_units);  // first element of the chunk
+  const int e1 = e0 + r;                                        // its partner (rotating)
+  for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+    const int64_t p = pos[row];
+    if (p < 0 || p >= max_positions) {
+      if (unit == 0) raise_device_error(err, FE_DEVERR_POS_RANGE);
+      continue;
+    }
+    float2 c[4], sn[4];
+    if (rotating) {
+      const float4* cp = reinterpret_cast<const float4*>(cache + p * rot + 8 * u);
+      const float4* sp = reinterpret_cast<const float4*>(cache + p * rot + r + 8 * u);
+      const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+      c[0] = make_float2(c0.x, c0.y);
+      c[1] = make_float2(c0.z, c0.w);
+      c[2] = make_float2(c1.x, c1.y);
+      c[3] = make_float2(c1.z, c1.w);
+      sn[0] = make_float2(s0.x, s0.y);
+      sn[1] = make_float2(s0.z, s0.w);
+      sn[2] = make_float2(s1.x, s1.y);
+      sn[3] = make_float2(s1.z, s1.w);
+    }
+    if (head < hq) {
+      if (!rotating) continue;  // q's unrotated dims stay as they are
+      T* base = q + (static_cast<int64_t>(row) * hq + head) * dim;
+      Chunk lo, hi;
+      lo.u = *reinterpret_cast<const uint4*>(base + e0);
+      hi.u = *reinterpret_cast<const uint4*>(base + e1);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) rotate<T>(lo.v[i], hi.v[i], c[i], sn[i]);
+      *reinterpret_cast<uint4*>(base + e0) = lo.u;
+      *reinterpret_cast<uint4*>(base + e1) = hi.u;
+      continue;
+    }
+    const int h = head - hq;
+    const int64_t off = (static_cast<int64_t>(row) * hkv + h) * dim;
+    Chunk lo, hi;
+    lo.u = *reinterpret_cast<const uint4*>(k + off + e0);
+    if (rotating) {
+      hi.u = *reinterpret_cast<const uint4*>(k + off + e1);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) rotate<T>(lo.v[i], hi.v[i], c[i], sn[i]);
+    }
+    if (k_out && (rotating || k_out != k)) {
+      *reinterpret_cast<uint4*>(k_out + off + e0) = lo.u;
+      if (rotating) *reinterpret_cast<uint4*>(k_out + off + e1) = hi.u;
+    }
+    if (!kc) continue;
+    const int64_t slot = slots[row];
+    if (slot < 0) continue;
+    if (slot >= cache_slots) {
+      if (u == 0 && h == 0) raise_device_error(err, FE_DEVERR_SLOT_RANGE);
+      continue;
+    }
+    const int64_t dst = (slot * hkv + h) * dim;
+    *reinterpret_cast<uint4*>(kc + dst + e0) = lo.u;
+    *reinterpret_cast<uint4*>(vc + dst + e0) = *reinterpret_cast<const uint4*>(v + off + e0);
+    if (rotating) {
+      *reinterpret_cast<uint4*>(kc + dst + e1) = hi.u;
+      *reinterpret_cast<uint4*>(vc + dst + e1) = *reinterpret_cast<const uint4*>(v + off + e1);
+    }
+  }
+}
+
 // One thread per batch row: accept drafts while they equal the verifier's
 // argmax, then take the verifier's token; out row b (stride k + 2) holds the
 // committed tokens and, at k + 1, their count. Other entries are untouched.
@@ -156,6 +250,23 @@ int launch_rope(void* q, const void* k, const void* v, void* k_out, void* kc, vo
                 const int64_t* slots, const int64_t* pos, const float* cache, int rows, int hq,
                 int hkv, int dim, int rot, int max_positions, int64_t cache_slots,
                 cudaStream_t stream) {
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (rot % 16 == 0 && dim % 8 == 0 && a16(q) && a16(k) && a16(v) && a16(k_out) && a16(kc) &&
+      a16(vc) && a16(cache)) {
+    const int64_t units = static_cast<int64_t>(hq + hkv) * (rot / 16 + (dim - rot) / 8);
+    if (units <= INT32_MAX / 2) {
+      // one row's units over as few blocks as 256 threads allow, evenly sized
+      const int nb = static_cast<int>((units + kRopeThreads - 1) / kRopeThreads);
+      const int bt = static_cast<int>(((units + nb - 1) / nb + 31) / 32 * 32);
+      const dim3 grid(nb, rows < 65535 ? rows : 65535);
+      FE_CUDA_TRY(launch_pdl(rope_vec_kernel<T>, grid, dim3(bt), 0, stream, static_cast<T*>(q),
+                             static_cast<const T*>(k), static_cast<const T*>(v),
+                             static_cast<T*>(k_out), static_cast<T*>(kc), static_cast<T*>(vc),
+                             slots, pos, cache, rows, hq, hkv, dim, rot, max_positions,
+                             cache_slots, device_error_word()));
+      return FE_OK;
+    }
+  }
   const int64_t threads = static_cast<int64_t>(rows) * (hq + hkv) * (dim / 4);
   const int64_t blocks = (threads + kRopeThreads - 1) / kRopeThreads;
   if (blocks > INT32_MAX) return fail(FE_ERR_CAPACITY, "rope: too many rows");

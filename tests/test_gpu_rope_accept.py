@@ -121,6 +121,59 @@ def test_rope_append_equals_reference_rope_then_store(dtype, rows, hq, hkv, in_p
     assert _errors() == 0
 
 
+def _shifted(a, bf, shift):
+    """A device copy of bit array `a` that starts `shift` elements into its
+    allocation (shift 2: 4-byte but not 16-byte aligned)."""
+    import torch
+    flat = to_device(np.concatenate([np.zeros(shift, np.uint16), a.reshape(-1)]), bf)
+    return flat[shift:].view(*a.shape)
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+@pytest.mark.parametrize("rot,shift", [(128, 0), (48, 0), (36, 0), (128, 2), (64, 2)])
+def test_rope_kernel_forms_bit_exact(dtype, rot, shift):
+    """Both kernel forms -- 16-byte (rotary_dim a multiple of 16, 16-byte
+    aligned buffers) and 4-byte (any other rotary_dim that is a multiple of 4,
+    or buffers only 4-byte aligned) -- against the C restatement, for RoPE
+    alone and fused with the append, full and partial rotary."""
+    import fekv
+    import torch
+    rng = np.random.default_rng(rot * 3 + shift + dtype)
+    rows, hq, hkv, max_pos, page, blocks = 45, 16, 4, 2048, 16, 16
+    cache_slots = (blocks + 1) * page
+    bf = dtype == 1
+    cache = rope_cache(max_pos, dim=rot)
+    q = _bits(rng, (rows, hq, DIM), dtype)
+    k = _bits(rng, (rows, hkv, DIM), dtype)
+    v = _bits(rng, (rows, hkv, DIM), dtype)
+    pos = rng.integers(0, max_pos, rows).astype(np.int64)
+    slots = rng.permutation(cache_slots)[:rows].astype(np.int64)
+    slots[::7] = -1
+    posd, cd, sd = _dev(pos), _dev(cache), _dev(slots)
+    qo, ko = oracle.rope(q, k, pos, cache, dtype)
+    # RoPE alone, in place
+    qd, kd = _shifted(q, bf, shift), _shifted(k, bf, shift)
+    fekv.rope(qd, kd, posd, cd)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(to_host_bits(qd), qo)
+    np.testing.assert_array_equal(to_host_bits(kd), ko)
+    # fused with the append, keys also written to k_out
+    pool = _bits(rng, (cache_slots, hkv * DIM), dtype)
+    qd, kd, vd = _shifted(q, bf, shift), _shifted(k, bf, shift), _shifted(v, bf, shift)
+    kcd, vcd = _shifted(pool, bf, shift), _shifted(pool, bf, shift)
+    k_out = _shifted(np.zeros_like(k), bf, shift)
+    fekv.rope_append(qd, kd, vd, kcd, vcd, sd, posd, cd, k_out=k_out)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(to_host_bits(qd), qo)
+    np.testing.assert_array_equal(to_host_bits(k_out), ko)
+    np.testing.assert_array_equal(to_host_bits(kd), k)  # k itself is read only
+    pk, pv = pool.copy(), pool.copy()
+    oracle.append(ko.reshape(rows, -1), v.reshape(rows, -1), pk, pv, slots, cache_slots)
+    np.testing.assert_array_equal(to_host_bits(kcd), pk)
+    np.testing.assert_array_equal(to_host_bits(vcd), pv)
+    assert _errors() == 0
+
+
 def test_rope_append_out_of_range_position_and_slot():
     """Invalid rows are skipped and flagged (the reference would read or write
     out of bounds there, so it is not run on these inputs)."""
