@@ -1,5 +1,5 @@
-"""Draft / hybrid attention through the paged kernels (SURVEY-listed neighbours
-of the hot path), against torch restatements of the reference's dense
+"""Draft / hybrid attention through the paged kernels (the hot path's
+neighbours in the hybrid and draft models), against torch restatements of the reference's dense
 formulations on the GPU:
 
 * DFlash draft block (src/block_draft.cpp:24-30, read_/valid_ built at
@@ -11,7 +11,7 @@ formulations on the GPU:
   (leading rotary dims only), store, attention of one row over its context.
 
 head_dim 128 runs on the decode / tcgen05 kernels; head_dim 256 (Qwen3.5's
-full-attention layers) on the separate wide kernel."""
+full-attention layers) on the same kernels instantiated for 256 dims."""
 import math
 
 import numpy as np
