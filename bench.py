@@ -12,11 +12,11 @@ rank runs its own 64 sequences (weak scaling); NCCL is used only after the
 timed loop to gather per-rank results (no collective on the hot path).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3|c4|c5|q35|draft]
+  python bench.py --impl reference ...   # the reference's own CPU/ATen path
 
 c3 / c4 time the chunked-prefill and verify steps (rows/s, tensor-core
 roofline); q35 and draft are head_dim 256 steps (hybrid-model full-attention
 decode, and 16-row draft blocks under the full mask).
-  python bench.py --impl reference ...   # the reference's own CPU/ATen path
 
 Prints one JSON line (rank 0).
 """
@@ -83,6 +83,20 @@ def ncu_traffic(workload: str, kernel: str, units_per_launch: float):
     if abs(ratio - 1.0) <= 1e-3:
         return dram, f"ncu capture, {src}"
     return None, None
+
+
+def row_step_bound(block_tables, flops: float, nbytes: float, tpeak_tflops: float,
+                   peak_gbs: float) -> str:
+    """Roofline bound of a multi-row attention launch. With no page shared
+    between sequences every K/V byte comes from HBM once per launch; below the
+    ridge (FLOPs per byte < peak FLOP/s / peak B/s, e.g. 16-row draft blocks x
+    a GQA group of 8 = 128 FLOP/B) the launch is bound by HBM, not by the
+    tensor pipe. Shared pages (a common prefix) are served from L2, so such a
+    step stays tensor-bound whatever its per-byte intensity."""
+    all_pages = np.concatenate([np.asarray(t) for t in block_tables])
+    shared = len(np.unique(all_pages)) < len(all_pages)
+    ridge = tpeak_tflops * 1e12 / (peak_gbs * 1e9)
+    return "hbm" if (not shared and flops / nbytes < ridge) else "tensor"
 
 
 def measured_peak_gbs():
@@ -527,14 +541,9 @@ def run_ours(args, rank, world, local):
             "avg_launch_ms": round(float(stats[0, 2]), 5), "traffic": None,
             "traffic_source": None,
         }
-        # With no page shared between sequences every K/V byte comes from HBM
-        # once per launch; below the ridge (FLOPs per byte < peak FLOP/s /
-        # peak B/s, e.g. 16-row draft blocks x a GQA group of 8 = 128 FLOP/B)
-        # the launch is bound by HBM, not by the tensor pipe.
-        all_pages = np.concatenate([np.asarray(t) for t in w.block_tables])
-        shared = len(np.unique(all_pages)) < len(all_pages)
         ridge = tpeak * 1e12 / (peak * 1e9)
-        if not mixed and not shared and per_launch_flops / per_launch_bytes < ridge:
+        if not mixed and row_step_bound(w.block_tables, per_launch_flops, per_launch_bytes,
+                                        tpeak, peak) == "hbm":
             line["roofline"] = {
                 "bound": "hbm", "achieved": round(float(stats[0, 3]), 1), "peak": peak,
                 "unit": "GB/s", "frac": round(float(stats[0, 3]) / peak, 4),
