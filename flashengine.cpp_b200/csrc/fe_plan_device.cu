@@ -170,13 +170,24 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_device_kernel(const DevP
         }
       }
       __syncthreads();
-      // block-table rows -> concatenated pages (one warp per sequence)
+      // block-table rows -> concatenated pages (one warp per sequence; four
+      // independent loads per lane in flight before their stores)
       for (int b = tid >> 5; b < B; b += kPlanWarps) {
         const int st = a.starts[b];
         const int p0 = a.s_kv[b];
         const int n = a.s_kv[b + 1] - p0;
-        for (int i = tid & 31; i < n; i += 32)
-          pages_out[p0 + i] = st < 0 ? a.num_blocks : a.tables[int64_t(b) * a.stride + i];
+        const int32_t* row = a.tables + int64_t(b) * a.stride;
+        for (int i0 = tid & 31; i0 < n; i0 += 128) {
+          int32_t v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int i = i0 + 32 * u;
+            v[u] = i < n ? (st < 0 ? a.num_blocks : __ldg(row + i)) : 0;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (i0 + 32 * u < n) pages_out[p0 + i0 + 32 * u] = v[u];
+        }
       }
       // slot and position of every row (padding rows: slot -1, position j)
       for (int r = tid; r < B * rps; r += kPlanThreads) {
@@ -216,10 +227,20 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_device_kernel(const DevP
     }
     if (__syncthreads_or(bad)) goto fail;
     const int total_pages = B > 0 ? kv[B] : 0;
-    for (int i = tid; i < total_pages; i += kPlanThreads) {
-      const int32_t pid = pages_in[i];
-      if (pid < 0 || pid > a.num_blocks) bad = 1;
-      if (a.mode == 0) pages_out[i] = pid;
+    for (int i0 = tid; i0 < total_pages; i0 += 4 * kPlanThreads) {
+      int32_t pid[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * kPlanThreads;
+        pid[u] = i < total_pages ? pages_in[i] : 0;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * kPlanThreads;
+        if (i >= total_pages) continue;
+        if (pid[u] < 0 || pid[u] > a.num_blocks) bad = 1;
+        if (a.mode == 0) pages_out[i] = pid[u];
+      }
     }
     if (__syncthreads_or(bad)) goto fail;
 
