@@ -68,6 +68,8 @@ NCU_TRAFFIC = {
                                         "profiles/paged_prefill_tc_kernel_c4.md"),
     ("DFL", "paged_prefill_tc_kernel"): (159589120, 155019264.0, True,
                                          "profiles/paged_prefill_tc_kernel_d256_draft.md"),
+    ("Q35", "paged_decode_kernel"): (308690176, 302256128.0, True,
+                                     "profiles/paged_decode_kernel_d256_q35.md"),
 }
 
 
