@@ -355,8 +355,6 @@ int prepare_on_device(fe_attn_plan* p, DevPlanArgs& a, int batch, int rows, void
                       const char* what) {
   if (!p) return fail(FE_ERR_INVALID_ARGUMENT, std::string(what) + ": plan is null");
   if (p->host_only) return fail(FE_ERR_INVALID_ARGUMENT, std::string(what) + ": host-only plan");
-  if (p->cfg.dim != kHeadDim)
-    return fail(FE_ERR_UNSUPPORTED, std::string(what) + ": head_dim 128 plans only");
   if (batch < 0 || rows < 0)
     return fail(FE_ERR_INVALID_ARGUMENT,
                 std::string(what) + ": batch and rows must be non-negative");
@@ -370,6 +368,7 @@ int prepare_on_device(fe_attn_plan* p, DevPlanArgs& a, int batch, int rows, void
   a.rows = rows;
   a.hq = c.hq;
   a.hkv = c.hkv;
+  a.dim = c.dim;
   a.page = c.page;
   a.max_batch = c.max_batch;
   a.max_pages = c.max_pages;

@@ -24,7 +24,8 @@
 //    to end and cut into equal contiguous pieces, one per CTA. Every cut is a
 //    function of prefix sums, so the device list is the host's item for item
 //    (the same split points, hence bit-identical outputs);
-//  - the row lists (prefill / verify units, never split) sort the units by
+//  - the row lists (prefill / verify units, never split: head_dim 256 plans
+//    too, where the host planner may split them) sort the units by
 //    cost, longest first (a bitonic sort in shared memory, up to
 //    kMaxRowUnits units), and deal them to the CTAs in a snake order (0, 1,
 //    ..., n-1, n-1, ..., 0, ...), which needs only each unit's rank instead
@@ -307,7 +308,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_device_kernel(const DevP
         B,
         [&](int b) -> int64_t {
           const int64_t tiles = cdiv(seq_len(b), kTileTokens);
-          const int rec = partial_rec_floats(H * (qo[b + 1] - qo[b]) * G);
+          const int rec = partial_rec_floats(H * (qo[b + 1] - qo[b]) * G, a.dim);
           int64_t s = 0;
           for (int g = 0; g < n_dec(b); ++g) {
             const int64_t pc = pieces(p_tiles[b] + g * tiles, tiles);
@@ -349,7 +350,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_device_kernel(const DevP
         if (nd == 0) continue;
         const int P = (qo[b + 1] - qo[b]) * G;
         const int64_t tiles = cdiv(seq_len(b), kTileTokens);
-        const int rec = partial_rec_floats(H * P);
+        const int rec = partial_rec_floats(H * P, a.dim);
         int idx = c_item[b], gid = c_grp[b];
         int64_t part = p_part[b];
         for (int g = 0; g < nd; ++g) {

@@ -26,7 +26,7 @@ struct DevPlanArgs {
   const int32_t* last;
   int batch, rows;
   // plan configuration and capacities
-  int hq, hkv, page, max_batch, max_pages, num_blocks, dec_heads, grid_cap, dec_grid_cap;
+  int hq, hkv, dim, page, max_batch, max_pages, num_blocks, dec_heads, grid_cap, dec_grid_cap;
   int max_items, max_groups;
   int64_t partial_capacity, meta_cap;
   // outputs: the packed work lists (fe_attn_plan.h layout), split counters

@@ -15,7 +15,7 @@ fe_step_prepare_device) against the host path it replaces.
 import numpy as np
 import pytest
 
-from fe_testutil import to_host_bits
+from fe_testutil import compare_attention, to_host_bits, torch_reference_attention
 
 pytestmark = pytest.mark.gpu
 
@@ -307,3 +307,60 @@ def test_device_prepare_invalid_metadata_empties_plan(fk):
     assert fk.device_errors() == 0
     assert not (out == 7.0).any()
     plan.close()
+
+
+@pytest.mark.parametrize("which", ["q35", "mixed"])
+def test_device_decode_list_equals_host_head_dim_256(fk, which):
+    """head_dim 256 plans: the device-built decode list is the host's item for
+    item (two KV heads per item, split records of rows x 258 floats), so the
+    outputs are the same bits."""
+    import fekv.workloads as wl
+    if which == "q35":
+        w = wl.q35(seed=4)
+    else:
+        w = wl.decode_workload("m256", 16, 2, [9000, 17, 3000, 1, 900, 16, 33], True, 6, dim=256)
+    md = w.metadata()
+    ha, da = _plans(fk, w, md)
+    host = ha.host_meta()
+    dev = da.device_meta(total_pages=int(md.kv[-1]))
+    np.testing.assert_array_equal(dev["seqs"], host["seqs"])
+    _same_list(dev["views"][2], host["views"][2])
+    assert (host["views"][2]["groups"]["nsplit"] > 1).any()
+    _attend_both(fk, w, md, ha, da, True)
+    ha.close()
+    da.close()
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_device_row_lists_head_dim_256(fk, causal):
+    """head_dim 256 draft blocks: the device planner deals whole 128-row items
+    (the host cuts them into pieces across CTAs); both outputs match the fp32
+    restatement of the reference's attention."""
+    import torch
+    import fekv.workloads as wl
+    w = wl.draft(seed=3, batch=6)
+    md = w.metadata()
+    ha, da = _plans(fk, w, md)
+    host = ha.host_meta()
+    dev = da.device_meta(total_pages=int(md.kv[-1]))
+    view = 1 if causal else 0
+    _same_row_list(dev["views"][view], host["views"][view], dev["views"][view]["grid"])
+    assert len(host["views"][view]["groups"]) > 0  # the host split some items
+    g = torch.Generator(device="cuda")
+    g.manual_seed(12)
+    dt = torch.bfloat16
+    kc = torch.randn(w.cache_slots, w.width, generator=g, device="cuda").to(dt)
+    vc = torch.randn(w.cache_slots, w.width, generator=g, device="cuda").to(dt)
+    q = torch.randn(md.rows, w.hq, w.dim, generator=g, device="cuda").to(dt)
+    ref = torch_reference_attention(q, kc, vc, md.qo, md.kv, md.pages, md.last, w.hq, w.hkv,
+                                    w.page, causal)
+    for plan in (ha, da):
+        out = torch.full_like(q, float("nan"))
+        plan.attention(q, kc, vc, out, causal)
+        torch.cuda.synchronize()
+        assert fk.device_errors() == 0
+        res = compare_attention(to_host_bits(out), to_host_bits(ref.to(dt)), True,
+                                ref_f32=ref.cpu().numpy())
+        assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, res
+    ha.close()
+    da.close()

@@ -81,16 +81,6 @@ def test_graph_mode_plan(fk):
     assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, res
 
 
-def test_device_prepare_is_refused_for_head_dim_256(fk):
-    import torch
-    plan = fk.AttentionPlan(16, 2, DIM, PAGE, 2, 8, True, 32)
-    z = torch.zeros(3, dtype=torch.int32, device="cuda")
-    with pytest.raises(fk.FeError) as e:
-        plan.prepare_device(z, z, z, z[:2], 2, 2)
-    assert e.value.status == fk._lib.FE_ERR_UNSUPPORTED
-    plan.close()
-
-
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("bf16", [True, False])
 def test_draft_blocks_split_across_ctas(fk, causal, bf16):
