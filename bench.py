@@ -70,6 +70,8 @@ NCU_TRAFFIC = {
                                          "profiles/paged_prefill_tc_kernel_d256_draft.md"),
     ("Q35", "paged_decode_kernel"): (308690176, 302256128.0, True,
                                      "profiles/paged_decode_kernel_d256_q35.md"),
+    ("C3", "paged_prefill_tc_kernel"): (42910208, 42966450176.0, False,
+                                        "profiles/paged_prefill_tc_kernel_c3.md"),
 }
 
 
