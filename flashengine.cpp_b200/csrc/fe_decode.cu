@@ -669,14 +669,20 @@ int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const 
 // ===========================================================================
 // Allocation-free decode entry point (fe_paged_decode_noalloc, fe_kv.h).
 //
-// For callers that cannot allocate device memory on their path: code running
-// under CUDA stream capture, hosts that hand all of HBM to their own pool
-// allocator (as a KV-cache engine sized by a memory-utilisation fraction
-// does), or latency-critical loops where cudaMalloc may block. The plan-based
-// entry points allocate their work lists and split-K workspace in
-// fe_attn_plan_create; this one needs neither: its work split is computed on
-// the device from the caller's metadata, and its split-K scratch is the
-// file-scope array below.
+// For callers that cannot allocate device memory where they run attention:
+// hosts that hand all of HBM to their own pool allocator at start-up (as a
+// KV-cache engine sized by a memory-utilisation fraction does), so that a
+// later cudaMalloc fails, and hot loops in which an allocation, which may
+// synchronise the device, is not allowed. The plan-based entry points
+// allocate their work lists and split-K workspace in fe_attn_plan_create;
+// this one needs neither: its work split is computed on the device from the
+// caller's metadata, and its split-K scratch is the file-scope array below.
+// head_dim 128 only: q and out are [batch, hq, 128].
+//
+// When batch x KV-head groups is so large that even two split records per
+// unit would not fit the array, every unit runs unsplit (one CTA per unit,
+// no records): the results are the same, long contexts just get less
+// parallelism.
 //
 // The array is fixed at kNoAllocScratchBytes (16 MiB of fp32 split records +
 // 64 KiB of split counters) and exists on every GPU that loads this library
@@ -716,6 +722,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, grp = blockIdx.y, s = blockIdx.x;
+  // the metadata, q, the pools and the split scratch belong to earlier
+  // kernels until here (a no-op when launched without programmatic
+  // serialization, as fe_paged_decode_noalloc launches it)
+  pdl_wait();
   const int p0 = __ldg(kv + b), p1 = __ldg(kv + b + 1), ln = __ldg(last + b);
   if (p1 <= p0 || p1 - p0 > max_pages || ln < 1 || ln > a0.page) {
     if (threadIdx.x == 0 && s == 0 && grp == 0) raise_device_error(a0.err, FE_DEVERR_PAGE_RANGE);
@@ -756,9 +766,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     fence_barrier_init();
   }
   __syncthreads();
-  // q, the pools and the split workspace belong to earlier kernels until here
-  // (a no-op when launched without programmatic serialization)
-  pdl_wait();
 
   if (warp == kDecWarps) {
     if (lane == 0) {
@@ -915,12 +922,12 @@ extern "C" int fe_paged_decode_noalloc(const void* q, const void* k_pool, const 
   const int units = batch * groups;
   const int rec = partial_rec_floats(H * G);
   const size_t unit_bytes = sizeof(float) * size_t(rec);
-  if (size_t(units) * unit_bytes > kNoAllocPartialBytes || units > kNoAllocCounters) {
-    // a single split per unit would still fit; more than this cannot be served
-    if (units > kNoAllocCounters)
-      return fail(FE_ERR_CAPACITY, "fe_paged_decode_noalloc: batch x KV-head groups exceeds " +
-                                       std::to_string(kNoAllocCounters));
-  }
+  // One split counter per unit. When the units' split records would not fit
+  // the scratch even twice over, every unit runs unsplit (nsplit = 1 below),
+  // which needs neither records nor counters.
+  if (units > kNoAllocCounters)
+    return fail(FE_ERR_CAPACITY, "fe_paged_decode_noalloc: batch x KV-head groups exceeds " +
+                                     std::to_string(kNoAllocCounters));
 
   int dev = 0;
   FE_CUDA_TRY(cudaGetDevice(&dev));

@@ -209,15 +209,20 @@ int fe_attn_run_lists(fe_attn_plan* plan, const void* q, const void* k_pool, con
                       void* out, int causal, int lists, void* stream);
 
 /* Decode attention that allocates nothing. No counterpart in the reference:
- * it is for callers that cannot call cudaMalloc on their path (code running
- * under CUDA stream capture, hosts that give all device memory to their own
- * pool allocator, latency-critical loops). Same arithmetic as fe_attn_run
- * for one query row per sequence (row b of q/out belongs to sequence b), but
- * no plan: kv, pages and last are DEVICE int32 arrays laid out as in
- * fe_attn_plan_prepare, and the work split is derived on the device.
+ * it is for callers that cannot call cudaMalloc where they run attention
+ * (hosts that give all free device memory to their own pool allocator at
+ * start-up, so a later allocation fails; hot loops where an allocation,
+ * which may synchronise the device, is not allowed). Same arithmetic as
+ * fe_attn_run for one query row per sequence, but no plan: kv, pages and
+ * last are DEVICE int32 arrays laid out as in fe_attn_plan_prepare, and the
+ * work split is derived on the device.
+ * head_dim 128 only: q and out are [batch, hq, 128], row b of q/out belongs
+ * to sequence b; pools are [cache_slots, hkv, 128].
  * Split-K scratch is a fixed 16 MiB (+64 KiB counters) array inside the
  * library that every GPU loading it holds until exit; batch x KV-head groups
- * beyond 16384 is rejected with FE_ERR_CAPACITY. The first call on a device
+ * beyond 16384 is rejected with FE_ERR_CAPACITY, and batches whose split
+ * records would not fit that array run every sequence unsplit (same
+ * results, less parallelism for long contexts). The first call on a device
  * resolves that array's device address and sets kernel attributes — make it
  * before any stream capture. Calls share the array: sequential calls are
  * safe, calls that overlap on the GPU race. Out-of-range page ids or last

@@ -53,6 +53,20 @@ def compare_attention(out_bits, ref_bits, bf16, rows=None, ref_f32=None):
     return res
 
 
+def ref_aten_attention(q_bits, kpool_bits, vpool_bits, md, hq, hkv, dim, page, causal, bf16,
+                       num_blocks):
+    """The reference's own ATen attention (oracle/_ref, src/portable_gpu_ops.cpp:27-44)
+    on host uint16 arrays; returns its 16-bit output bits [rows, hq, dim]."""
+    max_pages = int((np.asarray(md.kv)[1:] - np.asarray(md.kv)[:-1]).max()) + 1
+    ref = oracle.RefAten(hq, hkv, dim, page, md.batch, max_pages, bf16, num_blocks)
+    try:
+        ref.prepare(md.qo, md.kv, md.pages, md.last)
+        return ref.attention(np.ascontiguousarray(q_bits), np.ascontiguousarray(kpool_bits),
+                             np.ascontiguousarray(vpool_bits), causal)
+    finally:
+        ref.close()
+
+
 def torch_dtype(bf16):
     import torch
     return torch.bfloat16 if bf16 else torch.float16
@@ -70,9 +84,11 @@ def to_host_bits(t) -> np.ndarray:
 
 
 def torch_reference_attention(q, kpool, vpool, qo, kv, pages, last, hq, hkv, page, causal):
-    """fp32 restatement of src/portable_gpu_ops.cpp:39-44 on the GPU, for
-    sizes the CPU oracle cannot finish quickly. q: [rows, hq, d] (cuda);
-    pools [cache_slots, hkv, d] (cuda); metadata numpy. Returns fp32 [rows, hq, d]."""
+    """fp32 restatement of src/portable_gpu_ops.cpp:39-44, for sizes the CPU
+    oracle cannot finish quickly. q: [rows, hq, d]; pools [cache_slots, hkv, d]
+    (all on one device, cuda or cpu); metadata numpy. Returns fp32 [rows, hq, d].
+    Pinned against the reference's fixtures and live library by
+    tests/test_cpu_torch_restatement.py."""
     import torch
     dim = q.shape[-1]
     G = hq // hkv

@@ -102,3 +102,73 @@ def test_plan_create_without_gpu_fails_cleanly():
     with pytest.raises(fekv.FeError) as e:
         fekv.AttentionPlan(8, 2, 128, 16, 4, 4, True, 8)
     assert e.value.status in (_lib.FE_ERR_CUDA, _lib.FE_ERR_NO_DEVICE)
+
+
+REFERENCE_ROOT = os.environ.get("FE_REFERENCE_ROOT",
+                                os.path.join(os.path.dirname(ROOT), "reference"))
+
+
+def _torch_includes():
+    torch = pytest.importorskip("torch")
+    troot = os.path.dirname(torch.__file__)
+    return troot, int(torch._C._GLIBCXX_USE_CXX11_ABI)
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(REFERENCE_ROOT, "src", "cuda_model.cpp")),
+                    reason="reference source tree not present")
+def test_reference_cuda_model_compiles_against_shim_header(tmp_path):
+    """The reference's CUDA DeviceModel (src/cuda_model.cpp), unmodified,
+    type-checks against this library's fe::cuda header. Its own
+    include/fe/native_cuda.hpp is replaced by a stand-in that includes
+    include/fe_native_cuda.hpp and declares the two operators that stay in
+    the reference's src/cuda_kernels.cu (norm and silu_mul, copied from
+    include/fe/native_cuda.hpp:11-12)."""
+    troot, abi = _torch_includes()
+    stand_in = tmp_path / "fe"
+    stand_in.mkdir()
+    (stand_in / "native_cuda.hpp").write_text(
+        "#pragma once\n#include \"fe_native_cuda.hpp\"\nnamespace fe::cuda {\n"
+        "void norm(const void* x,const void* residual,const void* weight,void* output,"
+        "void* new_residual,int rows,int width,float eps,bool bf16,void* stream);\n"
+        "void silu_mul(const void* gu,void* output,int rows,int width,bool bf16,void* stream);\n}\n")
+    # the reference's headers need nlohmann/json; the wheel's cuDNN frontend
+    # carries a copy of it
+    json_dir = os.path.join(os.path.dirname(troot), "include", "cudnn_frontend", "thirdparty")
+    if not os.path.exists(os.path.join(json_dir, "nlohmann", "json.hpp")):
+        pytest.skip("no nlohmann/json.hpp for the reference's headers")
+    cmd = ["g++", "-std=c++20", "-fsyntax-only", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           "-I", str(tmp_path), "-I", os.path.join(ROOT, "include"),
+           "-I", os.path.join(REFERENCE_ROOT, "include"), "-I", json_dir,
+           "-I", os.path.join(troot, "include"),
+           "-I", os.path.join(troot, "include", "torch", "csrc", "api", "include"),
+           "-I", "/usr/local/cuda/include", os.path.join(REFERENCE_ROOT, "src", "cuda_model.cpp")]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-4000:]
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(REFERENCE_ROOT, "include", "fe",
+                                                    "native_cuda.hpp")),
+                    reason="reference source tree not present")
+def test_reference_header_links_against_shim(tmp_path):
+    """A caller compiled against the reference's own include/fe/native_cuda.hpp
+    links against the shim: every operator of this path it declares
+    (create_plan, destroy_plan, prepare_plan, attention, rope, store, accept)
+    resolves to a shim symbol."""
+    src = tmp_path / "caller.cpp"
+    src.write_text(
+        "#include \"fe/native_cuda.hpp\"\n"
+        "int main(int argc, char**){\n"
+        "  if (argc < 100) return 0;\n"
+        "  auto* p = fe::cuda::create_plan(8,2,128,16,1,2,true,4);\n"
+        "  fe::cuda::prepare_plan(p,nullptr,nullptr,nullptr,nullptr,0,0,false,nullptr);\n"
+        "  fe::cuda::attention(p,nullptr,nullptr,nullptr,nullptr,true,nullptr);\n"
+        "  fe::cuda::rope(nullptr,nullptr,nullptr,nullptr,0,0,0,0,true,nullptr,0);\n"
+        "  fe::cuda::store(nullptr,nullptr,nullptr,nullptr,nullptr,0,0,true,nullptr,0);\n"
+        "  fe::cuda::accept(nullptr,nullptr,nullptr,0,0,nullptr);\n"
+        "  fe::cuda::destroy_plan(p);\n  return 1;\n}\n")
+    libdir = os.path.dirname(_lib.SHIM_PATH)
+    cmd = ["g++", "-std=c++17", "-I", os.path.join(REFERENCE_ROOT, "include"), str(src),
+           "-o", str(tmp_path / "caller"), "-L", libdir, "-lfe_native_cuda_b200",
+           "-lfe_kv_b200", f"-Wl,-rpath,{libdir}", "-Wl,--no-undefined"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-4000:]

@@ -8,7 +8,7 @@ import pytest
 
 import cases
 import oracle
-from fe_testutil import (compare_attention, to_device, to_host_bits,
+from fe_testutil import (compare_attention, ref_aten_attention, to_device, to_host_bits,
                          torch_reference_attention)
 
 pytestmark = pytest.mark.gpu
@@ -48,7 +48,7 @@ def run_case(fk, case, inp, md, causal=None, graph=False):
 
 
 @pytest.mark.parametrize("name", [c.name for c in cases.all_cases()])
-def test_attention_matches_reference_fixture(fk, name):
+def test_attention_matches_reference_fixture(fk, parity_record, name):
     case = cases.case_by_name(name)
     fx = dict(np.load(cases.fixture_path(name)))
     inp = case.inputs()
@@ -61,6 +61,7 @@ def test_attention_matches_reference_fixture(fk, name):
     _, ref32 = oracle.attention(inp["q"], ko, vo, md.qo, md.kv, md.pages, md.last, case.hq,
                                 case.hkv, case.dim, case.page, case.causal, case.dtype_code)
     res = compare_attention(out, fx["ref_out"], case.bf16, rows=real, ref_f32=ref32)
+    parity_record(f"fixture {name} (reference ATen output)", res)
     assert res["excess"] <= 0, (res, info)
     assert res["excess_vs_f32"] <= 0, (res, info)
     assert np.isfinite(oracle.to_float(out[real], case.dtype_code)).all()
@@ -103,9 +104,11 @@ def test_attention_random_shapes_vs_oracle(fk, seed):
     assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, (res, info)
 
 
-def _full_size(fk, w, layer_seed=0):
+def _full_size(fk, w, layer_seed=0, ref_aten=False):
     """One layer of a BASELINE config at full size, against the fp32 torch
-    restatement of the ATen algorithm."""
+    restatement of the ATen algorithm (pinned on the CPU by
+    test_cpu_torch_restatement.py) and, with `ref_aten`, against the
+    reference's own ATen path run on the host (oracle/_ref)."""
     import torch
     md = w.metadata()
     g = torch.Generator(device="cuda")
@@ -130,24 +133,57 @@ def _full_size(fk, w, layer_seed=0):
     torch.cuda.synchronize()
     assert fk.device_errors() == 0
     ref16 = ref.to(dt)
-    res = compare_attention(to_host_bits(out), to_host_bits(ref16), w.bf16,
-                            ref_f32=ref.cpu().numpy())
+    out_bits = to_host_bits(out)
+    res = compare_attention(out_bits, to_host_bits(ref16), w.bf16, ref_f32=ref.cpu().numpy())
+    if ref_aten:
+        want = ref_aten_attention(to_host_bits(q), to_host_bits(kc), to_host_bits(vc), md, w.hq,
+                                  w.hkv, w.dim, w.page, w.causal, w.bf16, w.num_blocks)
+        res["vs_reference"] = compare_attention(out_bits, want, w.bf16)
     info = plan.info()
     plan.close()
     return res, info
 
 
-def test_c2_layer_full_size(fk):
+def test_c2_layer_full_size(fk, parity_record):
     import fekv.workloads as wl
     res, info = _full_size(fk, wl.c2(seed=0))
+    parity_record("C2 layer (64 seqs, torch fp32 restatement)", res)
     assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, (res, info)
     assert res["n_over_2e-3"] == 0, res  # |o| is small at this scale: the flat bar holds
 
 
-def test_c3_layer_full_size(fk):
+def test_c3_layer_full_size(fk, parity_record):
     import fekv.workloads as wl
     res, info = _full_size(fk, wl.c3(seed=0))
+    parity_record("C3 layer (4 prefill chunks + 60 decode rows)", res)
     assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, (res, info)
+
+
+def test_c5_long_contexts_vs_reference(fk, parity_record):
+    """BASELINE config 5's attention shape (hq64/hkv8, bf16, x0.5) over
+    contexts from 2,048 to exactly 32,768 keys (the config's clip range),
+    eight sequences over 148 CTAs so every sequence is split-K; checked
+    against the reference's own ATen path on the host and the fp32
+    restatement."""
+    import fekv.workloads as wl
+    cached = [2047, 32767, 8191, 5000, 12000, 2048, 20000, 9273]
+    w = wl.decode_workload("C5", 64, 8, cached, True, 55, steps=1, scale=0.5, layers=1)
+    res, info = _full_size(fk, w, layer_seed=5, ref_aten=True)
+    parity_record("C5 shape, 8 seqs, contexts 2,048-32,768 (reference ATen path)", res)
+    assert info["split_sequences"] == len(cached), info
+    assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, (res, info)
+    assert res["vs_reference"]["excess"] <= 0, res
+    assert res["n_over_2e-3"] == 0 and res["vs_reference"]["n_over_2e-3"] == 0, res
+
+
+def test_c5_layer_full_size(fk, parity_record):
+    """One layer of a full C5 shard: 128 sequences, log-normal contexts."""
+    import fekv.workloads as wl
+    w = wl.c5(rank=0, world=1, steps=1)
+    res, info = _full_size(fk, w, layer_seed=6)
+    parity_record("C5 layer (128 seqs, torch fp32 restatement)", res)
+    assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, (res, info)
+    assert res["n_over_2e-3"] == 0, res
 
 
 def test_run_lists_parts_equal_one_call(fk):
@@ -174,9 +210,10 @@ def test_run_lists_parts_equal_one_call(fk):
     assert torch.equal(one.view(torch.int16), parts.view(torch.int16))
 
 
-def test_c4_layer_full_size(fk):
+def test_c4_layer_full_size(fk, parity_record):
     import fekv.workloads as wl
     res, info = _full_size(fk, wl.c4(seed=0))
+    parity_record("C4 layer (128 verify blocks, full mask, CoW tails)", res)
     assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, (res, info)
 
 

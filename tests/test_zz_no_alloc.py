@@ -1,14 +1,15 @@
 """fe_paged_decode_noalloc — the decode entry point that allocates nothing.
 
-Some callers cannot make a device allocation where they call attention: a
-model step being recorded under CUDA stream capture, an engine that handed all
-free HBM to its own KV-page pool at start-up, or a latency-critical loop. This
-entry point takes the step metadata as device arrays and keeps its split-K
-scratch in a fixed array inside the library, so it needs no plan and no
-cudaMalloc. These tests check, through the C ABI, that two calls in a row give
-the same results as the plan-based fe_attn_run within the attention tolerance
-used by every parity test here, and that device memory does not move while it
-runs.
+Some callers cannot make a device allocation where they call attention: an
+engine that handed all free HBM to its own KV-page pool at start-up (a later
+cudaMalloc fails), or a hot loop in which an allocation, which may
+synchronise the device, is not allowed. This entry point takes the step
+metadata as device arrays and keeps its split-K scratch in a fixed array
+inside the library, so it needs no plan and no cudaMalloc. These tests check,
+through the C ABI, that two calls in a row give the same results as the
+plan-based fe_attn_run within the attention tolerance used by every parity
+test here, that small cases also match the CPU oracle, and that device memory
+does not move while it runs.
 
 This file is collected last on purpose (name order).
 """
@@ -30,7 +31,7 @@ def fk():
     return fekv
 
 
-def _run_pair(fk, hq, hkv, ctx, bf16, seed):
+def _run_pair(fk, hq, hkv, ctx, bf16, seed, with_oracle=False):
     import torch
     from fekv import workloads
     w = workloads.decode_workload("noalloc", hq, hkv, ctx, bf16, seed, steps=1)
@@ -67,20 +68,51 @@ def _run_pair(fk, hq, hkv, ctx, bf16, seed):
     assert free_after == free_before, "device memory changed during allocation-free calls"
     assert fk.device_errors() == 0
     plan.close()
-    return [to_host_bits(o) for o in outs_plan], [to_host_bits(o) for o in outs_static]
+    plan_bits = [to_host_bits(o) for o in outs_plan]
+    static_bits = [to_host_bits(o) for o in outs_static]
+    if with_oracle:
+        kb, vb = to_host_bits(kc), to_host_bits(vc)
+        for q, got in zip(qs, static_bits):
+            want, want32 = oracle.attention(to_host_bits(q), kb, vb, md.qo, md.kv, md.pages,
+                                            md.last, hq, hkv, 128, w.page, True, 1 if bf16 else 0)
+            res = compare_attention(got, want, bf16, ref_f32=want32)
+            assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, res
+    return plan_bits, static_bits
 
 
 @pytest.mark.parametrize("hq,hkv,ctx,bf16", [
     (32, 8, [600, 3000, 4096, 17, 1, 2200, 900, 3500] * 3, True),   # C2 shape, split-K
     (16, 8, [17, 128, 511, 1000], False),                            # C1 shape, fp16
     (32, 4, [2049, 2304, 40, 700], True),                            # 4 heads per item
+    (32, 2, [5000, 12, 1700, 300, 2600], True),                      # G = 16: 2-row-block items
+    (16, 1, [3100, 1, 800, 2222], False),                            # H = 1, G = 16
+    (8, 2, [1025, 64, 4000], True),                                  # H = 2, G = 4
 ])
 def test_noalloc_matches_plan_path(fk, hq, hkv, ctx, bf16):
-    plan_outs, static_outs = _run_pair(fk, hq, hkv, ctx, bf16, seed=hq + hkv + len(ctx))
+    small = sum(ctx) <= 6000
+    plan_outs, static_outs = _run_pair(fk, hq, hkv, ctx, bf16, seed=hq + hkv + len(ctx),
+                                       with_oracle=small)
     for call, (want, got) in enumerate(zip(plan_outs, static_outs)):
         res = compare_attention(got, want, bf16)
         assert res["excess"] <= 0, (call, res)
         assert np.isfinite(oracle.to_float(got, 1 if bf16 else 0)).all()
+
+
+@pytest.mark.parametrize("hq,batch", [(32, 4096), (128, 200)])
+def test_noalloc_large_batch_runs_unsplit(fk, hq, batch):
+    """Batches whose split-K records cannot share the fixed scratch run every
+    sequence unsplit: 4096 sequences (more head groups than twice the SMs, so
+    no split is wanted) and 200 sequences of 128-row head groups (hq128 /
+    hkv8), whose two-way split would need 26.6 MB of records, more than the
+    16 MiB scratch. The results still equal the plan path's."""
+    rng = np.random.default_rng(11 + hq)
+    hi = 300 if batch > 1000 else 2000
+    ctx = [int(c) for c in rng.integers(1, hi, size=batch)]
+    ctx[7] = 2500  # one long context, which the plan path splits
+    plan_outs, static_outs = _run_pair(fk, hq, 8, ctx, True, seed=12)
+    for call, (want, got) in enumerate(zip(plan_outs, static_outs)):
+        res = compare_attention(got, want, True)
+        assert res["excess"] <= 0, (call, res)
 
 
 def test_noalloc_rejects_oversized_batch(fk):
