@@ -6,17 +6,27 @@ workload: build the step's slot mapping and page tables on the host (the
 reference's CudaModel::prepare), prepare the attention plan (one H2D copy),
 then per layer append one K/V row per sequence and run paged decode attention.
 
-Default workload: C2 (Qwen3-8B attention shape: hq32/hkv8/d128 bf16, 36
-layers, 64 sequences, contexts U[512,4096], page 16). Under torchrun every
-rank runs its own 64 sequences (weak scaling); NCCL is used only after the
-timed loop to gather per-rank results (no collective on the hot path).
+Headline workload: C2 (Qwen3-8B attention shape: hq32/hkv8/d128 bf16, 36
+layers, 64 sequences per GPU, contexts U[512,4096], page 16). Under torchrun
+every rank runs one of 8 shards of one seeded list of 512 sequences, split so
+that every shard holds the same KV bytes to within 0.1% (weak scaling). NCCL
+is used only after the timed loops: to gather per-rank stats, per-rank output
+checksums, and one sampled sequence per rank (its K/V, query and output),
+which rank 0 recomputes in fp32 (`results`). No collective runs on the hot
+path.
+
+The same JSON line carries sub-objects measured in the same process:
+  c5   BASELINE config 5 (hq64/hkv8, 64 layers, 128 sequences per GPU from
+       1024 log-normal contexts 2k-32k, split-K decode + append, 32 steps),
+       at every N, with its own roofline, e2e and results check;
+  c3   chunked prefill + decode rows (tcgen05 kernel roofline), N=1 only;
+  c4   shared-prefix verify blocks + copy-on-write (tcgen05), N=1 only;
+  ops  append / block copy / fused RoPE+append / accept / merge-free
+       preparation timings against the HBM roofline, N=1 only.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3|c4|c5|q35|draft]
+                  [--sub c5,c3,c4,ops|none] [--layers L]
   python bench.py --impl reference ...   # the reference's own CPU/ATen path
-
-c3 / c4 time the chunked-prefill and verify steps (rows/s, tensor-core
-roofline); q35 and draft are head_dim 256 steps (hybrid-model full-attention
-decode, and 16-row draft blocks under the full mask).
 
 Prints one JSON line (rank 0).
 """
@@ -29,6 +39,7 @@ import statistics
 import subprocess
 import sys
 import tempfile
+import threading
 import time
 
 import numpy as np
@@ -40,16 +51,25 @@ for _p in (ROOT, os.path.join(ROOT, "flashengine.cpp_b200")):
 
 METRIC = "paged decode-attn achieved TB/s (% HBM peak); decode tokens/s at 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_TFLOPS_SUSTAINED = 1400.0
+C5_STEPS = 32  # split-K decode + append for 32 steps
+
+
+def measured_peak_gbs():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
 
 
 def measured_peak_tflops():
     """Sustained bf16 dense peak (a kernel timed inside a long step)."""
-    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
-        with open(path) as f:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             return float(json.load(f)["bf16_tflops_sustained"]), "measured (sustained)"
     except Exception:
-        return 1400.0, "fallback (sustained)"
+        return FALLBACK_TFLOPS_SUSTAINED, "fallback (sustained)"
 
 
 # DRAM bytes (read + write) per launch of each roofline kernel, from one
@@ -103,86 +123,134 @@ def row_step_bound(block_tables, flops: float, nbytes: float, tpeak_tflops: floa
     return "hbm" if (not shared and flops / nbytes < ridge) else "tensor"
 
 
-def measured_peak_gbs():
-    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    try:
-        with open(path) as f:
-            return float(json.load(f)["hbm_gbs"]), "measured"
-    except Exception:
-        return FALLBACK_HBM_GBS, "fallback"
-
-
 # ---------------------------------------------------------------------------
-# clocks sampled during the timed region
+# clocks sampled during a timed region
 # ---------------------------------------------------------------------------
+
+# NVML clock-event reason bits (nvml.h: nvmlClocksEventReason*)
+_REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                "hw_thermal_slowdown": 0x40}
+
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock, power and clock-event reasons of this rank's GPU, read every
+    `period_ms` from a host thread through NVML while a timed region runs (a
+    few-ms period gives a usable sample count even for a region of a tenth of
+    a second). Falls back to `nvidia-smi -lms 200` when NVML is unavailable.
+    Only reads the GPU's state; changes nothing."""
 
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, period_ms: float = 5.0):
         self.dev = device_index
-        self.proc = None
-        self.path = None
+        self.period = period_ms / 1e3
+        self.samples = []
+        self._stop = threading.Event()
+        self._thread = None
+        self._proc = None
+        self._path = None
+        self.source = None
+
+    def _nvml_handle(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        try:
+            import torch
+
+            uuid = str(torch.cuda.get_device_properties(self.dev).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(
+                uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.dev)
 
     def start(self):
-        fd, self.path = tempfile.mkstemp(prefix="fe_clocks_", suffix=".csv")
+        try:
+            nv, h = self._nvml_handle()
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.source = f"nvml every {self.period * 1e3:.0f} ms"
+
+            def loop():
+                while not self._stop.is_set():
+                    try:
+                        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                        pw = nv.nvmlDeviceGetPowerUsage(h) / 1e3
+                        rs = reasons_fn(h)
+                        self.samples.append((float(sm), float(mx), pw, int(rs)))
+                    except Exception:
+                        pass
+                    time.sleep(self.period)
+
+            self._thread = threading.Thread(target=loop, daemon=True)
+            self._thread.start()
+            return
+        except Exception:
+            pass
+        fields = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        fd, self._path = tempfile.mkstemp(prefix="fe_clocks_", suffix=".csv")
         os.close(fd)
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={fields}", "--format=csv,noheader,nounits",
                  "-lms", "200", "-i", str(self.dev)],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                stdout=open(self._path, "w"), stderr=subprocess.DEVNULL)
+            self.source = "nvidia-smi every 200 ms"
         except Exception:
-            self.proc = None
+            self._proc = None
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        sm, mx, reasons, power = [], [], set(), []
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9:
-                    continue
-                try:
-                    sm.append(float(parts[1]))
-                    mx.append(float(parts[2]))
-                    power.append(float(parts[3]))
-                except ValueError:
-                    continue
-                for name, val in zip(names, parts[5:9]):
-                    if val.lower() == "active":
-                        reasons.add(name)
-        os.unlink(self.path)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None,
-                "power_w_max": max(power) if power else None,
-                "samples": len(sm), "reasons": sorted(reasons)}
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(2)
+        elif self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except Exception:
+                self._proc.kill()
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            with open(self._path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) < 7:
+                        continue
+                    try:
+                        bits = sum(_REASON_BITS[n] for n, v in zip(names, parts[3:7])
+                                   if v.lower() == "active")
+                        self.samples.append((float(parts[0]), float(parts[1]),
+                                             float(parts[2]), bits))
+                    except ValueError:
+                        continue
+            os.unlink(self._path)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "samples": 0,
+                    "reasons": ["no clock source"]}
+        sm = [s[0] for s in self.samples]
+        reasons = sorted(n for n, bit in _REASON_BITS.items()
+                         if any(s[3] & bit for s in self.samples))
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(s[1] for s in self.samples),
+                "sm_mhz_min": min(sm), "power_w_max": round(max(s[2] for s in self.samples), 1),
+                "samples": len(sm), "source": self.source, "reasons": reasons}
 
 
 # ---------------------------------------------------------------------------
 # distributed plumbing (one process per GPU; no collective on the hot path)
 # ---------------------------------------------------------------------------
 
-def dist_setup(n_gpus: int):
+def dist_setup():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+
+    torch.cuda.set_device(local)
     if world > 1:
         import datetime
 
-        import torch
         import torch.distributed as dist
 
-        torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     return rank, world, local
@@ -195,22 +263,22 @@ def barrier(world):
         dist.barrier()
 
 
-def gather_floats(values, world):
+def gather_floats(values, world, device="cuda"):
     """All-gather a small float64 vector per rank (after timing only)."""
     from fekv.dist import gather_floats as _gather
 
-    return _gather(values, world, device="cuda")
+    return _gather(values, world, device=device)
 
 
 # ---------------------------------------------------------------------------
-# workload
+# workloads
 # ---------------------------------------------------------------------------
 
 def make_workload(config, rank, world, total_steps):
     from fekv import workloads
 
     if config == "c2":
-        return workloads.c2(seed=1000 + rank, steps=total_steps)
+        return workloads.c2_shard(shard=rank, nshards=max(world, 8), steps=total_steps)
     if config == "c5":
         return workloads.c5(rank=rank, world=world, steps=total_steps)
     if config == "c3":
@@ -250,340 +318,748 @@ def decode_rows_mask(w, md):
     return q * (w.hq // w.hkv) <= 16
 
 
-class DecodeState:
-    """Device-resident pools and per-layer step inputs for one GPU."""
+def physical_pools(w, pool_gb, free_bytes=None):
+    """Layer pools held on the GPU: all layers when they fit in the budget,
+    else fewer, reused round-robin (layer l uses pool l mod P); each pool is
+    far larger than L2, so reuse adds no cache effect."""
+    per_layer = 2 * w.cache_slots * w.width * 2
+    budget = pool_gb * 1e9 if free_bytes is None else min(free_bytes * 0.85, pool_gb * 1e9)
+    return int(min(w.layers, max(1, budget // per_layer)))
 
-    def __init__(self, w, physical_layers, seed, rows):
+
+def config_dict(w, world, physical):
+    """The workload description both arms print (same dict, same config)."""
+    return {
+        "workload": f"{w.name}: hq{w.hq}/hkv{w.hkv}/d{w.dim} page{w.page}, {w.layers} layers, "
+                    f"{w.batch} seqs/GPU, "
+                    + ("1 appended token + decode attention per layer-step" if int(w.rows.max()) == 1
+                       else f"{int(w.rows.sum())} query rows per layer-step, "
+                            f"{'causal' if w.causal else 'non-causal'}"
+                            + (", copy-on-write of shared tail pages each step"
+                               if w.cow is not None else "")),
+        "seqs_per_gpu": w.batch, "layers": w.layers, "physical_layer_pools": physical,
+        "mean_context": round(float(np.mean(w.cached)), 2),
+        "shard": w.notes.get("shard"),
+        "l2": "inputs larger than L2 (each layer's KV pages exceed 126 MB)",
+        "parallelism": f"sequence-sharded x{world}, no hot-path collective",
+    }
+
+
+def dense_attention_f32(q, k, v, hq, hkv, causal):
+    """fp32 softmax attention of one sequence (result check after timing):
+    q [rows, hq, d], k/v [length, hkv, d] -> [rows, hq, d]; causal rows are
+    bottom-right aligned as in src/portable_gpu_ops.cpp:31."""
+    import torch
+
+    rows, _, d = q.shape
+    length = k.shape[0]
+    G = hq // hkv
+    kk = k.float().repeat_interleave(G, dim=1).permute(1, 2, 0)
+    vv = v.float().repeat_interleave(G, dim=1).permute(1, 0, 2)
+    logits = torch.bmm(q.float().permute(1, 0, 2), kk) / float(np.sqrt(d))
+    if causal:
+        t = torch.arange(length, device=q.device)
+        r = torch.arange(rows, device=q.device).unsqueeze(1)
+        logits = logits.masked_fill(~(t.unsqueeze(0) <= length - rows + r).unsqueeze(0),
+                                    float("-inf"))
+    return torch.bmm(torch.softmax(logits, -1), vv).permute(1, 0, 2)
+
+
+def check_sample(q, k, v, out, hq, hkv, causal):
+    """(ok, max_abs_err) of `out` against the fp32 recomputation: within 2e-3
+    plus one output ulp, the parity tests' bar."""
+    import torch
+
+    ref = dense_attention_f32(q, k, v, hq, hkv, causal)
+    ref16 = ref.to(out.dtype).float()
+    mant = 7 if out.dtype == torch.bfloat16 else 10
+    ulp = torch.exp2(torch.floor(torch.log2(ref16.abs().clamp_min(2.0 ** -126))) - mant)
+    err = (out.float() - ref16).abs()
+    return bool((err <= 2e-3 + ulp).all().item()), float(err.max().item())
+
+
+# ---------------------------------------------------------------------------
+# one GPU's share of a workload
+# ---------------------------------------------------------------------------
+
+class Runner:
+    """Device-resident pools, per-layer step inputs and the attention plan of
+    one rank. step(): host slot mapping + plan prepare, then per layer the
+    append and the attention (and, for C4, the copy-on-write of the forked
+    sequences' shared tail pages once per step)."""
+
+    def __init__(self, config, rank, world, steps, warmup, e2e_steps, pool_gb, layers=0):
         import torch
 
+        import fekv
+
+        self.config, self.rank, self.world = config, rank, world
+        self.steps, self.warmup, self.e2e_steps = steps, warmup, e2e_steps
+        self.total_steps = warmup + steps + e2e_steps + 1
+        w = make_workload(config, rank, world, self.total_steps)
+        if layers:
+            w.layers = layers
         self.w = w
+        free, _ = torch.cuda.mem_get_info()
+        self.physical = physical_pools(w, pool_gb, free)
+        self.decode = is_decode(config)
         dt = torch.bfloat16 if w.bf16 else torch.float16
         self.dt = dt
         g = torch.Generator(device="cuda")
-        g.manual_seed(seed)
+        g.manual_seed(7 + rank)
         self.kpools, self.vpools = [], []
-        for _ in range(physical_layers):
+        for _ in range(self.physical):
             for lst in (self.kpools, self.vpools):
                 t = torch.empty(w.cache_slots, w.width, dtype=dt, device="cuda")
                 t.normal_(0.0, w.scale, generator=g)
                 lst.append(t)
-        L = w.layers
+        self.rows = w.metadata(0).rows
+        L, rows = w.layers, self.rows
         self.q = torch.randn(L, rows, w.hq, w.dim, generator=g, device="cuda", dtype=dt) * w.scale
         self.knew = torch.randn(L, rows, w.width, generator=g, device="cuda", dtype=dt) * w.scale
         self.vnew = torch.randn(L, rows, w.width, generator=g, device="cuda", dtype=dt) * w.scale
         self.out = torch.empty_like(self.q)
         self.slots = torch.empty(rows, dtype=torch.int64, device="cuda")
-        self.physical = physical_layers
+        self.plan = fekv.AttentionPlan(w.hq, w.hkv, w.dim, w.page, w.batch,
+                                       w.max_pages(self.total_steps), w.bf16, w.num_blocks)
+        self.stream = torch.cuda.current_stream()
+        self.cow = None
+        if w.cow is not None:
+            self.cow = tuple(torch.from_numpy(np.asarray(x, np.int32)).cuda() for x in w.cow)
+        md0 = w.metadata(0)
+        dm = decode_rows_mask(w, md0)
+        # a step with both decode rows and multi-row sequences is timed in two
+        # parts (decode kernel + merge, then the tcgen05 kernel): the same
+        # kernels in the same order as one fe_attn_run, with an event between
+        self.mixed = (not self.decode) and bool(dm.any()) and bool((~dm).any())
+        self.sample_layer = w.layers // 2
+        self.attn_ev = []
+        self.last_md = None
 
+    def step(self, s, record=False, host_io=None):
+        import torch
 
-def run_ours(args, rank, world, local):
-    import torch
+        import fekv
 
-    import fekv
-    from fekv.dist import job_rate
-
-    fekv.load()
-    peak, peak_kind = measured_peak_gbs()
-    total_steps = args.warmup + args.steps + args.e2e_steps + 1
-    w = make_workload(args.config, rank, world, total_steps)
-    if args.layers:
-        w.layers = args.layers
-    # physical layer pools: all layers when they fit, else pools are reused
-    per_layer = 2 * w.cache_slots * w.width * 2
-    free, _ = torch.cuda.mem_get_info()
-    budget = min(free * 0.85, args.pool_gb * 1e9)
-    physical = int(min(w.layers, max(1, budget // per_layer)))
-    rows = w.metadata(0).rows
-    st = DecodeState(w, physical, seed=7 + rank, rows=rows)
-    plan = fekv.AttentionPlan(w.hq, w.hkv, w.dim, w.page, w.batch, w.max_pages(total_steps),
-                              w.bf16, w.num_blocks)
-    stream = torch.cuda.current_stream()
-    decode = is_decode(args.config)
-    cow = None
-    if w.cow is not None:
-        cow = tuple(torch.from_numpy(np.asarray(x, np.int32)).cuda() for x in w.cow)
-
-    attn_ev = []
-    md0 = w.metadata(0)
-    dmask0 = decode_rows_mask(w, md0)
-    # a step with both decode rows and multi-row sequences is timed in two
-    # parts (decode kernel + merge, then the tcgen05 kernel): the same kernels
-    # in the same order as one fe_attn_run, with an event between them
-    mixed = (not is_decode(args.config)) and bool(dmask0.any()) and bool((~dmask0).any())
-    sample_layer = w.layers // 2
-
-    def step(s, record=False, host_io=None):
-        md = w.metadata(s if decode else 0)
+        w = self.w
+        md = w.metadata(s if self.decode else 0)
         if host_io is not None:
             host_io["h2d"]()
-        plan.prepare(md.qo, md.kv, md.pages, md.last, md.batch, md.rows, False, stream)
-        st.slots.copy_(torch.from_numpy(md.slots).pin_memory(), non_blocking=True)
-        if cow is not None:
+        self.plan.prepare(md.qo, md.kv, md.pages, md.last, md.batch, md.rows, False, self.stream)
+        # a fresh pinned buffer per step: the host runs steps ahead of the GPU
+        # (torch's pinned allocator keeps it until the copy has run)
+        self.slots.copy_(torch.from_numpy(md.slots).pin_memory(), non_blocking=True)
+        if self.cow is not None:
             # copy-on-write of the forked sequences' shared partial tail pages,
             # every layer in one launch (idempotent, so it can repeat per step)
-            for l0 in range(0, st.physical, fekv._lib.FE_MAX_LAYERS):
-                l1 = min(st.physical, l0 + fekv._lib.FE_MAX_LAYERS)
-                fekv.copy_blocks(st.kpools[l0:l1], st.vpools[l0:l1], cow[0], cow[1], cow[2],
-                                 w.page, w.width, w.num_blocks + 1, None, stream)
+            for l0 in range(0, self.physical, fekv._lib.FE_MAX_LAYERS):
+                l1 = min(self.physical, l0 + fekv._lib.FE_MAX_LAYERS)
+                fekv.copy_blocks(self.kpools[l0:l1], self.vpools[l0:l1], *self.cow, w.page,
+                                 w.width, w.num_blocks + 1, None, self.stream)
         for layer in range(w.layers):
-            p = layer % st.physical
+            p = layer % self.physical
             # kernel durations for the roofline come from events around one
             # sampled layer per step: an event between two kernels ends their
             # programmatic overlap, so the other layers run without them
-            timed = record and layer == sample_layer
+            timed = record and layer == self.sample_layer
             if host_io is not None:
                 host_io["before"](layer)
-            fekv.store(st.knew[layer], st.vnew[layer], st.kpools[p], st.vpools[p], st.slots,
-                       md.rows, w.width, w.bf16, stream, w.cache_slots)
+            fekv.store(self.knew[layer], self.vnew[layer], self.kpools[p], self.vpools[p],
+                       self.slots, md.rows, w.width, w.bf16, self.stream, w.cache_slots)
             if timed:
                 e0 = torch.cuda.Event(enable_timing=True)
-                em = torch.cuda.Event(enable_timing=True) if mixed else None
+                em = torch.cuda.Event(enable_timing=True) if self.mixed else None
                 e1 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-            if timed and mixed:
-                plan.attention(st.q[layer], st.kpools[p], st.vpools[p], st.out[layer], w.causal,
-                               stream, lists=fekv._lib.FE_ATTN_LISTS_DECODE)
-                em.record(stream)
-                plan.attention(st.q[layer], st.kpools[p], st.vpools[p], st.out[layer], w.causal,
-                               stream, lists=fekv._lib.FE_ATTN_LISTS_ROWS)
+                e0.record(self.stream)
+            if timed and self.mixed:
+                self.plan.attention(self.q[layer], self.kpools[p], self.vpools[p], self.out[layer],
+                                    w.causal, self.stream, lists=fekv._lib.FE_ATTN_LISTS_DECODE)
+                em.record(self.stream)
+                self.plan.attention(self.q[layer], self.kpools[p], self.vpools[p], self.out[layer],
+                                    w.causal, self.stream, lists=fekv._lib.FE_ATTN_LISTS_ROWS)
             else:
-                plan.attention(st.q[layer], st.kpools[p], st.vpools[p], st.out[layer], w.causal,
-                               stream)
+                self.plan.attention(self.q[layer], self.kpools[p], self.vpools[p], self.out[layer],
+                                    w.causal, self.stream)
             if timed:
-                e1.record(stream)
-                attn_ev.append((e0, em, e1))
+                e1.record(self.stream)
+                self.attn_ev.append((e0, em, e1))
             if host_io is not None:
                 host_io["after"](layer)
+        self.last_md = md
         return md
 
-    # warm-up
-    for s in range(args.warmup):
-        step(s)
-    torch.cuda.synchronize()
-    barrier(world)
+    def run_device(self, clock_dev):
+        """W untimed steps, then K timed steps between CUDA events on the
+        launching stream, bracketed by barrier + synchronize; NVML clocks
+        sampled throughout the timed region."""
+        import torch
 
-    # timed region (device-resident inputs)
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
-    barrier(world)
-    torch.cuda.synchronize()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    keys = 0
-    flops = 0.0
-    rows_flops = 0.0
-    dec_keys = 0
-    dec_qrows = 0
-    t0.record(stream)
-    for i in range(args.steps):
-        md = step(args.warmup + i, record=True)
+        w = self.w
+        for s in range(self.warmup):
+            self.step(s)
+        torch.cuda.synchronize()
+        barrier(self.world)
+        clocks = ClockSampler(clock_dev)
+        clocks.start()
+        time.sleep(0.05)
+        barrier(self.world)
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        keys = flops = rows_flops = 0.0
+        dec_keys = dec_qrows = 0
+        t0.record(self.stream)
+        for i in range(self.steps):
+            md = self.step(self.warmup + i, record=True)
+            lengths = md.lengths(w.page)
+            keys += int(lengths.sum())
+            flops += attention_flops(w, md)
+            dm = decode_rows_mask(w, md)
+            rows_flops += attention_flops(w, md, ~dm)
+            dec_keys += int(lengths[dm].sum())
+            dec_qrows += int((md.qo[1:] - md.qo[:-1])[dm].sum())
+        t1.record(self.stream)
+        torch.cuda.synchronize()
+        clk = clocks.stop()
+        barrier(self.world)
+        ms = t0.elapsed_time(t1)
+        K = self.steps
+        attn_ms = [a.elapsed_time(b) for a, _, b in self.attn_ev]
+        attn_avg_ms = float(np.mean(attn_ms))
+        per_launch_bytes = (keys / K) * 2 * w.width * 2 + 2 * self.rows * w.hq * w.dim * 2
+        per_launch_flops = flops / K
+        st = {"ms": ms, "attn_avg_ms": attn_avg_ms, "kv_bytes_per_launch": per_launch_bytes,
+              "flops_per_launch": per_launch_flops,
+              "gbs": per_launch_bytes / (attn_avg_ms * 1e-3) / 1e9,
+              "tflops": per_launch_flops / (attn_avg_ms * 1e-3) / 1e12,
+              "step_gbs": per_launch_bytes * w.layers * K / (ms * 1e-3) / 1e9,
+              "rows_ms": 0.0, "rows_tflops": 0.0, "dec_ms": 0.0, "dec_gbs": 0.0,
+              "rows_flops_per_launch": rows_flops / K, "dec_bytes_per_launch": 0.0}
+        if self.mixed:
+            rows_ms = float(np.mean([m.elapsed_time(b) for _, m, b in self.attn_ev]))
+            dec_ms = float(np.mean([a.elapsed_time(m) for a, m, _ in self.attn_ev]))
+            dec_bytes = (dec_keys / K) * 2 * w.width * 2 + 2 * (dec_qrows / K) * w.hq * w.dim * 2
+            st.update({"rows_ms": rows_ms, "rows_tflops": (rows_flops / K) / (rows_ms * 1e-3) / 1e12,
+                       "dec_ms": dec_ms, "dec_gbs": dec_bytes / (dec_ms * 1e-3) / 1e9,
+                       "dec_bytes_per_launch": dec_bytes})
+        self.clocks = clk
+        return st
+
+    def run_e2e(self):
+        """The same steps through the C ABI with HOST buffers: per step, the
+        H2D of every layer's q/k/v from pinned memory and the D2H of every
+        layer's output, inside the timed region. The copies run on a second
+        stream per layer, so layer l+1's inputs arrive while layer l computes
+        and layer l's output leaves during layer l+1 (events keep a buffer
+        from being overwritten before the copy or kernel reading it)."""
+        import torch
+
+        w = self.w
+        hq_pin = torch.empty(self.q.shape, dtype=self.dt, pin_memory=True)
+        hk_pin = torch.empty(self.knew.shape, dtype=self.dt, pin_memory=True)
+        hv_pin = torch.empty(self.vnew.shape, dtype=self.dt, pin_memory=True)
+        ho_pin = torch.empty(self.out.shape, dtype=self.dt, pin_memory=True)
+        hq_pin.copy_(self.q)
+        hk_pin.copy_(self.knew)
+        hv_pin.copy_(self.vnew)
+        self.pins = (hq_pin, hk_pin, hv_pin, ho_pin)
+        copy_stream = torch.cuda.Stream()
+        h2d_ev = [torch.cuda.Event() for _ in range(w.layers)]
+        comp_ev = [torch.cuda.Event() for _ in range(w.layers)]
+        d2h_ev = [torch.cuda.Event() for _ in range(w.layers)]
+        started = [False]
+
+        def io_h2d():
+            with torch.cuda.stream(copy_stream):
+                for layer in range(w.layers):
+                    if started[0]:
+                        copy_stream.wait_event(comp_ev[layer])  # last step's layer done with them
+                    self.q[layer].copy_(hq_pin[layer], non_blocking=True)
+                    self.knew[layer].copy_(hk_pin[layer], non_blocking=True)
+                    self.vnew[layer].copy_(hv_pin[layer], non_blocking=True)
+                    h2d_ev[layer].record(copy_stream)
+
+        def io_before(layer):
+            self.stream.wait_event(h2d_ev[layer])
+            if started[0]:
+                self.stream.wait_event(d2h_ev[layer])  # last step's output of this layer left
+
+        def io_after(layer):
+            comp_ev[layer].record(self.stream)
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(comp_ev[layer])
+                ho_pin[layer].copy_(self.out[layer], non_blocking=True)
+                d2h_ev[layer].record(copy_stream)
+            if layer == w.layers - 1:
+                started[0] = True
+
+        io = {"h2d": io_h2d, "before": io_before, "after": io_after}
+        h2d_bytes = (hq_pin.numel() + hk_pin.numel() + hv_pin.numel()) * 2
+        d2h_bytes = ho_pin.numel() * 2
+        barrier(self.world)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        base = self.warmup + self.steps
+        e0.record(self.stream)
+        copy_stream.wait_stream(self.stream)  # no copy starts before the timed region
+        for i in range(self.e2e_steps):
+            self.step(base + i, host_io=io)
+        self.stream.wait_stream(copy_stream)  # the last outputs are on the host
+        e1.record(self.stream)
+        torch.cuda.synchronize()
+        barrier(self.world)
+        return {"e2e_ms": e0.elapsed_time(e1), "h2d_bytes": float(h2d_bytes),
+                "d2h_bytes": float(d2h_bytes)}
+
+    def host_copy_rates(self):
+        """One step's H2D inputs and D2H outputs copied alone (every rank at
+        once, between barriers): the host-link rate each rank gets while all
+        ranks copy, which bounds the end-to-end leg."""
+        import torch
+
+        hq_pin, hk_pin, hv_pin, ho_pin = self.pins
+        res = {}
+        for name, pairs in (("h2d", [(self.q, hq_pin), (self.knew, hk_pin),
+                                     (self.vnew, hv_pin)]),
+                            ("d2h", [(ho_pin, self.out)])):
+            nbytes = sum(dst.numel() * 2 for dst, _ in pairs)
+            best = None
+            for _ in range(3):
+                barrier(self.world)
+                torch.cuda.synchronize()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(self.stream)
+                for dst, src in pairs:
+                    dst.copy_(src, non_blocking=True)
+                e1.record(self.stream)
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1)
+                best = ms if best is None else min(best, ms)
+            res[f"{name}_gbs"] = nbytes / (best * 1e-3) / 1e9
+            res[f"{name}_ms"] = best
+        barrier(self.world)
+        return res
+
+    def sample(self):
+        """The longest sequence of this rank's shard in the last executed step:
+        its K/V rows (gathered through its block table from the last layer's
+        pool), query rows and output rows of that layer."""
+        import torch
+
+        w, md = self.w, self.last_md
+        layer = w.layers - 1
+        p = layer % self.physical
         lengths = md.lengths(w.page)
-        keys += int(lengths.sum())
-        flops += attention_flops(w, md)
-        dm = decode_rows_mask(w, md)
-        rows_flops += attention_flops(w, md, ~dm)
-        dec_keys += int(lengths[dm].sum())
-        dec_qrows += int((md.qo[1:] - md.qo[:-1])[dm].sum())
-    t1.record(stream)
+        b = int(np.argmax(lengths))
+        n = int(lengths[b])
+        t = np.arange(n)
+        pages = md.pages[md.kv[b]:md.kv[b + 1]].astype(np.int64)
+        slots = torch.from_numpy(pages[t // w.page] * w.page + t % w.page).cuda()
+        k = self.kpools[p].index_select(0, slots).view(n, w.hkv, w.dim)
+        v = self.vpools[p].index_select(0, slots).view(n, w.hkv, w.dim)
+        q0, q1 = int(md.qo[b]), int(md.qo[b + 1])
+        return n, k, v, self.q[layer, q0:q1].contiguous(), self.out[layer, q0:q1].contiguous()
+
+    def checksums(self):
+        o = self.out.float()
+        return [float(o.sum().item()), float(o.abs().sum().item())]
+
+    def launches_per_step(self):
+        inf = self.plan.info()
+        per_layer = (1 + (1 if inf["decode_items"] else 0) + (1 if inf["split_sequences"] else 0)
+                     + (1 if inf["prefill_items"] else 0))
+        return per_layer * self.w.layers + (1 if self.cow is not None else 0)
+
+    def close(self):
+        import torch
+
+        self.plan.close()
+        self.kpools = self.vpools = None
+        self.q = self.knew = self.vnew = self.out = None
+        self.pins = None
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+
+
+def verify_results(runner, world):
+    """After timing: every rank's output checksums, and one sampled sequence
+    per rank (K/V, q, output) gathered over NCCL and recomputed in fp32 on
+    rank 0. Returns the `results` object on rank 0 (None elsewhere)."""
+    import torch
+
+    n, k, v, q, out = runner.sample()
+    sums = runner.checksums()
+    info = gather_floats([float(n)] + sums, world, device=k.device.type)
+    w = runner.w
+    if world > 1:
+        import torch.distributed as dist
+
+        maxlen = int(info[:, 0].max())
+        pad = lambda t: torch.cat([t, t.new_zeros((maxlen - t.shape[0],) + tuple(t.shape[1:]))])  # noqa: E731
+        ks, vs = [torch.empty((maxlen,) + tuple(k.shape[1:]), dtype=k.dtype, device=k.device)
+                  for _ in range(world)], \
+                 [torch.empty((maxlen,) + tuple(v.shape[1:]), dtype=v.dtype, device=v.device)
+                  for _ in range(world)]
+        qs = [torch.empty_like(q) for _ in range(world)]
+        os_ = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(ks, pad(k).contiguous())
+        dist.all_gather(vs, pad(v).contiguous())
+        dist.all_gather(qs, q)
+        dist.all_gather(os_, out)
+    else:
+        ks, vs, qs, os_ = [k], [v], [q], [out]
+    if runner.rank != 0:
+        return None
+    oks, errs = [], []
+    for r in range(world):
+        nr = int(info[r, 0])
+        ok, err = check_sample(qs[r], ks[r][:nr], vs[r][:nr], os_[r], w.hq, w.hkv, w.causal)
+        oks.append(ok)
+        errs.append(err)
+    return {"ok": bool(all(oks)), "ranks_checked": world, "per_rank_ok": oks,
+            "max_abs_err": round(max(errs), 6),
+            "checked": "the longest sequence of each rank's shard, last layer of the final step, "
+                       "recomputed in fp32 on rank 0 from K/V gathered over NCCL "
+                       "(bar: 2e-3 + 1 output ulp)",
+            "checksums": [[round(float(x), 3) for x in info[r, 1:]] for r in range(world)]}
+
+
+STAT_KEYS = ["ms", "attn_avg_ms", "kv_bytes_per_launch", "flops_per_launch", "gbs", "tflops",
+             "step_gbs", "rows_ms", "rows_tflops", "dec_ms", "dec_gbs", "rows_flops_per_launch",
+             "dec_bytes_per_launch", "e2e_ms", "h2d_bytes", "d2h_bytes", "h2d_gbs", "d2h_gbs",
+             "h2d_ms", "d2h_ms"]
+
+
+def measure(config, args, rank, world, local, steps, with_e2e=True, verify=True):
+    """Run one workload on every rank; returns (rank-0 section or None, runner
+    stats table [world, len(STAT_KEYS)], runner) — the runner already closed."""
+    r = Runner(config, rank, world, steps, args.warmup, args.e2e_steps if with_e2e else 0,
+               args.pool_gb, args.layers if config == args.config else 0)
+    st = r.run_device(local)
+    if with_e2e:
+        st.update(r.run_e2e())
+        st.update(r.host_copy_rates())
+    results = verify_results(r, world) if verify else None
+    table = gather_floats([float(st.get(k, 0.0)) for k in STAT_KEYS], world)
+    launches = r.launches_per_step()
+    section = None
+    if rank == 0:
+        section = summarize(r, table, results, launches, with_e2e)
+    r.close()
+    return section, table, r
+
+
+def summarize(r, table, results, launches, with_e2e):
+    """The JSON fields of one workload from all ranks' stats."""
+    from fekv.dist import job_rate
+
+    w = r.w
+    col = {k: table[:, i] for i, k in enumerate(STAT_KEYS)}
+    world = table.shape[0]
+    K = r.steps
+    peak, peak_kind = measured_peak_gbs()
+    tpeak, tkind = measured_peak_tflops()
+    value = job_rate([r.rows * K] * world, col["ms"])
+    sec = {
+        "value": round(value, 2), "unit": "tokens/s" if r.decode else "rows/s",
+        "steps": K, "ms_per_step": round(float(col["ms"].max()) / K, 4),
+        "config": config_dict(w, world, r.physical),
+        "per_rank": {
+            "ms_per_step": [round(float(x) / K, 4) for x in col["ms"]],
+            "kv_bytes_per_step": [float(x) * w.layers for x in col["kv_bytes_per_launch"]],
+            "step_gbs": [round(float(x), 1) for x in col["step_gbs"]],
+            "sampled_launch_gbs": [round(float(x), 1) for x in col["gbs"]],
+        },
+        # all ranks' algorithmic KV bytes over the slowest rank's time
+        "job_kv_tbs": round(float((col["kv_bytes_per_launch"] * w.layers * K).sum())
+                            / (float(col["ms"].max()) * 1e-3) / 1e12, 4),
+        "gpu_launches": launches * K,
+        "clocks": r.clocks,
+    }
+    if r.decode:
+        sec["roofline"] = {
+            "bound": "hbm", "achieved": round(float(col["gbs"][0]), 1), "peak": peak,
+            "unit": "GB/s", "frac": round(float(col["gbs"][0]) / peak, 4),
+            "peak_kind": peak_kind, "kernel": "paged_decode_kernel",
+            "algorithmic_bytes_per_launch": float(col["kv_bytes_per_launch"][0]),
+            "avg_launch_ms": round(float(col["attn_avg_ms"][0]), 5),
+            "timing": "CUDA events around the attention call (decode kernel + split-K merge) "
+                      "of one sampled layer per step",
+            # the same bytes over the whole step's time (append, merge, PDL overlap included)
+            "step_level_gbs": round(float(col["step_gbs"][0]), 1),
+            "step_level_frac": round(float(col["step_gbs"][0]) / peak, 4),
+        }
+    else:
+        per_launch_flops = float(col["flops_per_launch"][0])
+        per_launch_bytes = float(col["kv_bytes_per_launch"][0])
+        sec["roofline"] = {
+            "bound": "tensor", "achieved": round(float(col["tflops"][0]), 2), "peak": tpeak,
+            "unit": "TFLOP/s", "frac": round(float(col["tflops"][0]) / tpeak, 4),
+            "peak_kind": tkind, "kernel": "paged_prefill_tc_kernel",
+            "algorithmic_flops_per_launch": per_launch_flops,
+            "avg_launch_ms": round(float(col["attn_avg_ms"][0]), 5),
+        }
+        if not r.mixed and row_step_bound(w.block_tables, per_launch_flops, per_launch_bytes,
+                                          tpeak, peak) == "hbm":
+            sec["roofline"] = {
+                "bound": "hbm", "achieved": round(float(col["gbs"][0]), 1), "peak": peak,
+                "unit": "GB/s", "frac": round(float(col["gbs"][0]) / peak, 4),
+                "peak_kind": peak_kind, "kernel": "paged_prefill_tc_kernel",
+                "algorithmic_bytes_per_launch": per_launch_bytes,
+                "flops_per_byte": round(per_launch_flops / per_launch_bytes, 1),
+                "ridge_flops_per_byte": round(tpeak * 1e12 / (peak * 1e9), 1),
+                "avg_launch_ms": round(float(col["attn_avg_ms"][0]), 5),
+            }
+            sec["tensor_tflops"] = round(float(col["tflops"][0]), 2)
+        if r.mixed:
+            sec["roofline"].update({
+                "achieved": round(float(col["rows_tflops"][0]), 2),
+                "frac": round(float(col["rows_tflops"][0]) / tpeak, 4),
+                "algorithmic_flops_per_launch": float(col["rows_flops_per_launch"][0]),
+                "avg_launch_ms": round(float(col["rows_ms"][0]), 5),
+            })
+            sec["roofline_decode_rows"] = {
+                "bound": "hbm", "achieved": round(float(col["dec_gbs"][0]), 1), "peak": peak,
+                "unit": "GB/s", "frac": round(float(col["dec_gbs"][0]) / peak, 4),
+                "peak_kind": peak_kind, "kernel": "paged_decode_kernel + decode_merge_kernel",
+                "algorithmic_bytes_per_launch": float(col["dec_bytes_per_launch"][0]),
+                "avg_launch_ms": round(float(col["dec_ms"][0]), 5),
+            }
+            sec["attention_call_tflops"] = round(float(col["tflops"][0]), 2)
+    rl = sec["roofline"]
+    units = rl.get("algorithmic_bytes_per_launch", rl.get("algorithmic_flops_per_launch"))
+    rl["traffic"], rl["traffic_source"] = ncu_traffic(w.name, rl["kernel"], float(units))
+    if with_e2e:
+        e2e_value = job_rate([r.rows * r.e2e_steps] * world, col["e2e_ms"])
+        sec["e2e"] = {
+            "value": round(e2e_value, 2), "unit": sec["unit"],
+            "h2d_bytes_per_step": int(col["h2d_bytes"][0]),
+            "d2h_bytes_per_step": int(col["d2h_bytes"][0]), "steps": r.e2e_steps,
+            "per_rank_ms_per_step": [round(float(x) / r.e2e_steps, 4) for x in col["e2e_ms"]],
+            # one step's copies alone, all ranks copying at once
+            "host_copy": {
+                "h2d_gbs": [round(float(x), 1) for x in col["h2d_gbs"]],
+                "d2h_gbs": [round(float(x), 1) for x in col["d2h_gbs"]],
+                "h2d_ms_per_step": [round(float(x), 3) for x in col["h2d_ms"]],
+                "d2h_ms_per_step": [round(float(x), 3) for x in col["d2h_ms"]],
+            },
+        }
+    if results is not None:
+        sec["results"] = results
+    return sec
+
+
+# ---------------------------------------------------------------------------
+# small operators (append, block copy, fused RoPE + append, accept, prepare)
+# ---------------------------------------------------------------------------
+
+def _graph_time_us(fn, iters, warmup):
+    """Mean device time per call: `iters` calls captured in one CUDA graph and
+    replayed between CUDA events (host-side argument handling stays out)."""
+    import torch
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
-    clk = clocks.stop()
-    ms = t0.elapsed_time(t1)
-    attn_ms = [a.elapsed_time(b) for a, _, b in attn_ev]
-    dec_part_ms = [a.elapsed_time(m) for a, m, _ in attn_ev] if mixed else [0.0]
-    rows_part_ms = [m.elapsed_time(b) for _, m, b in attn_ev] if mixed else [0.0]
-    barrier(world)
-
-    # algorithmic bytes / FLOPs of one attention launch (averaged over steps)
-    per_launch_bytes = (keys / args.steps) * 2 * w.width * 2 + 2 * rows * w.hq * w.dim * 2
-    per_launch_flops = flops / args.steps
-    attn_avg_ms = float(np.mean(attn_ms))
-    achieved_gbs = per_launch_bytes / (attn_avg_ms * 1e-3) / 1e9
-    achieved_tflops = per_launch_flops / (attn_avg_ms * 1e-3) / 1e12
-    rows_ms = float(np.mean(rows_part_ms))
-    dec_ms = float(np.mean(dec_part_ms))
-    rows_tflops = (rows_flops / args.steps) / (rows_ms * 1e-3) / 1e12 if mixed else 0.0
-    dec_bytes = ((dec_keys / args.steps) * 2 * w.width * 2 +
-                 2 * (dec_qrows / args.steps) * w.hq * w.dim * 2)
-    dec_gbs = dec_bytes / (dec_ms * 1e-3) / 1e9 if mixed else 0.0
-
-    # end-to-end through the C ABI with host buffers: per step, H2D of every
-    # layer's q/k/v from pinned memory and D2H of every layer's output, on a
-    # copy stream and per layer, so layer l+1's inputs arrive while layer l
-    # computes and layer l's output leaves during layer l+1 (events keep a
-    # buffer from being overwritten before the copy or kernel reading it).
-    hq_pin = torch.empty(st.q.shape, dtype=st.dt, pin_memory=True)
-    hk_pin = torch.empty(st.knew.shape, dtype=st.dt, pin_memory=True)
-    hv_pin = torch.empty(st.vnew.shape, dtype=st.dt, pin_memory=True)
-    ho_pin = torch.empty(st.out.shape, dtype=st.dt, pin_memory=True)
-    hq_pin.copy_(st.q)
-    hk_pin.copy_(st.knew)
-    hv_pin.copy_(st.vnew)
-    copy_stream = torch.cuda.Stream()
-    h2d_ev = [torch.cuda.Event() for _ in range(w.layers)]
-    comp_ev = [torch.cuda.Event() for _ in range(w.layers)]
-    d2h_ev = [torch.cuda.Event() for _ in range(w.layers)]
-    io_started = [False]
-
-    def io_h2d():
-        with torch.cuda.stream(copy_stream):
-            for layer in range(w.layers):
-                if io_started[0]:
-                    copy_stream.wait_event(comp_ev[layer])  # last step's layer done with them
-                st.q[layer].copy_(hq_pin[layer], non_blocking=True)
-                st.knew[layer].copy_(hk_pin[layer], non_blocking=True)
-                st.vnew[layer].copy_(hv_pin[layer], non_blocking=True)
-                h2d_ev[layer].record(copy_stream)
-
-    def io_before(layer):
-        stream.wait_event(h2d_ev[layer])
-        if io_started[0]:
-            stream.wait_event(d2h_ev[layer])  # last step's output of this layer has left
-
-    def io_after(layer):
-        comp_ev[layer].record(stream)
-        with torch.cuda.stream(copy_stream):
-            copy_stream.wait_event(comp_ev[layer])
-            ho_pin[layer].copy_(st.out[layer], non_blocking=True)
-            d2h_ev[layer].record(copy_stream)
-        if layer == w.layers - 1:
-            io_started[0] = True
-
-    io = {"h2d": io_h2d, "before": io_before, "after": io_after}
-    h2d_bytes = (hq_pin.numel() + hk_pin.numel() + hv_pin.numel()) * 2
-    d2h_bytes = ho_pin.numel() * 2
-    barrier(world)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    g.replay()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    base = args.warmup + args.steps
-    e0.record(stream)
-    copy_stream.wait_stream(stream)  # no copy starts before the timed region
-    for i in range(args.e2e_steps):
-        step(base + i, host_io=io)
-    stream.wait_stream(copy_stream)  # the last outputs are on the host
-    e1.record(stream)
+    e0.record()
+    g.replay()
+    e1.record()
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
+    del g
+    return e0.elapsed_time(e1) * 1e3 / iters
 
-    # this repo's kernels per layer-step: the append, the decode kernel and its
-    # split-K merge when the step has decode rows, the tcgen05 kernel when it
-    # has multi-row sequences
-    inf = plan.info()
-    launches_per_layer = (1 + (1 if inf["decode_items"] else 0) +
-                          (1 if inf["split_sequences"] else 0) + (1 if inf["prefill_items"] else 0))
-    stats = gather_floats([ms, e2e_ms, attn_avg_ms, achieved_gbs, keys, achieved_tflops,
-                           rows_ms, rows_tflops, dec_ms, dec_gbs], world)
-    plan.close()
-    if rank != 0:
-        return None
-    ms_max = float(stats[:, 0].max())
-    e2e_max = float(stats[:, 1].max())
-    value = job_rate([rows * args.steps] * world, stats[:, 0])
-    e2e_value = job_rate([rows * args.e2e_steps] * world, stats[:, 1])
-    line = {
-        "metric": METRIC,
-        "value": round(value, 2),
-        "unit": "tokens/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(ms_max / args.steps, 4),
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "bf16" if w.bf16 else "f16",
-        "data": "synthetic (seeded N(0,1) x scale K/V/q; random non-contiguous pages)",
-        "config": {
-            "workload": f"{w.name}: hq{w.hq}/hkv{w.hkv}/d{w.dim} page{w.page}, {w.layers} layers, "
-                        f"{w.batch} seqs/GPU, 1 appended token + decode attention per layer-step",
-            "seqs_per_gpu": w.batch, "layers": w.layers, "physical_layer_pools": physical,
-            "mean_context": float(np.mean(w.cached)),
-            "kv_bytes_per_step": float(per_launch_bytes * w.layers),
-            "l2": "inputs larger than L2 (each layer's KV pages exceed 126 MB)",
-            "parallelism": f"sequence-sharded x{world}, no hot-path collective",
-        },
-        "decode_attn_tbs": round(float(stats[:, 3].sum()) / 1e3, 4),
-        "decode_attn_frac_of_peak": round(float(stats[:, 3].mean()) / peak, 4),
-        "roofline": {
-            "bound": "hbm",
-            "achieved": round(float(stats[0, 3]), 1),
-            "peak": peak,
-            "unit": "GB/s",
-            "frac": round(float(stats[0, 3]) / peak, 4),
-            "peak_kind": peak_kind,
-            "kernel": "paged_decode_kernel",
-            "algorithmic_bytes_per_launch": float(per_launch_bytes),
-            "avg_launch_ms": round(float(stats[0, 2]), 5),
-            "traffic": None,
-            "traffic_source": None,
-        },
-        "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s",
-                "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": int(d2h_bytes),
-                "steps": args.e2e_steps},
-        "gpu_launches": launches_per_layer * w.layers * args.steps,
-        "clocks": clk,
+
+def ops_suite(iters=50, warmup=5, only=None):
+    """Timings of the path's smaller operators on one GPU; each entry gives
+    the mean time per call and, where the operator moves data, its
+    algorithmic bytes (every byte it must read or write once) against the HBM
+    copy peak. Cases larger than L2 show the kernel's bandwidth; the
+    decode-step cases are bound by launch latency. `only` runs one case."""
+    import torch
+
+    import fekv
+    from fekv import workloads
+
+    peak, peak_kind = measured_peak_gbs()
+    dev = torch.device("cuda")
+    bf = torch.bfloat16
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    out = {"peak_gbs": peak, "peak_kind": peak_kind, "iters": iters,
+           "timing": "CUDA-graph replay of `iters` calls between CUDA events"}
+
+    def entry(us, nbytes, **kw):
+        e = {"us": round(us, 2)}
+        if nbytes:
+            gbs = nbytes / (us * 1e-6) / 1e9
+            e.update({"bytes": int(nbytes), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)})
+        e.update(kw)
+        return e
+
+    def append_case(rows, slots_total, width=1024):
+        k = torch.randn(rows, width, generator=g, device=dev).to(bf)
+        v = torch.randn(rows, width, generator=g, device=dev).to(bf)
+        kc = torch.empty(slots_total, width, dtype=bf, device=dev)
+        vc = torch.empty_like(kc)
+        slots = torch.randperm(slots_total, device=dev)[:rows].to(torch.int64)
+        us = _graph_time_us(lambda: fekv.store(k, v, kc, vc, slots), iters, warmup)
+        return entry(us, rows * (width * 2 * 2 * 2 + 8), kernel="append_kernel", rows=rows,
+                     width=width)
+
+    def copy_case(full, sets):
+        # C4's copy-on-write tails move 78 MB, less than L2: they cycle over
+        # four copies of the pools so that each call finds its pages evicted
+        w4 = workloads.c4(seed=0)
+        src, dst, ntok = (np.asarray(x, np.int32) for x in w4.cow)
+        n = 256 if full else len(src)
+        s_ = torch.from_numpy(np.arange(n, dtype=np.int32) if full else src).to(dev)
+        d_ = torch.from_numpy((np.arange(n, dtype=np.int32) + 512) if full else dst).to(dev)
+        t_ = torch.from_numpy(np.full(n, 16, np.int32) if full else ntok).to(dev)
+        pages_total = int(max(int(d_.max()), int(s_.max()))) + 2
+        pools = []
+        for _ in range(sets):
+            kp = [torch.zeros(pages_total * 16, w4.width, dtype=bf, device=dev) for _ in range(48)]
+            pools.append((kp, [torch.zeros_like(p) for p in kp]))
+        turn = [0]
+
+        def call():
+            kp, vp = pools[turn[0] % sets]
+            turn[0] += 1
+            fekv.copy_blocks(kp, vp, s_, d_, t_, 16, w4.width, pages_total)
+
+        us = _graph_time_us(call, iters, warmup)
+        tok = int(t_.sum())
+        return entry(us, 48 * 2 * tok * w4.width * 2 * 2, kernel="copy_blocks_kernel", copies=n,
+                     tokens=tok, pool_sets=sets)
+
+    def gather_case():
+        # a C2 layer's K gathered densely (the ATen path's index_select
+        # without its max_context padding)
+        w2 = workloads.c2(seed=0)
+        md = w2.metadata(0)
+        lengths = md.lengths(w2.page)
+        pool = torch.randn(w2.cache_slots, w2.width, generator=g, device=dev).to(bf)
+        dense = torch.empty(int(lengths.sum()), w2.width, dtype=bf, device=dev)
+        kv_d, pages_d, last_d = (torch.from_numpy(a).to(dev) for a in (md.kv, md.pages, md.last))
+        roff = torch.from_numpy(np.concatenate([[0], np.cumsum(lengths)[:-1]]).astype(np.int32)
+                                ).to(dev)
+        us = _graph_time_us(lambda: fekv.gather(pool, dense, kv_d, pages_d, last_d, roff,
+                                                md.batch, int(lengths.max()), w2.page, w2.width),
+                            iters, warmup)
+        return entry(us, int(lengths.sum()) * w2.width * 2 * 2, kernel="gather_kernel",
+                     tokens=int(lengths.sum()))
+
+    def clear_case():
+        pages = torch.arange(256, dtype=torch.int32, device=dev)
+        pools = [torch.empty(300 * 16, 1024, dtype=bf, device=dev) for _ in range(96)]
+        us = _graph_time_us(lambda: fekv.clear_pages(pools, pages, 16, 1024, 300), iters, warmup)
+        return entry(us, 96 * 256 * 16 * 1024 * 2, kernel="clear_pages_kernel", pools=96,
+                     pages=256)
+
+    def rope_case(rows, hq=32, hkv=8, dim=128, max_pos=8192):
+        # fused RoPE + append (Qwen3-8B shape), and the reference's order:
+        # rope in place, then the append
+        inv = 1.0 / (1e6 ** (np.arange(0, dim, 2, dtype=np.float64) / dim))
+        ang = np.arange(max_pos, dtype=np.float64)[:, None] * inv[None, :]
+        cache = torch.from_numpy(np.concatenate([np.cos(ang), np.sin(ang)], 1).astype(np.float32)
+                                 ).to(dev)
+        q = torch.randn(rows, hq, dim, generator=g, device=dev).to(bf)
+        k = torch.randn(rows, hkv, dim, generator=g, device=dev).to(bf)
+        v = torch.randn(rows, hkv, dim, generator=g, device=dev).to(bf)
+        slots_total = max(1 << 18, rows)
+        kc = torch.empty(slots_total, hkv * dim, dtype=bf, device=dev)
+        vc = torch.empty_like(kc)
+        slots = torch.randperm(slots_total, device=dev)[:rows].to(torch.int64)
+        pos = torch.randint(0, max_pos, (rows,), generator=g, device=dev)
+        # q read + written, k and v read, both written to the pools, the cos |
+        # sin row of each position read, slot and position read
+        nbytes = rows * (2 * hq * dim * 2 + 2 * hkv * dim * 2 + 2 * hkv * dim * 2 + dim * 4 + 16)
+        us = _graph_time_us(lambda: fekv.rope_append(q, k, v, kc, vc, slots, pos, cache), iters,
+                            warmup)
+        us2 = _graph_time_us(lambda: (fekv.rope(q, k, pos, cache),
+                                      fekv.store(k, v, kc, vc, slots)), iters, warmup)
+        return entry(us, nbytes, kernel="rope_vec_kernel (fused append)", rows=rows,
+                     rope_then_append_us=round(us2, 2))
+
+    def accept_case():
+        draft = torch.randint(0, 1000, (64, 15), generator=g, device=dev)
+        verify = torch.randint(0, 1000, (64, 16), generator=g, device=dev)
+        acc = torch.zeros(64, 17, dtype=torch.int64, device=dev)
+        return entry(_graph_time_us(lambda: fekv.accept(draft, verify, acc), iters, warmup), 0,
+                     kernel="accept_kernel")
+
+    def prepare_host_case():
+        w2 = workloads.c2(seed=0, steps=2)
+        md = w2.metadata(0)
+        plan = fekv.AttentionPlan(w2.hq, w2.hkv, 128, 16, w2.batch, w2.max_pages(2), True,
+                                  w2.num_blocks)
+        stream = torch.cuda.current_stream()
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        for _ in range(iters):
+            plan.prepare(md.qo, md.kv, md.pages, md.last, md.batch, md.rows, False, stream)
+        torch.cuda.synchronize()
+        us = (time.perf_counter() - t) * 1e6 / iters
+        plan.close()
+        return entry(us, 0, note="host planner + one H2D copy, wall clock")
+
+    def prepare_device_case():
+        w2 = workloads.c2(seed=0, steps=2)
+        md = w2.metadata(0)
+        stride = int(np.diff(md.kv).max()) + 1
+        bt = np.zeros((w2.batch, stride), np.int32)
+        for b, tb in enumerate(w2.block_tables):
+            bt[b, :len(tb)] = tb
+        bt_d = torch.from_numpy(bt).to(dev)
+        starts = torch.from_numpy(w2.cached.astype(np.int32)).to(dev)
+        sl = torch.empty(w2.batch, dtype=torch.int64, device=dev)
+        ps = torch.empty_like(sl)
+        plan = fekv.AttentionPlan(w2.hq, w2.hkv, 128, 16, w2.batch, w2.max_pages(2), True,
+                                  w2.num_blocks)
+        us = _graph_time_us(lambda: plan.step_prepare_device(bt_d, starts, 1, sl, ps), iters,
+                            warmup)
+        plan.close()
+        return entry(us, 0, kernel="plan_device_kernel",
+                     note="slot mapping + work lists of a C2 step, one kernel")
+
+    cases = {
+        "append_c2_step": lambda: append_case(64, 1 << 20),
+        "append_c3_step": lambda: append_case(2108, 1 << 20),
+        "append_64k_rows": lambda: append_case(65536, 1 << 18),
+        "copy_blocks_c4_cow_48_layers": lambda: copy_case(False, 4),
+        "copy_blocks_256_pages_48_layers": lambda: copy_case(True, 1),
+        "gather_c2_layer": gather_case,
+        "clear_pages_256_pages_96_pools": clear_case,
+        "rope_append_c2_step": lambda: rope_case(64),
+        "rope_append_c3_step": lambda: rope_case(2108),
+        "rope_append_64k_rows": lambda: rope_case(65536),
+        "accept_batch64_k15": accept_case,
+        "prepare_host_c2_step": prepare_host_case,
+        "prepare_device_c2_step": prepare_device_case,
     }
-    if not decode:
-        # prefill / verify workloads: the attention is a tensor-core contraction
-        tpeak, tkind = measured_peak_tflops()
-        line["metric"] = f"{w.name} paged attention TFLOP/s (tensor pipe) and query rows/s"
-        line["unit"] = "rows/s"
-        line["config"]["workload"] = (
-            f"{w.name}: hq{w.hq}/hkv{w.hkv}/d{w.dim} page{w.page}, {w.layers} layers, "
-            f"{w.batch} seqs, {rows} query rows per layer-step, "
-            f"{'causal' if w.causal else 'non-causal'}"
-            + (", copy-on-write of shared tail pages each step" if w.cow is not None else ""))
-        line["config"]["attention_flops_per_step"] = per_launch_flops * w.layers
-        line.pop("decode_attn_tbs")
-        line.pop("decode_attn_frac_of_peak")
-        line["roofline"] = {
-            "bound": "tensor", "achieved": round(float(stats[0, 5]), 2), "peak": tpeak,
-            "unit": "TFLOP/s", "frac": round(float(stats[0, 5]) / tpeak, 4), "peak_kind": tkind,
-            "kernel": "paged_prefill_tc_kernel",
-            "algorithmic_flops_per_launch": per_launch_flops,
-            "avg_launch_ms": round(float(stats[0, 2]), 5), "traffic": None,
-            "traffic_source": None,
-        }
-        ridge = tpeak * 1e12 / (peak * 1e9)
-        if not mixed and row_step_bound(w.block_tables, per_launch_flops, per_launch_bytes,
-                                        tpeak, peak) == "hbm":
-            line["roofline"] = {
-                "bound": "hbm", "achieved": round(float(stats[0, 3]), 1), "peak": peak,
-                "unit": "GB/s", "frac": round(float(stats[0, 3]) / peak, 4),
-                "peak_kind": peak_kind, "kernel": "paged_prefill_tc_kernel",
-                "algorithmic_bytes_per_launch": float(per_launch_bytes),
-                "flops_per_byte": round(per_launch_flops / per_launch_bytes, 1),
-                "ridge_flops_per_byte": round(ridge, 1),
-                "avg_launch_ms": round(float(stats[0, 2]), 5), "traffic": None,
-                "traffic_source": None,
-            }
-            line["tensor_tflops"] = round(float(stats[0, 5]), 2)
-        if mixed:
-            # the step's multi-row sequences on the tcgen05 kernel, and its
-            # decode rows on the decode kernel, each against its own roof
-            line["roofline"].update({
-                "achieved": round(float(stats[0, 7]), 2),
-                "frac": round(float(stats[0, 7]) / tpeak, 4),
-                "algorithmic_flops_per_launch": rows_flops / args.steps,
-                "avg_launch_ms": round(float(stats[0, 6]), 5),
-            })
-            line["roofline_decode_rows"] = {
-                "bound": "hbm", "achieved": round(float(stats[0, 9]), 1), "peak": peak,
-                "unit": "GB/s", "frac": round(float(stats[0, 9]) / peak, 4),
-                "peak_kind": peak_kind, "kernel": "paged_decode_kernel + decode_merge_kernel",
-                "algorithmic_bytes_per_launch": dec_bytes,
-                "avg_launch_ms": round(float(stats[0, 8]), 5),
-            }
-            line["attention_call_tflops"] = round(float(achieved_tflops), 2)
-        line["gpu_launches"] = launches_per_layer * w.layers * args.steps + (
-            args.steps if w.cow is not None else 0)
-    rl = line["roofline"]
-    units = rl.get("algorithmic_bytes_per_launch", rl.get("algorithmic_flops_per_launch"))
-    rl["traffic"], rl["traffic_source"] = ncu_traffic(w.name, rl["kernel"], float(units))
-    if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(w, args)
-    return line
+    if only is not None and only not in cases:
+        raise ValueError(f"unknown operator case {only}; one of {sorted(cases)}")
+    for name, fn in cases.items():
+        if only is None or name == only:
+            out[name] = fn()
+            torch.cuda.empty_cache()
+    if fekv.device_errors() != 0:
+        raise RuntimeError("device error bits set during the operator timings")
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -598,7 +1074,7 @@ def _ref_layer_step(ref, w, md, pools, inputs):
     return ref.attention(q, kp, vp, w.causal)
 
 
-def cpu_reference_setup(w, steps):
+def cpu_reference_setup(w):
     import oracle
     from fekv import workloads
 
@@ -611,36 +1087,49 @@ def cpu_reference_setup(w, steps):
     q = workloads.random_bits(rng, (rows, w.hq, w.dim), w.bf16, w.scale)
     kn = workloads.random_bits(rng, (rows, w.width), w.bf16, w.scale)
     vn = workloads.random_bits(rng, (rows, w.width), w.bf16, w.scale)
-    ref = oracle.RefAten(w.hq, w.hkv, w.dim, w.page, w.batch, w.max_pages(steps), w.bf16,
+    # max_pages sized to this step's longest context (the ATen path's gather
+    # is padded to max_pages)
+    ref = oracle.RefAten(w.hq, w.hkv, w.dim, w.page, w.batch, w.max_pages(1), w.bf16,
                          w.num_blocks)
     return ref, (kp, vp), (q, kn, vn), oracle.ref_get_threads()
 
 
+def time_reference_layer_steps(w, count=None, seconds=None, warmup=1):
+    """Per-layer-step wall times of the reference library on this workload's
+    first step (store + prepare_plan + attention of every sequence):
+    `count` steps, or as many as fit in `seconds`. Returns (times, threads)."""
+    ref, pools, inputs, threads = cpu_reference_setup(w)
+    md = w.metadata(0)
+    for _ in range(warmup):
+        _ref_layer_step(ref, w, md, pools, inputs)
+    times = []
+    t_end = time.time() + (seconds or 0)
+    while (count is not None and len(times) < count) or \
+            (count is None and (time.time() < t_end or len(times) < 3)):
+        t = time.perf_counter()
+        _ref_layer_step(ref, w, md, pools, inputs)
+        times.append(time.perf_counter() - t)
+    ref.close()
+    return times, threads
+
+
 def cpu_baseline(w, args):
-    """One layer-step of the workload (store + prepare_plan + attention for
-    every sequence) through the reference library, repeated for ~10 s."""
+    """The bench workload's first layer-step through the reference library,
+    repeated for ~args.cpu_seconds, median time scaled to the layer count."""
     import oracle
 
     if not oracle.ref_available():
         return {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference",
                 "sample": "oracle/_ref not built"}
-    ref, pools, inputs, threads = cpu_reference_setup(w, 4)
-    md = w.metadata(0)
-    _ref_layer_step(ref, w, md, pools, inputs)  # warm
-    times = []
-    t_end = time.time() + args.cpu_seconds
-    while time.time() < t_end or len(times) < 3:
-        t = time.perf_counter()
-        _ref_layer_step(ref, w, md, pools, inputs)
-        times.append(time.perf_counter() - t)
-    ref.close()
+    times, threads = time_reference_layer_steps(w, seconds=args.cpu_seconds)
     layer_s = statistics.median(times)
-    rows = md.rows
+    rows = w.metadata(0).rows
     return {"value": round(rows / (layer_s * w.layers), 3),
             "unit": "tokens/s" if rows == w.batch else "rows/s",
             "cores": threads, "kind": "reference",
-            "sample": f"{len(times)} layer-steps of {w.name} ({w.batch} seqs, {rows} rows: store + prepare_plan "
-                      f"+ attention), median {layer_s*1e3:.1f} ms/layer, scaled to {w.layers} layers",
+            "sample": f"{len(times)} layer-steps of {w.name} ({w.batch} seqs, {rows} rows: store + "
+                      f"prepare_plan + attention), median {layer_s*1e3:.1f} ms/layer, scaled to "
+                      f"{w.layers} layers",
             "cpu_model": _cpu_model()}
 
 
@@ -655,42 +1144,167 @@ def _cpu_model():
     return None
 
 
+def reference_gpu(args, world):
+    """The reference's own GPU attention (src/flashinfer_attention.cu: FlashInfer's
+    FA2 paged kernel, split-KV disabled, built for sm_100a from the reference
+    source by oracle/build_oracle.py) timed on one GPU, on the same layer
+    inputs this repository's arm times: a C2 decode layer (shard 0, the
+    headline) and a C4 verify layer. Each launch reads the next of eight
+    layer pools, so its pages are not in L2. Only the attention launches are
+    timed (CUDA events), as in the repository arm's `roofline`."""
+    import torch
+
+    import oracle
+
+    if not torch.cuda.is_available():
+        return {"unavailable": "no GPU"}
+    if not oracle.ref_flashinfer_available():
+        return {"unavailable": "oracle/_ref/libfe_ref_flashinfer.so not built"}
+    peak, peak_kind = measured_peak_gbs()
+    tpeak, tkind = measured_peak_tflops()
+    out = {"kernel": "FlashInfer BatchPrefillWithPagedKVCache (FA2, split-KV off), "
+                     "src/flashinfer_attention.cu built for sm_100a",
+           "flashinfer_headers": "flashinfer wheel 0.6.11.post2 (the reference pins 0.6.14)"}
+    total_steps = args.warmup + args.steps + args.e2e_steps + 1
+    for name, config in (("c2_decode_layer", "c2"), ("c4_verify_layer", "c4")):
+        w = make_workload(config, 0, world, total_steps)
+        md = w.metadata(args.warmup if config == "c2" else 0)
+        g = torch.Generator(device="cuda")
+        g.manual_seed(11)
+        pools = []
+        for _ in range(8):
+            kc = torch.empty(w.cache_slots, w.width, dtype=torch.bfloat16, device="cuda")
+            vc = torch.empty_like(kc)
+            kc.normal_(0.0, w.scale, generator=g)
+            vc.normal_(0.0, w.scale, generator=g)
+            pools.append((kc, vc))
+        q = (torch.randn(md.rows, w.hq, w.dim, generator=g, device="cuda") * w.scale).to(
+            torch.bfloat16)
+        o = torch.empty_like(q)
+        stream = torch.cuda.current_stream().cuda_stream
+        fi = oracle.RefFlashInfer(w.hq, w.hkv, w.dim, w.page, w.batch, w.max_pages(total_steps),
+                                  True, w.num_blocks)
+        fi.prepare(md.qo, md.kv, md.pages, md.last, stream)
+        for i in range(max(args.warmup, 3)):
+            fi.attention(q, *pools[i % 8], o, w.causal, stream)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        n = max(args.steps, 8)
+        e0.record()
+        for i in range(n):
+            fi.attention(q, *pools[i % 8], o, w.causal, stream)
+        e1.record()
+        torch.cuda.synchronize()
+        fi.close()
+        ms = e0.elapsed_time(e1) / n
+        keys = int(md.lengths(w.page).sum())
+        nbytes = keys * 2 * w.width * 2 + 2 * md.rows * w.hq * w.dim * 2
+        flops = attention_flops(w, md)
+        ent = {"avg_launch_ms": round(ms, 5), "launches": n,
+               "algorithmic_bytes_per_launch": float(nbytes),
+               "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+               "frac_of_hbm_peak": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4),
+               "algorithmic_flops_per_launch": flops,
+               "tflops": round(flops / (ms * 1e-3) / 1e12, 2)}
+        if config == "c4":
+            ent["frac_of_tensor_peak"] = round(flops / (ms * 1e-3) / 1e12 / tpeak, 4)
+        out[name] = ent
+        del pools, q, o
+        torch.cuda.empty_cache()
+    out["peaks"] = {"hbm_gbs": peak, "hbm_kind": peak_kind, "bf16_tflops": tpeak,
+                    "bf16_kind": tkind}
+    return out
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU/ATen implementation of the path
     (FlashEngine.cpp src/portable_gpu_ops.cpp compiled for the CPU), all host
-    threads. Each step = one layer-step of the workload; rank 0 only."""
+    threads, on the same workload as this repository's headline (shard 0).
+    Each timed step is one layer-step (store + prepare_plan + attention of
+    all sequences); `ms_per_step` is that measured time, `value` converts it
+    to decode tokens/s of the whole layer stack. Rank 0 only."""
     if rank != 0:
         return None
     import oracle
 
-    w = make_workload(args.config, 0, 1, 4)
+    total_steps = args.warmup + args.steps + args.e2e_steps + 1
+    w = make_workload(args.config, 0, world, total_steps)
     if not oracle.ref_available():
         return {"impl": "reference", "unavailable": "oracle/_ref/libfe_ref_aten.so not built"}
-    ref, pools, inputs, threads = cpu_reference_setup(w, 4)
-    md = w.metadata(0)
-    for _ in range(args.warmup):
-        _ref_layer_step(ref, w, md, pools, inputs)
-    t = time.perf_counter()
-    for _ in range(args.steps):
-        _ref_layer_step(ref, w, md, pools, inputs)
-    el = time.perf_counter() - t
-    ref.close()
-    layer_s = el / args.steps
-    value = w.batch / (layer_s * w.layers)
-    return {
-        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s",
+    times, threads = time_reference_layer_steps(w, count=args.steps, warmup=args.warmup)
+    layer_s = statistics.median(times)
+    rows = w.metadata(0).rows
+    value = rows / (layer_s * w.layers)
+    unit = "tokens/s" if rows == w.batch else "rows/s"
+    sample = (f"{args.steps} layer-steps of {w.name} shard 0 ({w.batch} seqs, {rows} rows: "
+              f"store + prepare_plan + attention), median {layer_s * 1e3:.1f} ms, "
+              f"scaled to {w.layers} layers")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(layer_s * 1e3 * w.layers, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if w.bf16 else "f16",
-        "data": "synthetic", "config": {"workload": f"{w.name} (one layer-step per step, scaled "
-                                                    f"to {w.layers} layers)",
-                                        "seqs": w.batch, "layers": w.layers},
-        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads,
-                         "kind": "reference",
-                         "sample": f"{args.steps} layer-steps of {w.name}, all sequences"},
-        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+        "ms_per_step": round(layer_s * 1e3, 3),
+        "step": "one layer-step (the timed unit)",
+        "ms_per_model_step_extrapolated": round(layer_s * 1e3 * w.layers, 3),
+        "timed_region_s": round(float(sum(times)), 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16" if w.bf16 else "f16",
+        "data": "synthetic (seeded N(0,1) x scale K/V/q; random non-contiguous pages)",
+        "config": config_dict(w, world, physical_pools(w, args.pool_gb)),
+        "cpu_baseline": {"value": round(value, 3), "unit": unit, "cores": threads,
+                         "kind": "reference", "sample": sample, "cpu_model": _cpu_model()},
+        "e2e": {"value": round(value, 3), "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    # the reference's own GPU attention on the same layer inputs (one GPU)
+    if not args.no_reference_gpu:
+        try:
+            line["reference_gpu"] = reference_gpu(args, world)
+        except Exception as e:  # reported, not fatal: the CPU arm above stands
+            line["reference_gpu"] = {"unavailable": f"{type(e).__name__}: {str(e)[:200]}"}
+    return line
+
+
+# ---------------------------------------------------------------------------
+# this repository's arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, rank, world, local):
+    import fekv
+
+    fekv.load()
+    head, table, runner = measure(args.config, args, rank, world, local, args.steps)
+    w = runner.w
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if w.bf16 else "f16",
+            "data": "synthetic (seeded N(0,1) x scale K/V/q; random non-contiguous pages)",
+        }
+        line.update({k: v for k, v in head.items() if k not in ("value", "unit", "ms_per_step",
+                                                               "steps")})
+        if runner.decode:
+            line["decode_attn_tbs"] = round(float(table[:, STAT_KEYS.index("gbs")].sum()) / 1e3, 4)
+        else:
+            line["metric"] = f"{w.name} paged attention TFLOP/s (tensor pipe) and query rows/s"
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(w, args)
+    subs = [s for s in args.sub.split(",") if s and s != "none"] if args.config == "c2" else []
+    for sub in subs:
+        if sub == "c5":
+            sec, _, _ = measure("c5", args, rank, world, local, C5_STEPS)
+        elif sub in ("c3", "c4") and world == 1:
+            sec, _, _ = measure(sub, args, rank, world, local, args.steps, verify=False)
+        elif sub == "ops" and world == 1:
+            sec = ops_suite(args.ops_iters)
+        else:
+            continue
+        if rank == 0:
+            line[sub] = sec
+    return line
 
 
 def main(argv=None):
@@ -699,22 +1313,39 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c2", "c3", "c4", "c5", "q35", "draft"], default="c2")
+    ap.add_argument("--config", choices=["c2", "c3", "c4", "c5", "q35", "draft", "ops"],
+                    default="c2",
+                    help="headline workload; `ops` prints only the small-operator timings "
+                         "(profiling one operator: --ops-case)")
+    ap.add_argument("--ops-case", default=None, help="with --config ops: one operator case")
+    ap.add_argument("--ops-iters", type=int, default=50)
+    ap.add_argument("--sub", default="c5,c3,c4,ops",
+                    help="workloads measured beside the c2 headline (comma list, or none)")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--pool-gb", type=float, default=150.0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="reference arm: skip timing the reference's FlashInfer GPU path")
     ap.add_argument("--layers", type=int, default=0,
-                    help="override the layer count (profiling a small case only)")
+                    help="override the layer count of --config (profiling a small case only)")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.impl == "reference":
+    if args.config == "ops":
+        import torch
+
+        import fekv
+
+        fekv.load()
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        line = {"ops": ops_suite(args.ops_iters, min(5, args.ops_iters), args.ops_case)}
+    elif args.impl == "reference":
         line = run_reference(args, rank, world)
     else:
-        rank, world, local = dist_setup(args.gpus)
+        rank, world, local = dist_setup()
         line = run_ours(args, rank, world, local)
         if world > 1:
             import torch.distributed as dist

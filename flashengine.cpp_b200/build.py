@@ -33,7 +33,7 @@ NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2", "-Xpt
 CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wextra"]
 
 KV_SOURCES = ["fe_kv_ops.cu", "fe_attn.cu", "fe_decode.cu", "fe_prefill_tc.cu", "fe_rope_accept.cu",
-              "fe_plan_device.cu", "fe_attn_plan.cpp"]
+              "fe_plan_device.cu", "fe_attn_plan.cpp", "fe_kv_fork.cpp"]
 SHIM_SOURCES = ["fe_native_cuda_shim.cpp"]
 HEADERS = ["fe_common.cuh", "fe_attn_common.cuh", "fe_attn_plan.h", "fe_tcgen05.cuh"]
 

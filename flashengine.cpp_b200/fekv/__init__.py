@@ -13,5 +13,5 @@ from . import metadata, workloads  # noqa: F401
 from ._lib import (FE_DTYPE_BF16, FE_DTYPE_F16, FeError, LIB_PATH, SHIM_PATH,  # noqa: F401
                    load)
 from .ops import (AttentionPlan, HostPlan, accept, attention, clear_pages,  # noqa: F401
-                  copy_blocks, create_plan, destroy_plan, device_errors, gather,
+                  copy_blocks, create_plan, destroy_plan, device_errors, fork_copies, gather,
                   paged_decode_noalloc, prepare_plan, rope, rope_append, store)

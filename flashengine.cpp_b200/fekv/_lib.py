@@ -52,6 +52,7 @@ SIGNATURES = {
     "fe_kv_copy_blocks": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "fe_kv_clear_pages": (_I, [_P, _I, _P, _I, _I, _I, _I, _I, _P]),
     "fe_kv_gather": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "fe_kv_fork_copies": (_I, [_I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _I, ctypes.POINTER(_I)]),
     "fe_attn_plan_create": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
     "fe_attn_plan_destroy": (_I, [_P]),
     "fe_attn_plan_prepare": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),

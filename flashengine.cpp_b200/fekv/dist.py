@@ -13,6 +13,27 @@ def shard_range(rank: int, per_rank: int) -> range:
     return range(rank * per_rank, (rank + 1) * per_rank)
 
 
+def balanced_shards(costs, nshards: int, per_shard: int) -> list:
+    """Split len(costs) == nshards * per_shard items into `nshards` shards of
+    exactly `per_shard` items with nearly equal total cost: items are taken
+    longest first and each goes to the open shard (fewer than per_shard
+    items) with the smallest total so far. Returns each shard's item
+    indices in ascending order."""
+    costs = np.asarray(costs, dtype=np.float64)
+    if costs.shape[0] != nshards * per_shard:
+        raise ValueError("need exactly nshards * per_shard items")
+    totals = np.zeros(nshards)
+    counts = np.zeros(nshards, dtype=np.int64)
+    members = [[] for _ in range(nshards)]
+    for i in np.argsort(-costs, kind="stable"):
+        open_ = np.flatnonzero(counts < per_shard)
+        s = int(open_[np.argmin(totals[open_])])
+        members[s].append(int(i))
+        totals[s] += costs[i]
+        counts[s] += 1
+    return [np.sort(np.asarray(m, dtype=np.int64)) for m in members]
+
+
 def gather_floats(values, world: int, device: str = "cuda") -> np.ndarray:
     """All-gather a small float64 vector per rank -> [world, len(values)]."""
     import torch

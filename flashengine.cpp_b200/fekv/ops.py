@@ -138,6 +138,34 @@ def copy_blocks(k_pools, v_pools, src, dst, ntok, page, width, num_pages_total, 
                                 _stream(stream)), "copy_blocks")
 
 
+def fork_copies(parent_tables, child_tables, fork_lens, page):
+    """Copy-on-write lists for forked sequences (host only): for fork f, the
+    pages of the first fork_lens[f] tokens that child_tables[f] does not share
+    with parent_tables[f] become (src, dst, ntok) entries for copy_blocks.
+    Returns three int32 numpy arrays. Raises FeError on tables that would let
+    one sequence write a page the other reads (a shared partial tail)."""
+    lib = _lib.load()
+    n = len(parent_tables)
+    if len(child_tables) != n or len(fork_lens) != n:
+        raise ValueError("one parent table, child table and fork length per fork")
+    pt = [np.asarray(t, np.int32) for t in parent_tables]
+    ct = [np.asarray(t, np.int32) for t in child_tables]
+    poff = _host_i32(np.concatenate([[0], np.cumsum([len(t) for t in pt])]))
+    coff = _host_i32(np.concatenate([[0], np.cumsum([len(t) for t in ct])]))
+    pcat = _host_i32(np.concatenate(pt) if n else np.zeros(1, np.int32))
+    ccat = _host_i32(np.concatenate(ct) if n else np.zeros(1, np.int32))
+    lens = np.ascontiguousarray(np.asarray(fork_lens, np.int64))
+    cap = int(sum(-(-int(L) // int(page)) for L in lens)) if n else 0
+    src, dst, ntok = (np.zeros(max(cap, 1), np.int32) for _ in range(3))
+    count = ctypes.c_int(0)
+    hp = lambda a: a.ctypes.data_as(_P)  # noqa: E731
+    check(lib.fe_kv_fork_copies(n, hp(pcat), hp(poff), hp(ccat), hp(coff), hp(lens), int(page),
+                                hp(src), hp(dst), hp(ntok), cap, ctypes.byref(count)),
+          "fork_copies")
+    k = count.value
+    return src[:k].copy(), dst[:k].copy(), ntok[:k].copy()
+
+
 def clear_pages(pools, pages, page, width, num_pages_total, dtype=None, stream=None):
     """Zero whole pages (int32 device tensor `pages`) of every pool."""
     lib = _lib.load()

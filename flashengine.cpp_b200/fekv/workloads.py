@@ -17,7 +17,10 @@ C4 ``c4``: hq32/hkv4 bf16, 48 layers; 128 sequences over one shared
     divergent tokens, so a partial shared tail page is copied on write; then
     a 16-row verify block per sequence, non-causal.
 C5 ``c5``: hq64/hkv8 bf16, 64 layers; 1024 sequences, 128 per GPU, contexts
-    LogNormal(ln 8192, 0.5) clipped to [2048, 32768]; split-K decode.
+    LogNormal(ln 8192, 0.5) clipped to [2048, 32768]; split-K decode. The
+    1024 sequences are split into 8 shards of nearly equal KV bytes.
+``c2_shard``: C2 for sequence-sharded runs (one seeded list of 8 x 64
+    contexts split into balanced shards of 64).
 
 Two head_dim 256 workloads cover the hybrid and draft models' full-attention
 layers (the reference serves them through ATen with any head_dim):
@@ -163,7 +166,7 @@ def c4(seed: int = 0, batch: int = 128, prefix: int = 2048, verify_rows: int = 1
         next_page[0] += n
         return out
 
-    tables, cached, src, dst, ntok = [None] * batch, np.zeros(batch, np.int64), [], [], []
+    tables, cached, forks = [None] * batch, np.zeros(batch, np.int64), []
     shared = list(range(prefix_pages))
     for e in range(0, batch, 2):
         # even sequence: prefix + its own divergent tokens (+ room for verify)
@@ -181,23 +184,42 @@ def c4(seed: int = 0, batch: int = 128, prefix: int = 2048, verify_rows: int = 1
             table = tables[e][:full]
             need = -(-(lo + verify_rows) // page) - full
             fresh = alloc(need)
-            if tail:
-                src.append(tables[e][full])
-                dst.append(fresh[0])
-                ntok.append(tail)
             tables[o] = table + fresh
             cached[o] = lo
+            if tail:
+                forks.append((e, o, le))
     blocks = next_page[0]
     # Scatter the logical page ids over a random physical permutation.
     perm = rng.permutation(blocks).astype(np.int32)
     tables = [perm[np.asarray(t, dtype=np.int64)] for t in tables]
-    cow = (perm[np.asarray(src, dtype=np.int64)], perm[np.asarray(dst, dtype=np.int64)],
-           np.asarray(ntok, dtype=np.int32)) if src else None
+    cow = None
+    if forks:
+        # the copy-on-write lists come from the library's fork helper
+        from .ops import fork_copies
+
+        cow = fork_copies([tables[e] for e, _, _ in forks], [tables[o] for _, o, _ in forks],
+                          [le for _, _, le in forks], page)
     w = PagedWorkload("C4", 32, 4, 128, page, True, blocks, tables, cached,
                       np.full(batch, verify_rows, np.int64), False, 1.0, 48, seed, cow=cow)
     w.notes["prefix_pages"] = perm[:0].tolist()
     w.notes["shared_prefix_pages"] = [int(x) for x in perm[:prefix_pages]]
     w.notes["divergent"] = div.tolist()
+    return w
+
+
+def c2_shard(shard: int = 0, nshards: int = 8, seed: int = 0, steps: int = 1,
+             per_shard: int = 64) -> PagedWorkload:
+    """C2 for sequence-sharded runs: one seeded list of nshards x 64 contexts
+    U[512, 4096], split into shards of 64 sequences with nearly equal KV
+    bytes (fekv.dist.balanced_shards); GPU `shard` runs one of them."""
+    from .dist import balanced_shards
+
+    rng = np.random.default_rng(seed)
+    ctx_all = rng.integers(512, 4097, size=per_shard * nshards)
+    own = balanced_shards(ctx_all, nshards, per_shard)[shard]
+    w = decode_workload("C2", 32, 8, ctx_all[own], True, seed + 1 + shard, steps=steps, scale=0.5,
+                        layers=36)
+    w.notes["shard"] = f"{shard} of {nshards} balanced shards of {per_shard} (seed {seed})"
     return w
 
 
@@ -208,14 +230,17 @@ def c5_contexts(seed: int = 0, total: int = 1024, median: float = 8192.0, sigma:
 
 
 def c5(rank: int = 0, world: int = 1, seed: int = 0, steps: int = 32, per_gpu: int = 128):
-    from .dist import shard_range
+    """C5: the 1024 contexts of the config, split into 8 shards of 128
+    sequences with nearly equal KV bytes; GPU `rank` runs shard `rank`."""
+    from .dist import balanced_shards
 
-    ctx_all = c5_contexts(seed, per_gpu * max(world, 8))
-    own = shard_range(rank, per_gpu)
-    ctx = ctx_all[own.start:own.stop]
-    w = decode_workload("C5", 64, 8, ctx, True, seed + 1000 + rank, steps=steps, scale=0.5,
-                        layers=64)
+    nshards = max(world, 8)
+    ctx_all = c5_contexts(seed, per_gpu * nshards)
+    own = balanced_shards(ctx_all, nshards, per_gpu)[rank]
+    w = decode_workload("C5", 64, 8, ctx_all[own], True, seed + 1000 + rank, steps=steps,
+                        scale=0.5, layers=64)
     w.notes["sigma"] = 0.5
+    w.notes["shard"] = f"{rank} of {nshards} balanced shards of {per_gpu}"
     return w
 
 

@@ -94,6 +94,28 @@ int fe_kv_copy_blocks(void* const* k_pools, void* const* v_pools, int num_layers
                       const int32_t* src, const int32_t* dst, const int32_t* ntok, int num_copies,
                       int page, int width, int num_pages_total, int dtype, void* stream);
 
+/* Copy lists for forked sequences (no reference counterpart; HOST memory
+ * only, needs no GPU). The reference shares only whole published pages and
+ * recomputes the rest of a shared prefix by prefill (src/scheduler.cpp:6-29);
+ * a fork that copies KV instead gives, for each fork f, the parent's block
+ * table parent_tables[parent_off[f] .. parent_off[f+1]), the child's table
+ * child_tables[child_off[f] .. child_off[f+1]) as the scheduler assigned it
+ * (the parent's full pages it shares, then pages of its own) and the
+ * length fork_len[f] of the prefix the child continues from. For every page
+ * j < ceil(fork_len/page) the child does not share, one copy entry
+ * (src = parent[j], dst = child[j], ntok = the prefix tokens on that page:
+ * page, or fork_len % page for the tail) is written to src/dst/ntok, ready
+ * for fe_kv_copy_blocks, which must run before either sequence appends.
+ * Rejected with FE_ERR_INVALID_ARGUMENT: a shared page that is not full (both
+ * sequences would append into it: the copy-on-write case), a child page that
+ * is one of the parent's pages at another position, a fork length beyond
+ * either table. FE_ERR_CAPACITY when the copies exceed `capacity`.
+ * *num_copies receives the number of entries written. */
+int fe_kv_fork_copies(int num_forks, const int32_t* parent_tables, const int32_t* parent_off,
+                      const int32_t* child_tables, const int32_t* child_off,
+                      const int64_t* fork_len, int page, int32_t* src, int32_t* dst,
+                      int32_t* ntok, int capacity, int* num_copies);
+
 /* Zero-fill whole pages (e.g. the graph-padding page num_blocks, which the
  * reference gets from at::zeros at start-up, src/cuda_model.cpp:60).
  *   pools: HOST array of num_pools device pool pointers

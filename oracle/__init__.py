@@ -4,13 +4,18 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
 leg / reference arm may import this package. The product library
 (``flashengine.cpp_b200``) never imports, links or calls it.
 
-Two checkers, both reached through ctypes with numpy arrays:
+Checkers, reached through ctypes:
 
 * :func:`c_oracle` — the plain-C restatement in ``oracle/fe_oracle.c``
   (append: ``src/cuda_kernels.cu:24``; attention: ``src/portable_gpu_ops.cpp:27-44``;
   block copy: memcpy, as the reference has no block-copy op).
 * :class:`RefAten` — the reference's own ATen path, ``src/portable_gpu_ops.cpp``,
   compiled for the CPU by ``oracle/build_oracle.py`` into ``oracle/_ref``.
+* :func:`ref_cuda` — the reference's own CUDA rope / store / accept kernels
+  (``src/cuda_kernels.cu``) for sm_100a, run beside this repository's kernels.
+* :class:`RefFlashInfer` — the reference's own CUDA attention
+  (``src/flashinfer_attention.cu``, FlashInfer FA2) for sm_100a: the GPU
+  comparator for attention outputs and timings.
 
 16-bit values travel as ``numpy.uint16`` bit patterns; ``dtype`` is 0 for
 fp16 and 1 for bf16, as in the product C-ABI.
@@ -301,6 +306,84 @@ class RefAten:
     def close(self):
         if self.handle:
             self.lib.fe_ref_destroy_plan(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------------------
+# The reference's own CUDA attention (src/flashinfer_attention.cu over
+# FlashInfer), built for sm_100a: the GPU comparator. Device pointers; GPU
+# tests and bench.py's reference arm only.
+# ---------------------------------------------------------------------------
+
+_ref_fi_lib = None
+
+
+def ref_flashinfer_available() -> bool:
+    return os.path.exists(build_oracle.REF_FI_LIB)
+
+
+def _ref_fi():
+    global _ref_fi_lib
+    if _ref_fi_lib is None:
+        path = build_oracle.REF_FI_LIB
+        if not os.path.exists(path):
+            built = build_oracle.build_reference_flashinfer()
+            if built is None:
+                raise FileNotFoundError("oracle/_ref/libfe_ref_flashinfer.so is not built and "
+                                        "the reference source tree is absent")
+        lib = ctypes.CDLL(path)
+        lib.fe_ref_fi_last_error.restype = ctypes.c_char_p
+        lib.fe_ref_fi_create_plan.argtypes = [_I, _I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]
+        lib.fe_ref_fi_destroy_plan.argtypes = [_P]
+        lib.fe_ref_fi_prepare_plan.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _P]
+        lib.fe_ref_fi_attention.argtypes = [_P, _P, _P, _P, _P, _I, _P]
+        for f in ("fe_ref_fi_create_plan", "fe_ref_fi_prepare_plan", "fe_ref_fi_attention"):
+            getattr(lib, f).restype = _I
+        _ref_fi_lib = lib
+    return _ref_fi_lib
+
+
+class RefFlashInfer:
+    """The reference's fe::cuda AttentionPlan / prepare_plan / attention on the
+    GPU (FlashInfer FA2 paged prefill kernel, split-KV disabled). Tensors are
+    torch CUDA tensors; metadata are host int32 arrays."""
+
+    def __init__(self, hq, hkv, dim, page, max_batch, max_pages, bf16, blocks):
+        self.lib = _ref_fi()
+        h = ctypes.c_void_p()
+        self._check(self.lib.fe_ref_fi_create_plan(hq, hkv, dim, page, max_batch, max_pages,
+                                                   int(bf16), blocks, ctypes.byref(h)))
+        self.handle = h
+        self._keep = []
+
+    def _check(self, rc):
+        if rc != 0:
+            raise RefError(self.lib.fe_ref_fi_last_error().decode("utf-8", "replace"))
+
+    def prepare(self, qo, kv, pages, last, stream=0, graph=False):
+        qo, kv, pages, last = _i32(qo), _i32(kv), _i32(pages), _i32(last)
+        if pages.size == 0:
+            pages = np.zeros(1, np.int32)
+        self._keep = [qo, kv, pages, last]
+        self._check(self.lib.fe_ref_fi_prepare_plan(self.handle, _ptr(qo), _ptr(kv), _ptr(pages),
+                                                    _ptr(last), kv.shape[0] - 1, int(qo[-1]),
+                                                    int(bool(graph)), ctypes.c_void_p(stream)))
+
+    def attention(self, q, k, v, out, causal, stream=0):
+        self._check(self.lib.fe_ref_fi_attention(
+            self.handle, ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(k.data_ptr()),
+            ctypes.c_void_p(v.data_ptr()), ctypes.c_void_p(out.data_ptr()), int(bool(causal)),
+            ctypes.c_void_p(stream)))
+
+    def close(self):
+        if self.handle:
+            self.lib.fe_ref_fi_destroy_plan(self.handle)
             self.handle = None
 
     def __del__(self):

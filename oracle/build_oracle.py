@@ -12,6 +12,13 @@
   ``oracle/ref_cuda_wrap.cu``; the GPU tests run them as the comparator for the
   fused RoPE+append and accept kernels. Built the same way (reference tree
   only; the GPU box uses the prebuilt file).
+* ``oracle/_ref/libfe_ref_flashinfer.so`` — the reference's own CUDA attention
+  (``src/flashinfer_attention.cu`` over the FlashInfer headers installed with
+  the flashinfer wheel) for sm_100a through ``oracle/ref_flashinfer_wrap.cu``:
+  the GPU comparator for decode and verify attention. Built the same way.
+
+The reference tree is looked up in ``$FE_REFERENCE_ROOT``, else in a
+``reference`` directory beside this repository's root.
 
 Run directly: ``python oracle/build_oracle.py [--reference-root DIR]``.
 """
@@ -23,7 +30,9 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-DEFAULT_REFERENCE_ROOT = os.environ.get("FE_REFERENCE_ROOT", "/root/reference")
+REPO_ROOT = os.path.dirname(HERE)
+DEFAULT_REFERENCE_ROOT = os.environ.get(
+    "FE_REFERENCE_ROOT", os.path.join(os.path.dirname(REPO_ROOT), "reference"))
 
 C_ORACLE_SRC = os.path.join(HERE, "fe_oracle.c")
 C_ORACLE_LIB = os.path.join(HERE, "libfe_oracle.so")
@@ -32,6 +41,8 @@ REF_DIR = os.path.join(HERE, "_ref")
 REF_LIB = os.path.join(REF_DIR, "libfe_ref_aten.so")
 REF_CUDA_WRAP_SRC = os.path.join(HERE, "ref_cuda_wrap.cu")
 REF_CUDA_LIB = os.path.join(REF_DIR, "libfe_ref_cuda.so")
+REF_FI_WRAP_SRC = os.path.join(HERE, "ref_flashinfer_wrap.cu")
+REF_FI_LIB = os.path.join(REF_DIR, "libfe_ref_flashinfer.so")
 
 
 def _stale(target: str, *sources: str) -> bool:
@@ -94,6 +105,43 @@ def build_reference_cuda(reference_root: str = DEFAULT_REFERENCE_ROOT,
     return REF_CUDA_LIB
 
 
+def flashinfer_include() -> str | None:
+    """The C++ headers shipped inside the flashinfer wheel (flashinfer/data)."""
+    try:
+        import importlib.util
+
+        spec = importlib.util.find_spec("flashinfer")
+    except Exception:
+        return None
+    if spec is None or not spec.submodule_search_locations:
+        return None
+    data = os.path.join(list(spec.submodule_search_locations)[0], "data")
+    ok = os.path.exists(os.path.join(data, "include", "flashinfer", "attention", "prefill.cuh"))
+    return data if ok else None
+
+
+def build_reference_flashinfer(reference_root: str = DEFAULT_REFERENCE_ROOT,
+                               force: bool = False) -> str | None:
+    """Compile the reference's FlashInfer attention (src/flashinfer_attention.cu)
+    for sm_100a. None when the tree or the FlashInfer headers are absent."""
+    src = os.path.join(reference_root, "src", "flashinfer_attention.cu")
+    data = flashinfer_include()
+    if not os.path.exists(src) or data is None:
+        return REF_FI_LIB if os.path.exists(REF_FI_LIB) else None
+    if not (force or _stale(REF_FI_LIB, REF_FI_WRAP_SRC, src)):
+        return REF_FI_LIB
+    os.makedirs(REF_DIR, exist_ok=True)
+    # the reference's own CUDA flags (CMakeLists.txt: --expt-relaxed-constexpr,
+    # --extended-lambda, C++17), for sm_100a
+    cmd = ["nvcc", "-gencode", "arch=compute_100a,code=sm_100a", "-std=c++17", "-O2",
+           "--expt-relaxed-constexpr", "--extended-lambda", "-Xcompiler", "-fPIC", "-shared",
+           "-I", os.path.join(reference_root, "include"), "-I", os.path.join(data, "include"),
+           "-I", os.path.join(data, "cutlass", "include"), "-I", os.path.join(data, "spdlog", "include"),
+           REF_FI_WRAP_SRC, "-o", REF_FI_LIB, "-Xlinker", "-Bsymbolic"]
+    subprocess.run(cmd, check=True)
+    return REF_FI_LIB
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-root", default=DEFAULT_REFERENCE_ROOT)
@@ -102,6 +150,7 @@ def main(argv=None) -> int:
     print(build_c_oracle(a.force))
     print(build_reference(a.reference_root, a.force))
     print(build_reference_cuda(a.reference_root, a.force))
+    print(build_reference_flashinfer(a.reference_root, a.force))
     return 0
 
 

@@ -165,3 +165,56 @@ def test_gather_bit_exact(fk, name):
               int(lengths.max()), case.page, case.width)
     want = oracle.gather(inp["kpool"], md.kv, md.pages, md.last, case.page, case.width)
     np.testing.assert_array_equal(to_host_bits(out).reshape(want.shape), want)
+
+
+@pytest.mark.parametrize("fork_len", [37, 48, 1000, 1])
+def test_fork_copy_on_write_then_attention(fk, fork_len):
+    """A child forked from a parent at `fork_len` tokens: fe_kv_fork_copies
+    turns the fork into copies, fe_kv_copy_blocks applies them on the GPU,
+    and decode attention of the child over the shared prefix equals the
+    parent's bit for bit (same keys in the same order, the same plan shape).
+    Both then append different tokens: neither changes the other's prefix."""
+    import torch
+    from fekv.metadata import build_step_metadata
+    rng = np.random.default_rng(fork_len)
+    hq, hkv, page = 32, 8, 16
+    width = hkv * 128
+    nblocks = 200
+    parent_len = fork_len + 20
+    perm = rng.permutation(nblocks).astype(np.int32)
+    parent = perm[:-(-parent_len // page)]
+    full = fork_len // page
+    child_pages = -(-(fork_len + 30) // page)
+    child = np.concatenate([parent[:full], perm[100:100 + child_pages - full]]).astype(np.int32)
+    src, dst, ntok = fk.fork_copies([parent], [child], [fork_len], page)
+    assert len(src) == (1 if fork_len % page else 0)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(fork_len)
+    kc = torch.randn((nblocks + 1) * page, width, generator=g, device="cuda").to(torch.bfloat16)
+    vc = torch.randn((nblocks + 1) * page, width, generator=g, device="cuda").to(torch.bfloat16)
+    if len(src):
+        fk.copy_blocks([kc], [vc], _i32(src), _i32(dst), _i32(ntok), page, width, nblocks + 1)
+    q = torch.randn(1, hq, 128, generator=g, device="cuda").to(torch.bfloat16)
+
+    def attend(table, length):
+        md = build_step_metadata([table], [length - 1], [1], page)
+        plan = fk.AttentionPlan(hq, hkv, 128, page, 1, len(table) + 1, True, nblocks)
+        plan.prepare(md.qo, md.kv, md.pages, md.last)
+        out = torch.empty_like(q)
+        plan.attention(q, kc, vc, out, True)
+        torch.cuda.synchronize()
+        plan.close()
+        return to_host_bits(out)
+
+    want = attend(parent, fork_len)
+    np.testing.assert_array_equal(attend(child, fork_len), want)
+    # each appends its own next tokens; the other's prefix is unchanged
+    for table, start in ((parent, fork_len), (child, fork_len)):
+        pos = np.arange(start, start + 10)
+        slots = table[pos // page].astype(np.int64) * page + pos % page
+        rows = torch.randn(10, width, generator=g, device="cuda").to(torch.bfloat16)
+        fk.store(rows, rows, kc, vc, _i64(slots), 10, width, True, None,
+                 (nblocks + 1) * page)
+    np.testing.assert_array_equal(attend(parent, fork_len), want)
+    np.testing.assert_array_equal(attend(child, fork_len), want)
+    assert fk.device_errors() == 0
