@@ -139,7 +139,7 @@ class ClockSampler:
     a second). Falls back to `nvidia-smi -lms 200` when NVML is unavailable.
     Only reads the GPU's state; changes nothing."""
 
-    def __init__(self, device_index: int, period_ms: float = 5.0):
+    def __init__(self, device_index: int, period_ms: float = 2.0):
         self.dev = device_index
         self.period = period_ms / 1e3
         self.samples = []
@@ -428,13 +428,14 @@ class Runner:
             self.cow = tuple(torch.from_numpy(np.asarray(x, np.int32)).cuda() for x in w.cow)
         md0 = w.metadata(0)
         dm = decode_rows_mask(w, md0)
-        # a step with both decode rows and multi-row sequences is timed in two
-        # parts (decode kernel + merge, then the tcgen05 kernel): the same
-        # kernels in the same order as one fe_attn_run, with an event between
+        # a step with both decode rows and multi-row sequences runs the decode
+        # kernel and the tcgen05 kernel side by side (one fe_attn_run); the
+        # per-kernel rooflines come from a serial full-width pass after timing
         self.mixed = (not self.decode) and bool(dm.any()) and bool((~dm).any())
         self.sample_layer = w.layers // 2
         self.attn_ev = []
         self.last_md = None
+        self.side_by_side = False
 
     def step(self, s, record=False, host_io=None):
         import torch
@@ -468,21 +469,13 @@ class Runner:
                        self.slots, md.rows, w.width, w.bf16, self.stream, w.cache_slots)
             if timed:
                 e0 = torch.cuda.Event(enable_timing=True)
-                em = torch.cuda.Event(enable_timing=True) if self.mixed else None
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(self.stream)
-            if timed and self.mixed:
-                self.plan.attention(self.q[layer], self.kpools[p], self.vpools[p], self.out[layer],
-                                    w.causal, self.stream, lists=fekv._lib.FE_ATTN_LISTS_DECODE)
-                em.record(self.stream)
-                self.plan.attention(self.q[layer], self.kpools[p], self.vpools[p], self.out[layer],
-                                    w.causal, self.stream, lists=fekv._lib.FE_ATTN_LISTS_ROWS)
-            else:
-                self.plan.attention(self.q[layer], self.kpools[p], self.vpools[p], self.out[layer],
-                                    w.causal, self.stream)
+            self.plan.attention(self.q[layer], self.kpools[p], self.vpools[p], self.out[layer],
+                                w.causal, self.stream)
             if timed:
                 e1.record(self.stream)
-                self.attn_ev.append((e0, em, e1))
+                self.attn_ev.append((e0, e1))
             if host_io is not None:
                 host_io["after"](layer)
         self.last_md = md
@@ -498,6 +491,10 @@ class Runner:
         for s in range(self.warmup):
             self.step(s)
         torch.cuda.synchronize()
+        if self.mixed:
+            inf = self.plan.info()
+            sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+            self.side_by_side = inf["grid_ctas"] <= sms
         barrier(self.world)
         clocks = ClockSampler(clock_dev)
         clocks.start()
@@ -524,7 +521,7 @@ class Runner:
         barrier(self.world)
         ms = t0.elapsed_time(t1)
         K = self.steps
-        attn_ms = [a.elapsed_time(b) for a, _, b in self.attn_ev]
+        attn_ms = [a.elapsed_time(b) for a, b in self.attn_ev]
         attn_avg_ms = float(np.mean(attn_ms))
         per_launch_bytes = (keys / K) * 2 * w.width * 2 + 2 * self.rows * w.hq * w.dim * 2
         per_launch_flops = flops / K
@@ -536,14 +533,47 @@ class Runner:
               "rows_ms": 0.0, "rows_tflops": 0.0, "dec_ms": 0.0, "dec_gbs": 0.0,
               "rows_flops_per_launch": rows_flops / K, "dec_bytes_per_launch": 0.0}
         if self.mixed:
-            rows_ms = float(np.mean([m.elapsed_time(b) for _, m, b in self.attn_ev]))
-            dec_ms = float(np.mean([a.elapsed_time(m) for a, m, _ in self.attn_ev]))
+            rows_ms, dec_ms = self.time_parts()
             dec_bytes = (dec_keys / K) * 2 * w.width * 2 + 2 * (dec_qrows / K) * w.hq * w.dim * 2
             st.update({"rows_ms": rows_ms, "rows_tflops": (rows_flops / K) / (rows_ms * 1e-3) / 1e12,
                        "dec_ms": dec_ms, "dec_gbs": dec_bytes / (dec_ms * 1e-3) / 1e9,
                        "dec_bytes_per_launch": dec_bytes})
         self.clocks = clk
         return st
+
+    def time_parts(self):
+        """Per-kernel durations of a mixed step at full width: a plan
+        prepared in graph mode runs the decode list (decode kernel + merge)
+        and the row list (tcgen05 kernel) one after the other on every SM;
+        K layer-calls of each, on the layer pools in turn, between CUDA
+        events. Untimed by the step clock (after the timed region)."""
+        import torch
+
+        import fekv
+
+        w = self.w
+        md = w.metadata(0)
+        plan = fekv.AttentionPlan(w.hq, w.hkv, w.dim, w.page, w.batch,
+                                  w.max_pages(self.total_steps), w.bf16, w.num_blocks)
+        plan.prepare(md.qo, md.kv, md.pages, md.last, md.batch, md.rows, True, self.stream)
+        res = []
+        for lists in (fekv._lib.FE_ATTN_LISTS_ROWS, fekv._lib.FE_ATTN_LISTS_DECODE):
+            for i in range(3):
+                p = i % self.physical
+                plan.attention(self.q[0], self.kpools[p], self.vpools[p], self.out[0], w.causal,
+                               self.stream, lists=lists)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(self.stream)
+            for i in range(self.steps):
+                p = i % self.physical
+                plan.attention(self.q[0], self.kpools[p], self.vpools[p], self.out[0], w.causal,
+                               self.stream, lists=lists)
+            e1.record(self.stream)
+            torch.cuda.synchronize()
+            res.append(e0.elapsed_time(e1) / self.steps)
+        plan.close()
+        return res[0], res[1]
 
     def run_e2e(self):
         """The same steps through the C ABI with HOST buffers: per step, the
@@ -814,11 +844,15 @@ def summarize(r, table, results, launches, with_e2e):
             }
             sec["tensor_tflops"] = round(float(col["tflops"][0]), 2)
         if r.mixed:
+            # the tcgen05 kernel on the step's prefill rows and the decode
+            # kernel on its decode rows, each at full width one after the
+            # other (graph-mode plan, after the timed steps)
             sec["roofline"].update({
                 "achieved": round(float(col["rows_tflops"][0]), 2),
                 "frac": round(float(col["rows_tflops"][0]) / tpeak, 4),
                 "algorithmic_flops_per_launch": float(col["rows_flops_per_launch"][0]),
                 "avg_launch_ms": round(float(col["rows_ms"][0]), 5),
+                "timing": "tcgen05 kernel alone at full width (serial pass after the timed steps)",
             })
             sec["roofline_decode_rows"] = {
                 "bound": "hbm", "achieved": round(float(col["dec_gbs"][0]), 1), "peak": peak,
@@ -826,6 +860,17 @@ def summarize(r, table, results, launches, with_e2e):
                 "peak_kind": peak_kind, "kernel": "paged_decode_kernel + decode_merge_kernel",
                 "algorithmic_bytes_per_launch": float(col["dec_bytes_per_launch"][0]),
                 "avg_launch_ms": round(float(col["dec_ms"][0]), 5),
+                "timing": "decode list alone at full width (serial pass after the timed steps)",
+            }
+            # the call the timed steps make: both kernels side by side
+            call_ms = float(col["attn_avg_ms"][0])
+            sec["attention_call"] = {
+                "avg_ms": round(call_ms, 5),
+                "side_by_side": bool(r.side_by_side),
+                "serial_parts_ms": round(float(col["rows_ms"][0] + col["dec_ms"][0]), 5),
+                "tflops": round(float(col["tflops"][0]), 2),
+                "kv_gbs": round(float(col["gbs"][0]), 1),
+                "timing": "CUDA events around fe_attn_run of one sampled layer per timed step",
             }
             sec["attention_call_tflops"] = round(float(col["tflops"][0]), 2)
     rl = sec["roofline"]

@@ -159,6 +159,10 @@ struct fe_attn_plan {
   const void* kmap_ptr = nullptr;
   const void* vmap_ptr = nullptr;
   bool per_head_tma = false;  // decode falls back to per-head-half boxes
+  // mixed steps run the row kernel on this stream beside the decode kernel
+  // (fork and join through the two events, so a capture follows them too)
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
 };
 
 namespace {
@@ -220,6 +224,17 @@ PlanConfig make_config(int hq, int hkv, int dim, int page, int max_batch, int ma
   c.max_items = static_cast<int>(items);
   c.max_groups = c.max_items;
   c.partial_capacity = int64_t(16) << 20;  // 64 MiB of floats
+  // side-by-side mixed steps, fitted to B200 timings of these kernels on a
+  // C3 step: the decode kernel moves ~100 GB/s per SM on part of the GPU
+  // (90 while the tcgen05 kernel runs beside it) after ~10 us of fill and
+  // merge, and reaches ~5.8 TB/s at full width on mid-size launches; the
+  // tcgen05 kernel takes ~0.2 us per 16-key piece of a 128-row item per SM
+  // (twice that at head_dim 256)
+  c.concurrent = true;
+  c.dec_sm_gbs = 90.f;
+  c.hbm_gbs = 5800.f;
+  c.dec_fixed_us = 10.f;
+  c.row_piece_us = dim == kWideHeadDim ? 0.4f : 0.2f;
   return c;
 }
 
@@ -235,6 +250,12 @@ void destroy(fe_attn_plan* p) {
     if (p->d_partials) cudaFree(p->d_partials);
     if (p->d_counters) cudaFree(p->d_counters);
     if (p->d_plan_scratch) cudaFree(p->d_plan_scratch);
+    if (p->side) {
+      cudaStreamSynchronize(p->side);
+      cudaStreamDestroy(p->side);
+    }
+    if (p->fork_ev) cudaEventDestroy(p->fork_ev);
+    if (p->join_ev) cudaEventDestroy(p->join_ev);
   }
   delete p;
 }
@@ -272,6 +293,9 @@ int fe_attn_plan_create(int hq, int hkv, int dim, int page, int max_batch, int m
     e = cudaMallocHost(&p->h_meta[i], p->meta_cap);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->h_ev[i], cudaEventDisableTiming);
   }
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->fork_ev, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->join_ev, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     destroy(p);
@@ -538,13 +562,31 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
   const int G = p->cfg.hq / p->cfg.hkv;
   const CUtensorMap& kd = p->per_head_tma ? p->kmap : p->kmap_dec;
   const CUtensorMap& vd = p->per_head_tma ? p->vmap : p->vmap_dec;
+  // A mixed step planned side by side (the two lists' grids sum to the SMs)
+  // forks: the row kernel runs on the plan's side stream while the decode
+  // kernel and its merge run on `stream`, which then waits for the side.
+  // They read the same q and pools and write disjoint output rows and split
+  // records.
+  const bool fork = grid_dec > 0 && grid_rows > 0 && !p->fixed_grid && p->last.concurrent;
+  cudaStream_t rs = s;
+  if (fork) {
+    FE_CUDA_TRY(cudaEventRecord(p->fork_ev, s));
+    FE_CUDA_TRY(cudaStreamWaitEvent(p->side, p->fork_ev, 0));
+    rs = p->side;
+  }
   auto launch_all = [&](const auto& a) -> int {
+    if (grid_rows > 0 && fork) {
+      int rc = prefill_tc_launch(p->dtype, dim, p->kmap_tc, p->vmap_tc, qmap, &a, grid_rows, rs);
+      if (rc == FE_OK)
+        rc = decode_merge_launch(p->dtype, dim, view, &a, grid_row_merge, merge_y(view), rs);
+      if (rc != FE_OK) return rc;
+    }
     if (grid_dec > 0) {
       int rc = decode_launch(p->dtype, dim, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
       if (rc == FE_OK) rc = decode_merge_launch(p->dtype, dim, 2, &a, grid_merge, merge_y(2), s);
       if (rc != FE_OK) return rc;
     }
-    if (grid_rows > 0) {
+    if (grid_rows > 0 && !fork) {
       int rc = prefill_tc_launch(p->dtype, dim, p->kmap_tc, p->vmap_tc, qmap, &a, grid_rows, s);
       if (rc == FE_OK)
         rc = decode_merge_launch(p->dtype, dim, view, &a, grid_row_merge, merge_y(view), s);
@@ -564,6 +606,13 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
                        p->d_partials, p->d_counters, device_error_word(), p->cfg.hq, G,
                        p->cfg.page, view, scale_log2, q_map_rows};
     rc = launch_all(a);
+  }
+  if (fork) {
+    // join even after a failed launch, so `stream` never runs ahead of the side
+    cudaError_t e1 = cudaEventRecord(p->join_ev, p->side);
+    cudaError_t e2 = cudaStreamWaitEvent(s, p->join_ev, 0);
+    if (rc == FE_OK && e1 != cudaSuccess) return cuda_fail(e1, "fe_attn_run: join record");
+    if (rc == FE_OK && e2 != cudaSuccess) return cuda_fail(e2, "fe_attn_run: join wait");
   }
   if (rc != FE_OK) return rc;
   FE_CUDA_TRY(cudaGetLastError());

@@ -229,6 +229,29 @@ int build_cut_view(const PlanConfig& cfg, const std::vector<Unit>& units, int gr
 
 }  // namespace
 
+int concurrent_decode_ctas(const PlanConfig& cfg, int sms, double dec_bytes, double row_pieces,
+                           double max_row_pieces) {
+  if (!cfg.concurrent || sms < 2 || dec_bytes <= 0 || row_pieces <= 0) return 0;
+  const double b_sm = double(cfg.dec_sm_gbs) * 1e3;  // bytes per microsecond
+  const double b_hbm = double(cfg.hbm_gbs) * 1e3;
+  const double c = cfg.row_piece_us;
+  auto t_dec = [&](int d) { return dec_bytes / std::min(d * b_sm, b_hbm) + cfg.dec_fixed_us; };
+  auto t_row = [&](int r) { return std::max(row_pieces * c / r, max_row_pieces * c); };
+  // one after the other: both at full width, plus the second kernel's ramp
+  const double serial = t_dec(sms) + t_row(sms) + 4.0;
+  int best = 0;
+  double best_t = serial;
+  for (int d = 1; d < sms; ++d) {
+    const double t = std::max(t_dec(d), t_row(sms - d));
+    if (t < best_t) {
+      best_t = t;
+      best = d;
+    }
+  }
+  // side by side only when it is clearly faster (the model is coarse)
+  return best_t < 0.92 * serial ? best : 0;
+}
+
 int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, const int32_t* pages,
                const int32_t* last, int batch, int rows, bool fixed_grid, PlanResult& out,
                std::string& err) {
@@ -318,6 +341,29 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
     }
   }
 
+  // Mixed steps outside graph mode may run the two kernels side by side:
+  // dec_ctas decode CTAs and the rest of the SMs for the row kernel.
+  int row_cap = cfg.grid_cap, dec_cap = cfg.dec_grid_cap;
+  if (!fixed_grid && !key_units.empty() && !row_units_causal.empty()) {
+    double dec_bytes = 0, pieces = 0, max_pieces = 0;
+    for (const auto& u : key_units)
+      dec_bytes += double(u.tiles) * kTileTokens * cfg.dec_heads * cfg.dim * 4.0;
+    for (const auto* list : {&row_units_full, &row_units_causal}) {
+      double total = 0;
+      for (const auto& u : *list) {
+        total += u.tiles;
+        max_pieces = std::max(max_pieces, double(u.tiles));
+      }
+      pieces = std::max(pieces, total);
+    }
+    const int sms = cfg.dec_grid_cap;
+    const int d = concurrent_decode_ctas(cfg, sms, dec_bytes, pieces, max_pieces);
+    if (d > 0) {
+      dec_cap = d;
+      row_cap = std::max(1, (sms - d) * std::max(1, cfg.grid_cap / sms));
+      out.concurrent = true;
+    }
+  }
   // List 0: row work, non-causal; 1: row work, causal (identical key ranges
   // when there is no row work); 2: decode work.
   View views[3];
@@ -329,23 +375,20 @@ int build_plan(const PlanConfig& cfg, const int32_t* qo, const int32_t* kv, cons
       // item's 128 rows are valid, so equal tile counts per CTA balance it,
       // at the price of up to one split unit per CTA boundary (pieces of at
       // least kWideMinChunk tiles per CTA)
-      rc = build_cut_view(cfg, row_units_full, cfg.grid_cap, kWideMinChunk, fixed_grid, views[0],
-                          err);
+      rc = build_cut_view(cfg, row_units_full, row_cap, kWideMinChunk, fixed_grid, views[0], err);
       if (rc != FE_OK) return rc;
-      rc = build_cut_view(cfg, row_units_causal, cfg.grid_cap, kWideMinChunk, fixed_grid,
-                          views[1], err);
+      rc = build_cut_view(cfg, row_units_causal, row_cap, kWideMinChunk, fixed_grid, views[1],
+                          err);
     } else {
       // head_dim 128 keeps whole items (cfg.row_split), longest first onto
       // the least-loaded CTA
       const int row_min_chunk = cfg.row_split ? 16 : (1 << 29);
-      rc = build_view(cfg, row_units_full, cfg.grid_cap, 4, row_min_chunk, fixed_grid, views[0],
-                      err);
+      rc = build_view(cfg, row_units_full, row_cap, 4, row_min_chunk, fixed_grid, views[0], err);
       if (rc != FE_OK) return rc;
-      rc = build_view(cfg, row_units_causal, cfg.grid_cap, 4, row_min_chunk, fixed_grid, views[1],
-                      err);
+      rc = build_view(cfg, row_units_causal, row_cap, 4, row_min_chunk, fixed_grid, views[1], err);
     }
     if (rc != FE_OK) return rc;
-    rc = build_cut_view(cfg, key_units, cfg.dec_grid_cap, 8, fixed_grid, views[2], err);
+    rc = build_cut_view(cfg, key_units, dec_cap, 8, fixed_grid, views[2], err);
     if (rc != FE_OK) return rc;
   }
   // Both kernels of one run share the split workspace and counters: offset

@@ -84,6 +84,13 @@ struct PlanConfig {
   int max_items;              // work-item capacity
   int64_t partial_capacity;   // floats in the split-K workspace
   int max_groups;             // split-counter capacity
+  // Mixed steps (decode rows and multi-row sequences) outside graph mode
+  // run the two kernels side by side on disjoint SMs when the cost model
+  // below predicts a gain: the decode list takes dec_fixed_us plus its bytes
+  // at dec_sm_gbs per decode SM, at most hbm_gbs in all; the row list takes
+  // row_piece_us per 16-key piece of a 128-row item on one SM.
+  bool concurrent;
+  float dec_sm_gbs, hbm_gbs, dec_fixed_us, row_piece_us;
 };
 
 struct PlanResult {
@@ -93,7 +100,16 @@ struct PlanResult {
   int grid[3] = {0, 0, 0};    // CTAs per work list (0 = nothing to launch)
   int split_rows[3] = {0, 0, 0};  // most rows in one split unit's records, per list
   int64_t kv_tokens = 0, partial_floats = 0;
+  bool concurrent = false;  // decode and row kernels run side by side (grids sum to the SMs)
 };
+
+// The SM split of a mixed step: CTAs of the decode kernel when both kernels
+// should run side by side, 0 to run them one after the other at full width.
+// `sms` persistent decode CTAs fit the GPU; dec_bytes are the decode list's
+// K/V bytes, row_pieces the row list's 16-key pieces (summed over items),
+// max_row_pieces those of its longest item (never split across CTAs).
+int concurrent_decode_ctas(const PlanConfig& cfg, int sms, double dec_bytes, double row_pieces,
+                           double max_row_pieces);
 
 // Validates the step metadata (same checks as the reference plus range
 // checks on page ids) and builds the work list. Returns an fe_status; on

@@ -160,7 +160,10 @@ __global__ void __launch_bounds__(kThreads) clear_pages_kernel(const __grid_cons
     to[i] = zero;
 }
 
-// gather: blockIdx.y = sequence; grid-x strides over that sequence's tokens.
+// gather: blockIdx.y = sequence; one warp per token row, the warps of the
+// grid's x dimension striding over the sequence's tokens. The row's slot is
+// computed once per warp; the lanes move its 16-byte chunks, kUnroll per lane
+// in flight, all loads before any store.
 __global__ void __launch_bounds__(kThreads) gather_kernel(const uint4* __restrict__ pool,
                                                           uint4* __restrict__ out,
                                                           const int32_t* __restrict__ kv,
@@ -170,15 +173,27 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(const uint4* __restric
                                                           int page, int chunks_per_row) {
   const int b = blockIdx.y;
   const int p0 = __ldg(kv + b), p1 = __ldg(kv + b + 1);
-  const int64_t len = static_cast<int64_t>(p1 - p0 - 1) * page + __ldg(last + b);
-  const int64_t total = len * chunks_per_row;
+  const int len = (p1 - p0 - 1) * page + __ldg(last + b);
   const int64_t orow = __ldg(row_offset + b);
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t t = i / chunks_per_row;
-    const int64_t col = i - t * chunks_per_row;
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x / 32);
+  for (int t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); t < len; t += warps) {
     const int64_t slot = static_cast<int64_t>(__ldg(pages + p0 + t / page)) * page + t % page;
-    out[(orow + t) * chunks_per_row + col] = __ldg(pool + slot * chunks_per_row + col);
+    const uint4* src = pool + slot * chunks_per_row;
+    uint4* dst = out + (orow + t) * chunks_per_row;
+    for (int c0 = 0; c0 < chunks_per_row; c0 += 32 * kUnroll) {
+      uint4 val[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < chunks_per_row) val[u] = __ldg(src + c);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < chunks_per_row) dst[c] = val[u];
+      }
+    }
   }
 }
 
@@ -340,8 +355,9 @@ int fe_kv_gather(const void* pool, void* out, const int32_t* kv, const int32_t* 
   if (!aligned16(pool) || !aligned16(out))
     return fail(FE_ERR_INVALID_ARGUMENT, "fe_kv_gather: buffers must be 16-byte aligned");
   const int chunks = width / 8;
-  const int64_t per_seq = static_cast<int64_t>(max_len) * chunks;
-  int64_t bx = (per_seq + kThreads - 1) / kThreads;
+  // one warp per token row of the longest sequence, at most 1024 CTAs per
+  // sequence (the warps stride over longer ones)
+  int64_t bx = (static_cast<int64_t>(max_len) + kThreads / 32 - 1) / (kThreads / 32);
   if (bx > 1024) bx = 1024;
   dim3 grid(static_cast<unsigned>(bx), batch);
   gather_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(

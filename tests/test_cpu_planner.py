@@ -244,3 +244,43 @@ def test_head_dim_256_draft_blocks_are_split():
             assert (x["part"] - gi["part0"]) % gi["rec_floats"] == 0
     assert len(meta["views"][2]["items"]) == 0
     hp.close()
+
+
+def test_mixed_step_splits_the_sms_between_the_kernels():
+    """C3 (chunked prefill + decode rows): outside graph mode the decode
+    list gets part of the SMs and the row list the rest, so the two kernels
+    run side by side; every tile is still covered once. Graph mode and
+    single-list steps keep the full width."""
+    w = workloads.c3(seed=1000)
+    # a host plan with grid_cap 296 models 148 SMs (two row CTAs per SM)
+    md, meta, hp = _plan(w, grid_cap=296)
+    sms = 148
+    dec, rows = meta["views"][2]["grid"], meta["views"][1]["grid"]
+    assert 8 <= dec <= 80, dec
+    assert rows == (sms - dec) * 2, (dec, rows)
+    hp.close()
+    _coverage(md, meta, w.hq, w.hkv, w.page, True)
+    _coverage(md, meta, w.hq, w.hkv, w.page, False)
+    md, meta, hp = _plan(w, grid_cap=296, graph=True)
+    assert meta["views"][2]["grid"] == sms and meta["views"][1]["grid"] == 296
+    hp.close()
+    for single in (workloads.c2_shard(0), workloads.c4(seed=0)):
+        md, meta, hp = _plan(single, grid_cap=296)
+        assert meta["views"][2]["grid"] in (0, min(sms, meta["views"][2]["grid"]))
+        assert meta["views"][2]["grid"] in (0, 148) or meta["views"][1]["grid"] == 0
+        assert meta["views"][1]["grid"] in (0, 296)
+        hp.close()
+
+
+def test_mixed_step_with_a_tiny_decode_part_stays_serial_or_balances():
+    """One short decode row beside a large prefill: whatever the split, the
+    decode list gets at least one CTA and the row list keeps most SMs."""
+    from fekv.metadata import build_step_metadata
+    tables = [np.arange(0, 200), np.arange(200, 203)]
+    md = build_step_metadata(tables, [1000, 40], [1024, 1], 16)
+    hp = HostPlan(32, 8, 128, 16, 2, 200, True, 300, grid_cap=296)
+    meta = hp.prepare(md.qo, md.kv, md.pages, md.last)
+    dec, rows = meta["views"][2]["grid"], meta["views"][1]["grid"]
+    items = len(meta["views"][1]["items"])  # 256 row items: one CTA each
+    assert dec >= 1 and rows >= min(items, 2 * 140), (dec, rows)
+    hp.close()

@@ -332,3 +332,61 @@ def test_plan_validation_errors(fk):
     with pytest.raises(fk.FeError):
         fk.AttentionPlan(8, 2, 64, 16, 2, 4, True, 10)  # head_dim 64 not compiled
     plan.close()
+
+
+def test_mixed_step_side_by_side_matches_serial(fk, parity_record):
+    """A C3 step (chunked prefill + decode rows) outside graph mode runs the
+    decode kernel and the tcgen05 kernel side by side on disjoint SMs (the
+    row kernel on the plan's side stream). Its output equals the serial
+    full-width run's (a graph-mode prepare): prefill rows bit for bit, decode
+    rows within the tolerance (their split points differ). The same call
+    captured in a CUDA graph replays to the same bits."""
+    import torch
+    import fekv.workloads as wl
+    w = wl.c3(seed=1000)
+    md = w.metadata()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(21)
+    dt = torch.bfloat16
+    kc = torch.randn(w.cache_slots, w.width, generator=g, device="cuda").to(dt)
+    vc = torch.randn(w.cache_slots, w.width, generator=g, device="cuda").to(dt)
+    q = torch.randn(md.rows, w.hq, w.dim, generator=g, device="cuda").to(dt)
+    side = fk.AttentionPlan(w.hq, w.hkv, w.dim, w.page, md.batch, w.max_pages(), True,
+                            w.num_blocks)
+    side.prepare(md.qo, md.kv, md.pages, md.last)
+    serial = fk.AttentionPlan(w.hq, w.hkv, w.dim, w.page, md.batch, w.max_pages(), True,
+                              w.num_blocks)
+    serial.prepare(md.qo, md.kv, md.pages, md.last, graph=True)
+    info = side.info()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert info["decode_items"] > 0 and info["prefill_items"] > 0
+    assert info["grid_ctas"] <= sms, info  # the two grids share the SMs
+    o_side = torch.full_like(q, float("nan"))
+    o_serial = torch.full_like(q, float("nan"))
+    side.attention(q, kc, vc, o_side, True)
+    serial.attention(q, kc, vc, o_serial, True)
+    torch.cuda.synchronize()
+    qrows = md.qo[1:] - md.qo[:-1]
+    is_dec = torch.from_numpy(np.repeat(qrows == 1, qrows)).cuda()
+    assert torch.equal(o_side[~is_dec].view(torch.int16), o_serial[~is_dec].view(torch.int16))
+    res = compare_attention(to_host_bits(o_side[is_dec]), to_host_bits(o_serial[is_dec]), True)
+    parity_record("C3 decode rows: side by side vs serial full width", res)
+    assert res["excess"] <= 0, res
+    # captured: the fork onto the side stream and the join are part of the graph
+    o_graph = torch.full_like(q, float("nan"))
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        side.attention(q, kc, vc, o_graph, True, s)
+    torch.cuda.current_stream().wait_stream(s)
+    o_graph.fill_(float("nan"))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        side.attention(q, kc, vc, o_graph, True, torch.cuda.current_stream())
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(o_graph.view(torch.int16), o_side.view(torch.int16))
+    del graph
+    side.close()
+    serial.close()
+    assert fk.device_errors() == 0
