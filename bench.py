@@ -21,11 +21,13 @@ The same JSON line carries sub-objects measured in the same process:
        at every N, with its own roofline, e2e and results check;
   c3   chunked prefill + decode rows (tcgen05 kernel roofline), N=1 only;
   c4   shared-prefix verify blocks + copy-on-write (tcgen05), N=1 only;
+  q35  head_dim 256 decode (hybrid-model full-attention layers), N=1 only;
+  draft head_dim 256 16-row draft blocks under the full mask, N=1 only;
   ops  append / block copy / fused RoPE+append / accept / merge-free
        preparation timings against the HBM roofline, N=1 only.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3|c4|c5|q35|draft]
-                  [--sub c5,c3,c4,ops|none] [--layers L]
+                  [--sub c5,c3,c4,q35,draft,ops|none] [--layers L]
   python bench.py --impl reference ...   # the reference's own CPU/ATen path
 
 Prints one JSON line (rank 0).
@@ -1341,8 +1343,9 @@ def run_ours(args, rank, world, local):
     for sub in subs:
         if sub == "c5":
             sec, _, _ = measure("c5", args, rank, world, local, C5_STEPS)
-        elif sub in ("c3", "c4") and world == 1:
-            sec, _, _ = measure(sub, args, rank, world, local, args.steps, verify=False)
+        elif sub in ("c3", "c4", "q35", "draft") and world == 1:
+            sec, _, _ = measure(sub, args, rank, world, local, args.steps,
+                                verify=sub == "q35")
         elif sub == "ops" and world == 1:
             sec = ops_suite(args.ops_iters)
         else:
@@ -1364,7 +1367,7 @@ def main(argv=None):
                          "(profiling one operator: --ops-case)")
     ap.add_argument("--ops-case", default=None, help="with --config ops: one operator case")
     ap.add_argument("--ops-iters", type=int, default=50)
-    ap.add_argument("--sub", default="c5,c3,c4,ops",
+    ap.add_argument("--sub", default="c5,c3,c4,q35,draft,ops",
                     help="workloads measured beside the c2 headline (comma list, or none)")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--pool-gb", type=float, default=150.0)

@@ -27,7 +27,7 @@ namespace fe {
 int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
 int decode_merge_launch(int dtype, int dim, int list, const void* args, int grid, int grid_rows,
-                        cudaStream_t stream);
+                        cudaStream_t stream, bool pdl);
 int prefill_tc_launch(int dtype, int dim, const CUtensorMap& kmap, const CUtensorMap& vmap,
                       const CUtensorMap& qmap, const void* args, int grid, cudaStream_t stream);
 
@@ -575,21 +575,26 @@ int fe_attn_run_lists(fe_attn_plan* p, const void* q, const void* k_pool, const 
     rs = p->side;
   }
   auto launch_all = [&](const auto& a) -> int {
+    // Side by side, a merge waits for its kernel's grid to complete before
+    // it takes an SM (a programmatic dependent would sit on SMs the other
+    // kernel needs while it waits).
     if (grid_rows > 0 && fork) {
       int rc = prefill_tc_launch(p->dtype, dim, p->kmap_tc, p->vmap_tc, qmap, &a, grid_rows, rs);
       if (rc == FE_OK)
-        rc = decode_merge_launch(p->dtype, dim, view, &a, grid_row_merge, merge_y(view), rs);
+        rc = decode_merge_launch(p->dtype, dim, view, &a, grid_row_merge, merge_y(view), rs,
+                                 false);
       if (rc != FE_OK) return rc;
     }
     if (grid_dec > 0) {
       int rc = decode_launch(p->dtype, dim, H, kd, vd, p->per_head_tma, &a, grid_dec, s);
-      if (rc == FE_OK) rc = decode_merge_launch(p->dtype, dim, 2, &a, grid_merge, merge_y(2), s);
+      if (rc == FE_OK)
+        rc = decode_merge_launch(p->dtype, dim, 2, &a, grid_merge, merge_y(2), s, !fork);
       if (rc != FE_OK) return rc;
     }
     if (grid_rows > 0 && !fork) {
       int rc = prefill_tc_launch(p->dtype, dim, p->kmap_tc, p->vmap_tc, qmap, &a, grid_rows, s);
       if (rc == FE_OK)
-        rc = decode_merge_launch(p->dtype, dim, view, &a, grid_row_merge, merge_y(view), s);
+        rc = decode_merge_launch(p->dtype, dim, view, &a, grid_row_merge, merge_y(view), s, true);
       return rc;
     }
     return FE_OK;

@@ -34,7 +34,7 @@ namespace fe {
 int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
 int decode_merge_launch(int dtype, int dim, int list, const void* args, int grid, int grid_rows,
-                        cudaStream_t stream);
+                        cudaStream_t stream, bool pdl);
 int decode_smem_bytes(int heads);
 
 namespace {
@@ -613,28 +613,35 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const AttnA
 }
 
 template <typename T>
-int launch_merge_t(const AttnArgs<T>& args, int dim, int list, dim3 grid, cudaStream_t stream) {
-  if (dim == kWideHeadDim)
-    FE_CUDA_TRY(launch_pdl(decode_merge_kernel<T, kWideHeadDim>, grid, dim3(kMergeThreads), 0,
-                           stream, args, list));
-  else
-    FE_CUDA_TRY(launch_pdl(decode_merge_kernel<T, kHeadDim>, grid, dim3(kMergeThreads), 0, stream,
-                           args, list));
+int launch_merge_t(const AttnArgs<T>& args, int dim, int list, dim3 grid, cudaStream_t stream,
+                   bool pdl) {
+  auto kernel = dim == kWideHeadDim ? decode_merge_kernel<T, kWideHeadDim>
+                                    : decode_merge_kernel<T, kHeadDim>;
+  if (pdl) {
+    FE_CUDA_TRY(launch_pdl(kernel, grid, dim3(kMergeThreads), 0, stream, args, list));
+  } else {
+    kernel<<<grid, kMergeThreads, 0, stream>>>(args, list);
+    FE_CUDA_TRY(cudaGetLastError());
+  }
   return FE_OK;
 }
 
 }  // namespace
 
 // grid: CTAs over the list's split units (strided); grid_rows: CTAs per
-// unit, each taking 32 of its record rows (one per warp), strided.
+// unit, each taking 32 of its record rows (one per warp), strided. With
+// `pdl` the merge is a programmatic dependent of the kernel before it (its
+// CTAs become resident on SMs that grid frees and wait for its completion);
+// without, it starts once that grid has completed, so it takes no SM from a
+// kernel running beside the decode kernel.
 int decode_merge_launch(int dtype, int dim, int list, const void* args, int grid, int grid_rows,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, bool pdl) {
   if (grid <= 0) return FE_OK;
   const dim3 g(grid, grid_rows > 0 ? grid_rows : 1);
   if (dtype == FE_DTYPE_BF16)
     return launch_merge_t(*static_cast<const AttnArgs<__nv_bfloat16>*>(args), dim, list, g,
-                          stream);
-  return launch_merge_t(*static_cast<const AttnArgs<__half>*>(args), dim, list, g, stream);
+                          stream, pdl);
+  return launch_merge_t(*static_cast<const AttnArgs<__half>*>(args), dim, list, g, stream, pdl);
 }
 
 int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const CUtensorMap& vmap,
