@@ -84,8 +84,10 @@ def measured_peak_tflops():
 # tcgen05 kernel's DRAM bytes depend on L2 reuse of shared prefixes and are
 # only reported for the captured launch itself.
 NCU_TRAFFIC = {
-    ("C2", "paged_decode_kernel"): (611757056, 603463680.0, True,
+    ("C2", "paged_decode_kernel"): (632665344, 625496064.0, True,
                                     "profiles/paged_decode_kernel_c2.md"),
+    ("C5", "paged_decode_kernel"): (4732976768, 4716232704.0, True,
+                                    "profiles/paged_decode_kernel_c5.md"),
     ("C4", "paged_prefill_tc_kernel"): (63075840, 75586338816.0, False,
                                         "profiles/paged_prefill_tc_kernel_c4.md"),
     ("DFL", "paged_prefill_tc_kernel"): (159589120, 155019264.0, True,
