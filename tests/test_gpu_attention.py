@@ -390,3 +390,74 @@ def test_mixed_step_side_by_side_matches_serial(fk, parity_record):
     side.close()
     serial.close()
     assert fk.device_errors() == 0
+
+
+def test_empty_step_launches_nothing(fk):
+    """batch 0 (an idle step): prepare and attention succeed and write nothing."""
+    import torch
+    plan = fk.AttentionPlan(8, 2, 128, 16, 4, 8, True, 32)
+    plan.prepare([0], [0], [], [])
+    q = torch.zeros(4, 8, 128, dtype=torch.bfloat16, device="cuda")
+    pool = torch.zeros(33 * 16, 2 * 128, dtype=torch.bfloat16, device="cuda")
+    out = torch.full_like(q, 7.0)
+    plan.attention(q, pool, pool, out, True)
+    torch.cuda.synchronize()
+    assert bool((out == 7.0).all())
+    assert plan.info()["grid_ctas"] == 0
+    plan.close()
+    assert fk.device_errors() == 0
+
+
+@pytest.mark.parametrize("bf16", [True, False])
+def test_ragged_batch_with_zero_row_sequences(fk, bf16):
+    """Sequences scheduled with no query rows this step (qo[b] == qo[b+1])
+    between decode rows and prefill chunks: they are skipped, every other
+    row matches the oracle."""
+    case = cases._case("ragged", 16, 4, [300, 50, 700, 9, 1200], [1, 0, 33, 0, 1], bf16, True, 77)
+    inp = case.inputs()
+    md = case.metadata()
+    out, info = run_case(fk, case, inp, md)
+    ko, vo = inp["kpool"].copy(), inp["vpool"].copy()
+    oracle.append(inp["knew"], inp["vnew"], ko, vo, md.slots, case.cache_slots)
+    want, want32 = oracle.attention(inp["q"], ko, vo, md.qo, md.kv, md.pages, md.last, case.hq,
+                                    case.hkv, case.dim, case.page, True, case.dtype_code)
+    res = compare_attention(out, want, bf16, ref_f32=want32)
+    assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, (res, info)
+
+
+def test_step_at_plan_capacity(fk):
+    """A step that fills the plan exactly: batch = max_batch and every
+    sequence at max_pages pages (the reference's capacity check,
+    src/flashinfer_attention.cu:30, accepts it; one more page is refused)."""
+    import torch
+    from fekv.metadata import build_step_metadata
+    batch, max_pages, page = 6, 40, 16
+    nblocks = batch * max_pages + 4
+    rng = np.random.default_rng(3)
+    perm = rng.permutation(nblocks).astype(np.int32)
+    tables = [perm[b * max_pages:(b + 1) * max_pages] for b in range(batch)]
+    starts = [max_pages * page - 1 - b for b in range(batch)]  # last page, 1..16 tokens
+    md = build_step_metadata(tables, starts, [1] * batch, page)
+    assert int(md.kv[-1]) == batch * max_pages
+    g = torch.Generator(device="cuda")
+    g.manual_seed(4)
+    kc = torch.randn((nblocks + 1) * page, 8 * 128, generator=g, device="cuda").to(torch.bfloat16)
+    vc = torch.randn((nblocks + 1) * page, 8 * 128, generator=g, device="cuda").to(torch.bfloat16)
+    q = torch.randn(batch, 32, 128, generator=g, device="cuda").to(torch.bfloat16)
+    plan = fk.AttentionPlan(32, 8, 128, page, batch, max_pages, True, nblocks)
+    plan.prepare(md.qo, md.kv, md.pages, md.last)
+    out = torch.empty_like(q)
+    plan.attention(q, kc, vc, out, True)
+    ref = torch_reference_attention(q, kc, vc, md.qo, md.kv, md.pages, md.last, 32, 8, page, True)
+    torch.cuda.synchronize()
+    res = compare_attention(to_host_bits(out), to_host_bits(ref.to(torch.bfloat16)), True,
+                            ref_f32=ref.cpu().numpy())
+    assert res["excess"] <= 0 and res["excess_vs_f32"] <= 0, res
+    # one page more than a sequence may hold is refused with the capacity status
+    big = build_step_metadata([np.concatenate([tables[0], perm[-1:]])] + tables[1:],
+                              [max_pages * page] + starts[1:], [1] * batch, page)
+    with pytest.raises(fk.FeError) as e:
+        plan.prepare(big.qo, big.kv, big.pages, big.last)
+    assert e.value.status == fk._lib.FE_ERR_CAPACITY
+    plan.close()
+    assert fk.device_errors() == 0
