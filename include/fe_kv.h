@@ -211,11 +211,17 @@ int fe_attn_plan_prepare(fe_attn_plan* plan, const int32_t* qo, const int32_t* k
 
 /* Paged GQA attention. Replaces fe::cuda::attention
  * (include/fe/native_cuda.hpp:10; src/flashinfer_attention.cu:35-44).
- *   q, out: [rows, hq, 128]; k_pool, v_pool: [cache_slots, hkv, 128]
+ *   q, out: [rows, hq, dim]; k_pool, v_pool: [cache_slots, hkv, dim]
+ *           (dim = the plan's head_dim, 128 or 256)
  *   causal != 0: row i of a sequence with qrows rows sees keys
  *                t <= length - qrows + i (bottom-right aligned);
  *   causal == 0: every row sees t < length (DFlash draft / block verify).
- * Scale 1/sqrt(128); fp32 accumulation; output rounded to nearest even. */
+ * Scale 1/sqrt(dim); fp32 accumulation; output rounded to nearest even.
+ * A step prepared outside graph mode that mixes decode rows with multi-row
+ * sequences may run its two kernels side by side: the multi-row kernel on a
+ * stream the plan owns, forked from `stream` by an event and joined back
+ * before the call returns, so the call is ordered on `stream` as usual (and
+ * a capture of `stream` records the fork and the join). */
 int fe_attn_run(fe_attn_plan* plan, const void* q, const void* k_pool, const void* v_pool,
                 void* out, int causal, void* stream);
 
