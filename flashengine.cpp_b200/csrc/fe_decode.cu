@@ -343,9 +343,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     fence_barrier_init();
   }
   __syncthreads();
-  // q, the pools and the split workspace belong to earlier kernels until here
-  // (a no-op when launched without programmatic serialization)
-  pdl_wait();
 
   if (warp == kDecWarps) {
     // ------------------------------------------------------------ producer
@@ -353,24 +350,30 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
     }
+    // Slots of 32 tiles are fetched per batch (one per lane); the next batch
+    // is requested before the current one is consumed.
+    auto tile_slot = [&](const WorkItem& w, const SeqInfo& si, int j) -> int {
+      if (j >= w.kt1) return 0;
+      const int t0 = j * kTileTokens;
+      return __ldg(pages + si.page_off + t0 / a.page) * a.page + (t0 % a.page);
+    };
+    // The work list and page ids are the plan's metadata, copied in by the
+    // prepare before the previous kernel started: the first item's page ids
+    // are fetched before waiting for that kernel, which owns the pools
+    // (a no-op wait when launched without programmatic serialization).
+    const int first_slot = tile_slot(items[it0], seqs[items[it0].seq], items[it0].kt0 + lane);
+    pdl_wait();
     uint32_t g = 0;
     bool ok = true;
     for (int it = it0; it < it1 && ok; ++it) {
       const WorkItem w = items[it];
       const SeqInfo si = seqs[w.seq];
       const int hh0 = w.kvh * C::kQ;  // first 64-dim box of the item's heads
-      // Slots of 32 tiles are fetched per batch (one per lane); the next
-      // batch is requested before the current one is consumed.
-      auto tile_slot = [&](int j) -> int {
-        if (j >= w.kt1) return 0;
-        const int t0 = j * kTileTokens;
-        return __ldg(pages + si.page_off + t0 / a.page) * a.page + (t0 % a.page);
-      };
-      int nxt = tile_slot(w.kt0 + lane);
+      int nxt = it == it0 ? first_slot : tile_slot(w, si, w.kt0 + lane);
       for (int j0 = w.kt0; j0 < w.kt1 && ok; j0 += 32) {
         const int n = min(32, w.kt1 - j0);
         const int slot0 = nxt;
-        nxt = tile_slot(j0 + 32 + lane);
+        nxt = tile_slot(w, si, j0 + 32 + lane);
         for (int jj = 0; jj < n; ++jj) {
           const int s0 = __shfl_sync(0xffffffffu, slot0, jj);
           const int s = g % C::kStages;
@@ -416,6 +419,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   }
 
   // -------------------------------------------------------------- consumers
+  // q and the split workspace belong to earlier kernels until here
+  pdl_wait();
   uint32_t g = 0;
   bool aborted = false;
   for (int it = it0; it < it1; ++it) {
