@@ -595,17 +595,28 @@ template <typename T, int D>
 __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const AttnArgs<T> a,
                                                                      int list) {
   pdl_trigger();
-  pdl_wait();
+  // The plan's metadata was complete before the kernel ahead of this one
+  // started (the kernel that wrote the records read it from its first
+  // instruction on), so the CTA's first unit is read before the wait; only
+  // the records need that kernel's completion.
   const MetaHeader* hdr = reinterpret_cast<const MetaHeader*>(a.meta);
   const int n = hdr->n_groups[list];
   const SplitGroup* groups = reinterpret_cast<const SplitGroup*>(a.meta + hdr->groups_off[list]);
   const SeqInfo* seqs = reinterpret_cast<const SeqInfo*>(a.meta + hdr->seqs_off);
+  SplitGroup first{};
+  SeqInfo first_seq{};
+  if (static_cast<int>(blockIdx.x) < n) {
+    first = groups[blockIdx.x];
+    if (first.nsplit >= 2) first_seq = seqs[first.seq];
+  }
+  pdl_wait();
   const int G = a.G;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int gidx = blockIdx.x; gidx < n; gidx += gridDim.x) {
-    const SplitGroup gi = groups[gidx];
+    const bool head = gidx == static_cast<int>(blockIdx.x);
+    const SplitGroup gi = head ? first : groups[gidx];
     if (gi.nsplit < 2) continue;  // placeholder ids of the row lists
-    const SeqInfo si = seqs[gi.seq];
+    const SeqInfo si = head ? first_seq : seqs[gi.seq];
     const int rph = gi.rows_per_head > 0 ? gi.rows_per_head : si.qrows * G;
     for (int r = warp + blockIdx.y * (kMergeThreads / 32); r < gi.rows;
          r += gridDim.y * (kMergeThreads / 32)) {
