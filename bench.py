@@ -448,8 +448,6 @@ class Runner:
 
         w = self.w
         md = w.metadata(s if self.decode else 0)
-        if host_io is not None:
-            host_io["h2d"]()
         self.plan.prepare(md.qo, md.kv, md.pages, md.last, md.batch, md.rows, False, self.stream)
         # a fresh pinned buffer per step: the host runs steps ahead of the GPU
         # (torch's pinned allocator keeps it until the copy has run)
@@ -461,14 +459,14 @@ class Runner:
                 l1 = min(self.physical, l0 + fekv._lib.FE_MAX_LAYERS)
                 fekv.copy_blocks(self.kpools[l0:l1], self.vpools[l0:l1], *self.cow, w.page,
                                  w.width, w.num_blocks + 1, None, self.stream)
+        if host_io is not None:
+            host_io["start"]()
         for layer in range(w.layers):
             p = layer % self.physical
             # kernel durations for the roofline come from events around one
             # sampled layer per step: an event between two kernels ends their
             # programmatic overlap, so the other layers run without them
             timed = record and layer == self.sample_layer
-            if host_io is not None:
-                host_io["before"](layer)
             fekv.store(self.knew[layer], self.vnew[layer], self.kpools[p], self.vpools[p],
                        self.slots, md.rows, w.width, w.bf16, self.stream, w.cache_slots)
             if timed:
@@ -480,8 +478,8 @@ class Runner:
             if timed:
                 e1.record(self.stream)
                 self.attn_ev.append((e0, e1))
-            if host_io is not None:
-                host_io["after"](layer)
+        if host_io is not None:
+            host_io["end"]()
         self.last_md = md
         return md
 
@@ -579,13 +577,19 @@ class Runner:
         plan.close()
         return res[0], res[1]
 
-    def run_e2e(self):
+    def run_e2e(self, device_ms_per_step):
         """The same steps through the C ABI with HOST buffers: per step, the
         H2D of every layer's q/k/v from pinned memory and the D2H of every
-        layer's output, inside the timed region. The copies run on a second
-        stream per layer, so layer l+1's inputs arrive while layer l computes
-        and layer l's output leaves during layer l+1 (events keep a buffer
-        from being overwritten before the copy or kernel reading it)."""
+        layer's output, inside the timed region. Inputs and outputs are
+        double-buffered on the device: a copy stream brings step i+1's inputs
+        in while step i computes and takes step i's outputs out while step
+        i+1 computes, and the compute stream waits once per step (a wait
+        between two layers' kernels would end their programmatic overlap).
+        Inputs and outputs get a stream each, so that the two directions of
+        the host link run at once, unless a step's copies take under 30% of
+        its kernel time: there one stream measured faster (C2: 4.03 ms per
+        step against 4.13). The first step's inputs and the last step's
+        outputs are not hidden."""
         import torch
 
         w = self.w
@@ -597,54 +601,71 @@ class Runner:
         hk_pin.copy_(self.knew)
         hv_pin.copy_(self.vnew)
         self.pins = (hq_pin, hk_pin, hv_pin, ho_pin)
-        copy_stream = torch.cuda.Stream()
-        h2d_ev = [torch.cuda.Event() for _ in range(w.layers)]
-        comp_ev = [torch.cuda.Event() for _ in range(w.layers)]
-        d2h_ev = [torch.cuda.Event() for _ in range(w.layers)]
-        started = [False]
-
-        def io_h2d():
-            with torch.cuda.stream(copy_stream):
-                for layer in range(w.layers):
-                    if started[0]:
-                        copy_stream.wait_event(comp_ev[layer])  # last step's layer done with them
-                    self.q[layer].copy_(hq_pin[layer], non_blocking=True)
-                    self.knew[layer].copy_(hk_pin[layer], non_blocking=True)
-                    self.vnew[layer].copy_(hv_pin[layer], non_blocking=True)
-                    h2d_ev[layer].record(copy_stream)
-
-        def io_before(layer):
-            self.stream.wait_event(h2d_ev[layer])
-            if started[0]:
-                self.stream.wait_event(d2h_ev[layer])  # last step's output of this layer left
-
-        def io_after(layer):
-            comp_ev[layer].record(self.stream)
-            with torch.cuda.stream(copy_stream):
-                copy_stream.wait_event(comp_ev[layer])
-                ho_pin[layer].copy_(self.out[layer], non_blocking=True)
-                d2h_ev[layer].record(copy_stream)
-            if layer == w.layers - 1:
-                started[0] = True
-
-        io = {"h2d": io_h2d, "before": io_before, "after": io_after}
+        sets = [(self.q, self.knew, self.vnew, self.out),
+                tuple(torch.empty_like(t) for t in (self.q, self.knew, self.vnew, self.out))]
         h2d_bytes = (hq_pin.numel() + hk_pin.numel() + hv_pin.numel()) * 2
         d2h_bytes = ho_pin.numel() * 2
+        copy_ms = (h2d_bytes + d2h_bytes) / 50e9 * 1e3  # at ~50 GB/s per direction
+        dual = copy_ms > 0.3 * device_ms_per_step
+        in_stream = torch.cuda.Stream()
+        out_stream = torch.cuda.Stream() if dual else in_stream
+        h2d_ev = [torch.cuda.Event() for _ in range(2)]
+        comp_ev = [torch.cuda.Event() for _ in range(2)]
+        d2h_ev = [torch.cuda.Event() for _ in range(2)]
+        n = self.e2e_steps
+        state = {"i": 0}
+
+        def h2d(b, after_compute):
+            with torch.cuda.stream(in_stream):
+                if after_compute:
+                    in_stream.wait_event(comp_ev[b])  # the step before last is done with set b
+                q, k, v, _ = sets[b]
+                q.copy_(hq_pin, non_blocking=True)
+                k.copy_(hk_pin, non_blocking=True)
+                v.copy_(hv_pin, non_blocking=True)
+                h2d_ev[b].record(in_stream)
+
+        def io_start():
+            i = state["i"]
+            b = i % 2
+            self.q, self.knew, self.vnew, self.out = sets[b]
+            self.stream.wait_event(h2d_ev[b])
+            if i >= 2:
+                self.stream.wait_event(d2h_ev[b])  # step i-2's outputs have left set b
+            if i + 1 < n:
+                h2d(1 - b, i >= 1)
+
+        def io_end():
+            i = state["i"]
+            b = i % 2
+            comp_ev[b].record(self.stream)
+            with torch.cuda.stream(out_stream):
+                out_stream.wait_event(comp_ev[b])
+                ho_pin.copy_(sets[b][3], non_blocking=True)
+                d2h_ev[b].record(out_stream)
+            state["i"] = i + 1
+
+        io = {"start": io_start, "end": io_end}
         barrier(self.world)
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         base = self.warmup + self.steps
         e0.record(self.stream)
-        copy_stream.wait_stream(self.stream)  # no copy starts before the timed region
-        for i in range(self.e2e_steps):
+        in_stream.wait_stream(self.stream)  # no copy starts before the timed region
+        out_stream.wait_stream(self.stream)
+        h2d(0, False)  # the first step's inputs
+        for i in range(n):
             self.step(base + i, host_io=io)
-        self.stream.wait_stream(copy_stream)  # the last outputs are on the host
+        self.stream.wait_stream(in_stream)
+        self.stream.wait_stream(out_stream)  # the last outputs are on the host
         e1.record(self.stream)
         torch.cuda.synchronize()
         barrier(self.world)
+        # the results check reads the last step's buffers
+        self.q, self.knew, self.vnew, self.out = sets[(n - 1) % 2 if n > 0 else 0]
         return {"e2e_ms": e0.elapsed_time(e1), "h2d_bytes": float(h2d_bytes),
-                "d2h_bytes": float(d2h_bytes)}
+                "d2h_bytes": float(d2h_bytes), "copy_streams": 2.0 if dual else 1.0}
 
     def host_copy_rates(self):
         """One step's H2D inputs and D2H outputs copied alone (every rank at
@@ -763,7 +784,7 @@ def verify_results(runner, world):
 STAT_KEYS = ["ms", "attn_avg_ms", "kv_bytes_per_launch", "flops_per_launch", "gbs", "tflops",
              "step_gbs", "rows_ms", "rows_tflops", "dec_ms", "dec_gbs", "rows_flops_per_launch",
              "dec_bytes_per_launch", "e2e_ms", "h2d_bytes", "d2h_bytes", "h2d_gbs", "d2h_gbs",
-             "h2d_ms", "d2h_ms"]
+             "h2d_ms", "d2h_ms", "copy_streams"]
 
 
 def measure(config, args, rank, world, local, steps, with_e2e=True, verify=True):
@@ -773,7 +794,7 @@ def measure(config, args, rank, world, local, steps, with_e2e=True, verify=True)
                args.pool_gb, args.layers if config == args.config else 0)
     st = r.run_device(local)
     if with_e2e:
-        st.update(r.run_e2e())
+        st.update(r.run_e2e(st["ms"] / r.steps))
         st.update(r.host_copy_rates())
     results = verify_results(r, world) if verify else None
     table = gather_floats([float(st.get(k, 0.0)) for k in STAT_KEYS], world)
@@ -887,6 +908,7 @@ def summarize(r, table, results, launches, with_e2e):
             "h2d_bytes_per_step": int(col["h2d_bytes"][0]),
             "d2h_bytes_per_step": int(col["d2h_bytes"][0]), "steps": r.e2e_steps,
             "per_rank_ms_per_step": [round(float(x) / r.e2e_steps, 4) for x in col["e2e_ms"]],
+            "copy_streams": int(col["copy_streams"][0]),
             # one step's copies alone, all ranks copying at once
             "host_copy": {
                 "h2d_gbs": [round(float(x), 1) for x in col["h2d_gbs"]],
