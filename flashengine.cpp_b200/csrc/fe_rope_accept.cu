@@ -164,63 +164,61 @@ __global__ void __launch_bounds__(kRopeThreads)
   const int e0 = rotating ? 8 * u : rot + 8 * (u - rot_units);  // first element of the chunk
   const int e1 = e0 + r;                                        // its partner (rotating)
   for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+    // every load that does not depend on the position first (the chunk, its
+    // partner, the value chunk and the slot), then the position and its
+    // cos / sin: one dependent round trip per row instead of three
+    const bool is_q = head < hq;
+    const bool idle = is_q && !rotating;  // q's unrotated dims stay as they are
+    const int h = head - hq;
+    T* qbase = q + (static_cast<int64_t>(row) * hq + head) * dim;
+    const int64_t off = (static_cast<int64_t>(row) * hkv + h) * dim;
+    const T* src = is_q ? qbase : k + off;
+    Chunk lo, hi, vlo, vhi;
+    if (!idle) lo.u = *reinterpret_cast<const uint4*>(src + e0);
+    if (rotating) hi.u = *reinterpret_cast<const uint4*>(src + e1);
+    int64_t slot = -1;
+    if (!is_q && kc) {
+      slot = slots[row];
+      vlo.u = *reinterpret_cast<const uint4*>(v + off + e0);
+      if (rotating) vhi.u = *reinterpret_cast<const uint4*>(v + off + e1);
+    }
     const int64_t p = pos[row];
     if (p < 0 || p >= max_positions) {
       if (unit == 0) raise_device_error(err, FE_DEVERR_POS_RANGE);
       continue;
     }
-    float2 c[4], sn[4];
+    if (idle) continue;
     if (rotating) {
       const float4* cp = reinterpret_cast<const float4*>(cache + p * rot + 8 * u);
       const float4* sp = reinterpret_cast<const float4*>(cache + p * rot + r + 8 * u);
       const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
-      c[0] = make_float2(c0.x, c0.y);
-      c[1] = make_float2(c0.z, c0.w);
-      c[2] = make_float2(c1.x, c1.y);
-      c[3] = make_float2(c1.z, c1.w);
-      sn[0] = make_float2(s0.x, s0.y);
-      sn[1] = make_float2(s0.z, s0.w);
-      sn[2] = make_float2(s1.x, s1.y);
-      sn[3] = make_float2(s1.z, s1.w);
-    }
-    if (head < hq) {
-      if (!rotating) continue;  // q's unrotated dims stay as they are
-      T* base = q + (static_cast<int64_t>(row) * hq + head) * dim;
-      Chunk lo, hi;
-      lo.u = *reinterpret_cast<const uint4*>(base + e0);
-      hi.u = *reinterpret_cast<const uint4*>(base + e1);
+      const float2 c[4] = {make_float2(c0.x, c0.y), make_float2(c0.z, c0.w),
+                           make_float2(c1.x, c1.y), make_float2(c1.z, c1.w)};
+      const float2 sn[4] = {make_float2(s0.x, s0.y), make_float2(s0.z, s0.w),
+                            make_float2(s1.x, s1.y), make_float2(s1.z, s1.w)};
 #pragma unroll
       for (int i = 0; i < 4; ++i) rotate<T>(lo.v[i], hi.v[i], c[i], sn[i]);
-      *reinterpret_cast<uint4*>(base + e0) = lo.u;
-      *reinterpret_cast<uint4*>(base + e1) = hi.u;
+    }
+    if (is_q) {
+      *reinterpret_cast<uint4*>(qbase + e0) = lo.u;
+      *reinterpret_cast<uint4*>(qbase + e1) = hi.u;
       continue;
-    }
-    const int h = head - hq;
-    const int64_t off = (static_cast<int64_t>(row) * hkv + h) * dim;
-    Chunk lo, hi;
-    lo.u = *reinterpret_cast<const uint4*>(k + off + e0);
-    if (rotating) {
-      hi.u = *reinterpret_cast<const uint4*>(k + off + e1);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) rotate<T>(lo.v[i], hi.v[i], c[i], sn[i]);
     }
     if (k_out && (rotating || k_out != k)) {
       *reinterpret_cast<uint4*>(k_out + off + e0) = lo.u;
       if (rotating) *reinterpret_cast<uint4*>(k_out + off + e1) = hi.u;
     }
-    if (!kc) continue;
-    const int64_t slot = slots[row];
-    if (slot < 0) continue;
+    if (!kc || slot < 0) continue;
     if (slot >= cache_slots) {
       if (u == 0 && h == 0) raise_device_error(err, FE_DEVERR_SLOT_RANGE);
       continue;
     }
     const int64_t dst = (slot * hkv + h) * dim;
     *reinterpret_cast<uint4*>(kc + dst + e0) = lo.u;
-    *reinterpret_cast<uint4*>(vc + dst + e0) = *reinterpret_cast<const uint4*>(v + off + e0);
+    *reinterpret_cast<uint4*>(vc + dst + e0) = vlo.u;
     if (rotating) {
       *reinterpret_cast<uint4*>(kc + dst + e1) = hi.u;
-      *reinterpret_cast<uint4*>(vc + dst + e1) = *reinterpret_cast<const uint4*>(v + off + e1);
+      *reinterpret_cast<uint4*>(vc + dst + e1) = vhi.u;
     }
   }
 }
