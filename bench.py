@@ -83,6 +83,8 @@ def measured_peak_tflops():
 # bytes a launch reads (the bench's contexts grow by one token per step); the
 # tcgen05 kernel's DRAM bytes depend on L2 reuse of shared prefixes and are
 # only reported for the captured launch itself.
+NOMINAL_HBM_GBS = 8000.0  # B200 HBM3e, nominal (the north star's "roughly 8 TB/s")
+
 NCU_TRAFFIC = {
     ("C2", "paged_decode_kernel"): (632665344, 625496064.0, True,
                                     "profiles/paged_decode_kernel_c2.md"),
@@ -845,6 +847,8 @@ def summarize(r, table, results, launches, with_e2e):
             # the same bytes over the whole step's time (append, merge, PDL overlap included)
             "step_level_gbs": round(float(col["step_gbs"][0]), 1),
             "step_level_frac": round(float(col["step_gbs"][0]) / peak, 4),
+            # against B200's nominal HBM3e rate, for context (`frac` is of the measured peak)
+            "frac_nominal": round(float(col["gbs"][0]) / NOMINAL_HBM_GBS, 4),
         }
     else:
         per_launch_flops = float(col["flops_per_launch"][0])
@@ -977,7 +981,8 @@ def ops_suite(iters=50, warmup=5, only=None):
         e = {"us": round(us, 2)}
         if nbytes:
             gbs = nbytes / (us * 1e-6) / 1e9
-            e.update({"bytes": int(nbytes), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)})
+            e.update({"bytes": int(nbytes), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                      "frac_nominal": round(gbs / NOMINAL_HBM_GBS, 4)})
         e.update(kw)
         return e
 
