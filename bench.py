@@ -1220,35 +1220,31 @@ def _cpu_model():
     return None
 
 
-def reference_gpu(args, world):
-    """The reference's own GPU attention (src/flashinfer_attention.cu: FlashInfer's
-    FA2 paged kernel, split-KV disabled, built for sm_100a from the reference
-    source by oracle/build_oracle.py) timed on one GPU, on the same layer
-    inputs this repository's arm times: a C2 decode layer (shard 0, the
-    headline) and a C4 verify layer. Each launch reads the next of eight
-    layer pools, so its pages are not in L2. Only the attention launches are
-    timed (CUDA events), as in the repository arm's `roofline`."""
+# Layers timed back to back by both arms (`layer_calls` in this repository's
+# line, `reference_gpu` in the reference arm's): name, workload, pool copies.
+LAYER_CALLS = (("c2_decode_layer", "c2", 8), ("c3_mixed_layer", "c3", 8),
+               ("c4_verify_layer", "c4", 8), ("c5_decode_layer", "c5", 3))
+
+
+def time_layer_calls(args, world, make_impl):
+    """Times one implementation's attention call on one layer of each of
+    LAYER_CALLS (shard 0): the call back to back in one stream, each launch
+    reading the next of several layer pools (each larger than L2, so no
+    launch finds its pages there), CUDA events around the timed launches.
+    `make_impl(w, md, total_steps)` returns (attention(q, k, v, o), close)."""
     import torch
 
-    import oracle
-
-    if not torch.cuda.is_available():
-        return {"unavailable": "no GPU"}
-    if not oracle.ref_flashinfer_available():
-        return {"unavailable": "oracle/_ref/libfe_ref_flashinfer.so not built"}
     peak, peak_kind = measured_peak_gbs()
     tpeak, tkind = measured_peak_tflops()
-    out = {"kernel": "FlashInfer BatchPrefillWithPagedKVCache (FA2, split-KV off), "
-                     "src/flashinfer_attention.cu built for sm_100a",
-           "flashinfer_headers": "flashinfer wheel 0.6.11.post2 (the reference pins 0.6.14)"}
+    out = {}
     total_steps = args.warmup + args.steps + args.e2e_steps + 1
-    for name, config in (("c2_decode_layer", "c2"), ("c4_verify_layer", "c4")):
+    for name, config, npools in LAYER_CALLS:
         w = make_workload(config, 0, world, total_steps)
-        md = w.metadata(args.warmup if config == "c2" else 0)
+        md = w.metadata(args.warmup if is_decode(config) else 0)
         g = torch.Generator(device="cuda")
         g.manual_seed(11)
         pools = []
-        for _ in range(8):
+        for _ in range(npools):
             kc = torch.empty(w.cache_slots, w.width, dtype=torch.bfloat16, device="cuda")
             vc = torch.empty_like(kc)
             kc.normal_(0.0, w.scale, generator=g)
@@ -1257,39 +1253,88 @@ def reference_gpu(args, world):
         q = (torch.randn(md.rows, w.hq, w.dim, generator=g, device="cuda") * w.scale).to(
             torch.bfloat16)
         o = torch.empty_like(q)
-        stream = torch.cuda.current_stream().cuda_stream
-        fi = oracle.RefFlashInfer(w.hq, w.hkv, w.dim, w.page, w.batch, w.max_pages(total_steps),
-                                  True, w.num_blocks)
-        fi.prepare(md.qo, md.kv, md.pages, md.last, stream)
+        attention, close = make_impl(w, md, total_steps)
         for i in range(max(args.warmup, 3)):
-            fi.attention(q, *pools[i % 8], o, w.causal, stream)
+            attention(q, *pools[i % npools], o)
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         n = max(args.steps, 8)
         e0.record()
         for i in range(n):
-            fi.attention(q, *pools[i % 8], o, w.causal, stream)
+            attention(q, *pools[i % npools], o)
         e1.record()
         torch.cuda.synchronize()
-        fi.close()
+        close()
         ms = e0.elapsed_time(e1) / n
         keys = int(md.lengths(w.page).sum())
         nbytes = keys * 2 * w.width * 2 + 2 * md.rows * w.hq * w.dim * 2
         flops = attention_flops(w, md)
-        ent = {"avg_launch_ms": round(ms, 5), "launches": n,
+        ent = {"avg_launch_ms": round(ms, 5), "launches": n, "pools": npools,
                "algorithmic_bytes_per_launch": float(nbytes),
                "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
                "frac_of_hbm_peak": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4),
                "algorithmic_flops_per_launch": flops,
-               "tflops": round(flops / (ms * 1e-3) / 1e12, 2)}
-        if config == "c4":
-            ent["frac_of_tensor_peak"] = round(flops / (ms * 1e-3) / 1e12 / tpeak, 4)
+               "tflops": round(flops / (ms * 1e-3) / 1e12, 2),
+               "frac_of_tensor_peak": round(flops / (ms * 1e-3) / 1e12 / tpeak, 4)}
         out[name] = ent
         del pools, q, o
         torch.cuda.empty_cache()
     out["peaks"] = {"hbm_gbs": peak, "hbm_kind": peak_kind, "bf16_tflops": tpeak,
                     "bf16_kind": tkind}
+    return out
+
+
+def layer_calls(args, world):
+    """This repository's attention call (plan prepared on the host, not in
+    graph mode) timed like the reference arm's `reference_gpu`."""
+    import torch
+
+    import fekv
+
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def make_impl(w, md, total_steps):
+        plan = fekv.AttentionPlan(w.hq, w.hkv, w.dim, w.page, w.batch, w.max_pages(total_steps),
+                                  w.bf16, w.num_blocks)
+        plan.prepare(md.qo, md.kv, md.pages, md.last, md.batch, md.rows, False, stream)
+        return (lambda q, k, v, o: plan.attention(q, k, v, o, w.causal, stream)), plan.close
+
+    out = {"method": "the attention call back to back in one stream, host-prepared plan; "
+                     "the reference arm's reference_gpu times the reference's FlashInfer path "
+                     "on the same inputs the same way"}
+    out.update(time_layer_calls(args, world, make_impl))
+    return out
+
+
+def reference_gpu(args, world):
+    """The reference's own GPU attention (src/flashinfer_attention.cu: FlashInfer's
+    FA2 paged kernel, split-KV disabled, built for sm_100a from the reference
+    source by oracle/build_oracle.py) timed on one GPU, on the same layer
+    inputs and in the same way as this repository's `layer_calls`: a C2
+    decode layer (shard 0, the headline), a C3 mixed layer (prefill chunks and
+    decode rows, causal), a C4 verify layer and a C5 long-context decode
+    layer."""
+    import torch
+
+    import oracle
+
+    if not torch.cuda.is_available():
+        return {"unavailable": "no GPU"}
+    if not oracle.ref_flashinfer_available():
+        return {"unavailable": "oracle/_ref/libfe_ref_flashinfer.so not built"}
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def make_impl(w, md, total_steps):
+        fi = oracle.RefFlashInfer(w.hq, w.hkv, w.dim, w.page, w.batch, w.max_pages(total_steps),
+                                  True, w.num_blocks)
+        fi.prepare(md.qo, md.kv, md.pages, md.last, stream)
+        return (lambda q, k, v, o: fi.attention(q, k, v, o, w.causal, stream)), fi.close
+
+    out = {"kernel": "FlashInfer BatchPrefillWithPagedKVCache (FA2, split-KV off), "
+                     "src/flashinfer_attention.cu built for sm_100a",
+           "flashinfer_headers": "flashinfer wheel 0.6.11.post2 (the reference pins 0.6.14)"}
+    out.update(time_layer_calls(args, world, make_impl))
     return out
 
 
@@ -1377,6 +1422,8 @@ def run_ours(args, rank, world, local):
                                 verify=sub == "q35")
         elif sub == "ops" and world == 1:
             sec = ops_suite(args.ops_iters)
+        elif sub == "calls" and world == 1:
+            sec = layer_calls(args, world)
         else:
             continue
         if rank == 0:
@@ -1396,7 +1443,7 @@ def main(argv=None):
                          "(profiling one operator: --ops-case)")
     ap.add_argument("--ops-case", default=None, help="with --config ops: one operator case")
     ap.add_argument("--ops-iters", type=int, default=50)
-    ap.add_argument("--sub", default="c5,c3,c4,q35,draft,ops",
+    ap.add_argument("--sub", default="c5,c3,c4,q35,draft,ops,calls",
                     help="workloads measured beside the c2 headline (comma list, or none)")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--pool-gb", type=float, default=150.0)
