@@ -469,6 +469,8 @@ class Runner:
             # sampled layer per step: an event between two kernels ends their
             # programmatic overlap, so the other layers run without them
             timed = record and layer == self.sample_layer
+            if host_io is not None:
+                host_io["layer_start"](layer)
             fekv.store(self.knew[layer], self.vnew[layer], self.kpools[p], self.vpools[p],
                        self.slots, md.rows, w.width, w.bf16, self.stream, w.cache_slots)
             if timed:
@@ -480,6 +482,8 @@ class Runner:
             if timed:
                 e1.record(self.stream)
                 self.attn_ev.append((e0, e1))
+            if host_io is not None:
+                host_io["layer_end"](layer)
         if host_io is not None:
             host_io["end"]()
         self.last_md = md
@@ -590,8 +594,10 @@ class Runner:
         Inputs and outputs get a stream each, so that the two directions of
         the host link run at once, unless a step's copies take under 30% of
         its kernel time: there one stream measured faster (C2: 4.03 ms per
-        step against 4.13). The first step's inputs and the last step's
-        outputs are not hidden."""
+        step against 4.13). The first step's inputs arrive and the last
+        step's outputs leave in four layer chunks, the first step's layers
+        waiting only for their own chunk, so one chunk of each stays exposed
+        rather than a whole step's copies."""
         import torch
 
         w = self.w
@@ -616,6 +622,27 @@ class Runner:
         d2h_ev = [torch.cuda.Event() for _ in range(2)]
         n = self.e2e_steps
         state = {"i": 0}
+        chunks = min(4, w.layers)
+        bounds = [w.layers * c // chunks for c in range(chunks + 1)]
+        first_ev = [torch.cuda.Event() for _ in range(chunks)]
+        last_ev = [torch.cuda.Event() for _ in range(chunks)]
+
+        def h2d_first():
+            with torch.cuda.stream(in_stream):
+                q, k, v, _ = sets[0]
+                for c in range(chunks):
+                    l0, l1 = bounds[c], bounds[c + 1]
+                    q[l0:l1].copy_(hq_pin[l0:l1], non_blocking=True)
+                    k[l0:l1].copy_(hk_pin[l0:l1], non_blocking=True)
+                    v[l0:l1].copy_(hv_pin[l0:l1], non_blocking=True)
+                    first_ev[c].record(in_stream)
+                h2d_ev[0].record(in_stream)
+
+        def d2h_chunk(b, c, ev):
+            with torch.cuda.stream(out_stream):
+                out_stream.wait_event(ev)
+                l0, l1 = bounds[c], bounds[c + 1]
+                ho_pin[l0:l1].copy_(sets[b][3][l0:l1], non_blocking=True)
 
         def h2d(b, after_compute):
             with torch.cuda.stream(in_stream):
@@ -631,23 +658,39 @@ class Runner:
             i = state["i"]
             b = i % 2
             self.q, self.knew, self.vnew, self.out = sets[b]
-            self.stream.wait_event(h2d_ev[b])
+            if i > 0:  # the first step waits per chunk (layer_start)
+                self.stream.wait_event(h2d_ev[b])
             if i >= 2:
                 self.stream.wait_event(d2h_ev[b])  # step i-2's outputs have left set b
             if i + 1 < n:
                 h2d(1 - b, i >= 1)
 
+        def layer_start(layer):
+            if state["i"] == 0 and layer in bounds[:-1]:
+                self.stream.wait_event(first_ev[bounds.index(layer)])
+
+        def layer_end(layer):
+            i = state["i"]
+            if i == n - 1 and layer + 1 in bounds[1:-1]:
+                c = bounds.index(layer + 1) - 1
+                last_ev[c].record(self.stream)
+                d2h_chunk(i % 2, c, last_ev[c])
+
         def io_end():
             i = state["i"]
             b = i % 2
             comp_ev[b].record(self.stream)
-            with torch.cuda.stream(out_stream):
-                out_stream.wait_event(comp_ev[b])
-                ho_pin.copy_(sets[b][3], non_blocking=True)
-                d2h_ev[b].record(out_stream)
+            if i == n - 1:  # earlier chunks left in layer_end
+                d2h_chunk(b, chunks - 1, comp_ev[b])
+            else:
+                with torch.cuda.stream(out_stream):
+                    out_stream.wait_event(comp_ev[b])
+                    ho_pin.copy_(sets[b][3], non_blocking=True)
+            d2h_ev[b].record(out_stream)
             state["i"] = i + 1
 
-        io = {"start": io_start, "end": io_end}
+        io = {"start": io_start, "end": io_end, "layer_start": layer_start,
+              "layer_end": layer_end}
         barrier(self.world)
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
@@ -656,7 +699,7 @@ class Runner:
         e0.record(self.stream)
         in_stream.wait_stream(self.stream)  # no copy starts before the timed region
         out_stream.wait_stream(self.stream)
-        h2d(0, False)  # the first step's inputs
+        h2d_first()
         for i in range(n):
             self.step(base + i, host_io=io)
         self.stream.wait_stream(in_stream)
