@@ -12,6 +12,8 @@ fp32).
   multiple of one query head's vector, so that head's maximum first appears
   tens of tiles after the running maximum was fixed, and nearly all of the
   row's weight moves to it; another head sees a needle at the first key.
+- NaN outside the sequences: every pool slot that holds none of the step's
+  keys (the rest of each last page, unused pages) is NaN in K and V.
 Shapes cover the decode kernel (one query row per sequence, GQA 4 and 8),
 the tcgen05 kernel (verify blocks with the full mask, causal prefill
 chunks) and both 16-bit types.
@@ -124,3 +126,49 @@ def test_late_needles_vs_oracle(fk, parity_record, shape, bf16):
     inp = _plant_needles(case, case.inputs(), md, 3.0)
     res = _check(fk, case, inp, md)
     parity_record(f"late needles {name} {'bf16' if bf16 else 'f16'}", res)
+
+
+def _poison_unused_slots(case, inp):
+    """Every pool slot outside the sequences' cached keys becomes NaN in K
+    and V (the rest of each last page, unused pages); the step's appends
+    then overwrite their own slots. The kernels read whole 16-token tiles
+    and must give those keys no weight and let none of their V in."""
+    nan = np.uint16(0x7FC0 if case.bf16 else 0x7E00)
+    used = np.zeros(case.cache_slots, bool)
+    for b, table in enumerate(case.block_tables):
+        pos = np.arange(int(case.cached[b]))
+        used[np.asarray(table, np.int64)[pos // case.page] * case.page + pos % case.page] = True
+    used[case.num_blocks * case.page:] = True  # the padding page stays zero
+    for key in ("kpool", "vpool"):
+        inp[key] = inp[key].copy()
+        inp[key][~used] = nan
+    return inp
+
+
+@pytest.mark.parametrize("page", [16, 32])
+@pytest.mark.parametrize("bf16", [True, False])
+@pytest.mark.parametrize("shape", SHAPES, ids=[s[0] for s in SHAPES])
+def test_nan_outside_sequences_vs_oracle(fk, shape, bf16, page):
+    name, hq, hkv, cached, rows, causal = shape
+    seed = 7800 + SHAPES.index(shape) + (0 if bf16 else 20) + page
+    case = cases._case(f"{name}_nan", hq, hkv, cached, rows, bf16, causal, seed, page=page,
+                       spare=3)
+    md = case.metadata()
+    _check(fk, case, _poison_unused_slots(case, case.inputs()), md)
+
+
+WIDE_SHAPES = [
+    ("decode_d256", 16, 2, [1500, 90, 3100], [1, 1, 1], True),
+    ("draft_d256", 16, 2, [800, 2400], [16, 16], False),
+]
+
+
+@pytest.mark.parametrize("bf16", [True, False])
+@pytest.mark.parametrize("shape", WIDE_SHAPES, ids=[s[0] for s in WIDE_SHAPES])
+def test_nan_outside_sequences_head_dim_256(fk, shape, bf16):
+    name, hq, hkv, cached, rows, causal = shape
+    seed = 7900 + WIDE_SHAPES.index(shape) + (0 if bf16 else 20)
+    case = cases._case(f"{name}_nan", hq, hkv, cached, rows, bf16, causal, seed, spare=3,
+                       dim=256)
+    md = case.metadata()
+    _check(fk, case, _poison_unused_slots(case, case.inputs()), md)
