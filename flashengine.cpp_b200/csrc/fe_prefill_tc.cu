@@ -11,7 +11,8 @@
 // sequence and KV head against a range of keys, processed in 128-key tiles.
 //  warps 8/11 producers of K / of V: gather each key tile (eight 16-token
 //             page pieces, one 4 KiB TMA box each) into a 2-stage K ring and a
-//             3-stage V ring (32 KiB per stage); a K stage is released when its
+//             3-stage V ring (32 KiB per stage; 3 K and 2 V stages at head_dim
+//             256); a K stage is released when its
 //             S MMA completed, a V stage when its PV did. The page ids of the
 //             next 32 pieces are fetched ahead by the warp's lanes. The K
 //             producer also loads each item's Q tile with two TMA boxes (query
@@ -63,17 +64,21 @@ namespace {
 
 // Per head dim D (128, or 256 for the hybrid / DFlash models' full-attention
 // layers). Both use the same shared-memory budget: 64 KiB of Q (two 128-dim
-// tiles, or one 256-dim tile), a 2-stage K and a 3-stage V ring of 32 KiB
-// stages (128 keys of 128 dims, or 64 keys of 256 dims).
-constexpr int kKStagesTc = 2;
-constexpr int kVStagesTc = 3;
+// tiles, or one 256-dim tile) and five 32 KiB K / V stages (128 keys of 128
+// dims, or 64 keys of 256 dims): 2 K + 3 V at head_dim 128, 3 K + 2 V at 256.
+// A K stage is refilled only when the S that read it has completed, and a V
+// stage when its P·V has, so the rings' depths bound how far the loads run
+// ahead. At head_dim 256 (draft blocks, whose pages come from HBM) per-tile
+// clock stamps showed each S waiting on its K tile with two K stages (one
+// tile per ~2,950 cycles); with three, ~2,200, P·V then waiting on V loads
+// of ~2.6 us: the 160 KiB of stages beside the 64 KiB Q tile are the limit.
 constexpr int kSlotsTc = 3;
 constexpr int kTcThreads = 12 * 32;  // 3 warpgroups: softmax 0, softmax 1, producers/MMA
 constexpr int kProducerWarp = 8, kMmaWarp = 9, kPvWarp = 10, kVProducerWarp = 11;
 // q_full[2], q_empty[2], o_free, l_done, k_full[2], k_empty[2], v_full[3],
 // v_empty[3], s_full[3], s_free[3], p_full[3][2], mma_drain, xmax[2][4]
 constexpr int kNumBarsTc =
-    4 + 2 + 2 * kKStagesTc + 2 * kVStagesTc + kSlotsTc + kSlotsTc + 2 * kSlotsTc + 1 + 8;
+    4 + 2 + 2 * 5 + kSlotsTc + kSlotsTc + 2 * kSlotsTc + 1 + 8;  // 5 K + V stages
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.f;
 
@@ -95,8 +100,10 @@ struct TcCfg {
   static constexpr int kKVTile = kPiecesPerTile * kPieceBytes;  // 32 KiB
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kQBufs * kQBytes;
-  static constexpr int kOffV = kOffK + kKStagesTc * kKVTile;
-  static constexpr int kOffX = kOffV + kVStagesTc * kKVTile;   // half-row maxima
+  static constexpr int kKStages = D == kHeadDim ? 2 : 3;
+  static constexpr int kVStages = 5 - kKStages;
+  static constexpr int kOffV = kOffK + kKStages * kKVTile;
+  static constexpr int kOffX = kOffV + kVStages * kKVTile;   // half-row maxima
   static constexpr int kXBytes = 2 * 2 * kM * 4;               // [tile parity][group][128 rows]
   static constexpr int kOffBar = kOffX + kXBytes;
   static constexpr int kSmem = kOffBar + kNumBarsTc * 8 + 32;
@@ -159,7 +166,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   using C = TcCfg<D>;
   constexpr int kTcM = C::kM, kTcN = C::kN, kHalfN = C::kHalfN;
   constexpr int kPiecesPerTile = C::kPiecesPerTile;
-  constexpr int kSlots = kSlotsTc, kKStages = kKStagesTc, kVStages = kVStagesTc;
+  constexpr int kSlots = kSlotsTc, kKStages = C::kKStages, kVStages = C::kVStages;
   constexpr uint32_t kOCol = C::kOCol;
   constexpr bool kSplits = D != kHeadDim;  // the planner splits head_dim 256 row items only
   // declared 16-byte aligned so that the 1 KiB check below is not folded away
