@@ -35,7 +35,6 @@ int decode_launch(int dtype, int dim, int heads, const CUtensorMap& kmap, const 
                   bool per_head_tma, const void* args, int grid, cudaStream_t stream);
 int decode_merge_launch(int dtype, int dim, int list, const void* args, int grid, int grid_rows,
                         cudaStream_t stream, bool pdl);
-int decode_smem_bytes(int heads);
 
 namespace {
 
@@ -453,19 +452,6 @@ int launch_t(const CUtensorMap& kmap, const CUtensorMap& vmap, bool per_head_tma
                          stream, kmap, vmap, args, per_head_tma ? 1 : 0));
   return FE_OK;
 }
-
-}  // namespace
-
-int decode_smem_bytes(int heads) {
-  switch (heads) {
-    case 8: return DecCfg<8>::kSmem;
-    case 4: return DecCfg<4>::kSmem;
-    case 2: return DecCfg<2>::kSmem;
-    default: return DecCfg<1>::kSmem;
-  }
-}
-
-namespace {
 
 // Merge the partial records of every split unit of a work list (the decode
 // list, or a head_dim 256 row list): gridDim.x CTAs stride over the units

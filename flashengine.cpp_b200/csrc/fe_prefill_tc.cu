@@ -58,7 +58,6 @@ namespace fe {
 
 int prefill_tc_launch(int dtype, int dim, const CUtensorMap& kmap, const CUtensorMap& vmap,
                       const CUtensorMap& qmap, const void* args, int grid, cudaStream_t stream);
-int prefill_tc_smem_bytes();
 
 namespace {
 
@@ -708,8 +707,6 @@ int launch_dim(int dim, const CUtensorMap& kmap, const CUtensorMap& vmap, const 
 }
 
 }  // namespace
-
-int prefill_tc_smem_bytes() { return TcCfg<kHeadDim>::kSmem; }
 
 int prefill_tc_launch(int dtype, int dim, const CUtensorMap& kmap, const CUtensorMap& vmap,
                       const CUtensorMap& qmap, const void* args, int grid, cudaStream_t stream) {
