@@ -11,8 +11,7 @@
 // sequence and KV head against a range of keys, processed in 128-key tiles.
 //  warps 8/11 producers of K / of V: gather each key tile (eight 16-token
 //             page pieces, one 4 KiB TMA box each) into a 2-stage K ring and a
-//             3-stage V ring (32 KiB per stage; 3 K and 2 V stages at head_dim
-//             256); a K stage is released when its
+//             3-stage V ring (32 KiB per stage); a K stage is released when its
 //             S MMA completed, a V stage when its PV did. The page ids of the
 //             next 32 pieces are fetched ahead by the warp's lanes. The K
 //             producer also loads each item's Q tile with two TMA boxes (query
@@ -64,20 +63,25 @@ namespace {
 // Per head dim D (128, or 256 for the hybrid / DFlash models' full-attention
 // layers). Both use the same shared-memory budget: 64 KiB of Q (two 128-dim
 // tiles, or one 256-dim tile) and five 32 KiB K / V stages (128 keys of 128
-// dims, or 64 keys of 256 dims): 2 K + 3 V at head_dim 128, 3 K + 2 V at 256.
-// A K stage is refilled only when the S that read it has completed, and a V
-// stage when its P·V has, so the rings' depths bound how far the loads run
-// ahead. At head_dim 256 (draft blocks, whose pages come from HBM) per-tile
-// clock stamps showed each S waiting on its K tile with two K stages (one
-// tile per ~2,950 cycles); with three, ~2,200, P·V then waiting on V loads
-// of ~2.6 us: the 160 KiB of stages beside the 64 KiB Q tile are the limit.
+// dims, or 64 keys of 256 dims): 2 K + 3 V. A K stage is refilled only when
+// the S that read it has completed, and a V stage when its P·V has, so the
+// rings' depths bound how far the loads run ahead.
 constexpr int kSlotsTc = 3;
+constexpr int kKStagesTc = 2;
+constexpr int kVStagesTc = 3;
+// The softmax warps wait on a V stage (to zero rows past the sequence end)
+// while running up to kSlotsTc tiles ahead of P·V. With a V ring shallower
+// than that, the stage's previous tile may not have been consumed yet and
+// its v_full phase would still be open; a parity wait for this tile's phase
+// would then return at once (the phase before has the same parity) and the
+// zeroing would hit the older tile.
+static_assert(kVStagesTc >= kSlotsTc, "V ring at least as deep as the S slots");
 constexpr int kTcThreads = 12 * 32;  // 3 warpgroups: softmax 0, softmax 1, producers/MMA
 constexpr int kProducerWarp = 8, kMmaWarp = 9, kPvWarp = 10, kVProducerWarp = 11;
 // q_full[2], q_empty[2], o_free, l_done, k_full[2], k_empty[2], v_full[3],
 // v_empty[3], s_full[3], s_free[3], p_full[3][2], mma_drain, xmax[2][4]
 constexpr int kNumBarsTc =
-    4 + 2 + 2 * 5 + kSlotsTc + kSlotsTc + 2 * kSlotsTc + 1 + 8;  // 5 K + V stages
+    4 + 2 + 2 * kKStagesTc + 2 * kVStagesTc + kSlotsTc + kSlotsTc + 2 * kSlotsTc + 1 + 8;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.f;
 
@@ -99,8 +103,8 @@ struct TcCfg {
   static constexpr int kKVTile = kPiecesPerTile * kPieceBytes;  // 32 KiB
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kQBufs * kQBytes;
-  static constexpr int kKStages = D == kHeadDim ? 2 : 3;
-  static constexpr int kVStages = 5 - kKStages;
+  static constexpr int kKStages = kKStagesTc;
+  static constexpr int kVStages = kVStagesTc;
   static constexpr int kOffV = kOffK + kKStages * kKVTile;
   static constexpr int kOffX = kOffV + kVStages * kKVTile;   // half-row maxima
   static constexpr int kXBytes = 2 * 2 * kM * 4;               // [tile parity][group][128 rows]
