@@ -75,8 +75,9 @@ constexpr int kSlotsTc = 3;
 constexpr int kKVStagesTc = 5;  // K + V stages
 constexpr int kTcThreads = 12 * 32;  // 3 warpgroups: softmax 0, softmax 1, producers/MMA
 constexpr int kProducerWarp = 8, kMmaWarp = 9, kPvWarp = 10, kVProducerWarp = 11;
-// q_full[2], q_empty[2], o_free, l_done, k_full[2], k_empty[2], v_full[3],
-// v_empty[3], s_full[3], s_free[3], p_full[3][2], mma_drain, xmax[2][4]
+// q_full[2], q_empty[2], o_free, l_done, k_full[K], k_empty[K], v_full[V],
+// v_empty[V] (K + V = 5 stages), s_full[3], s_free[3], p_full[3][2],
+// mma_drain, xmax[2][4]
 constexpr int kNumBarsTc =
     4 + 2 + 2 * kKVStagesTc + kSlotsTc + kSlotsTc + 2 * kSlotsTc + 1 + 8;
 constexpr uint32_t kTmemCols = 512;
